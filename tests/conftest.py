@@ -1,0 +1,58 @@
+"""Shared test set-up.
+
+* registers the ``gpu`` marker (tests that need a B200 and the built CUDA
+  library);
+* puts the repository root (for ``oracle``) and the package directory (for
+  the reference-compatible ``src`` package) on ``sys.path``;
+* loads the golden fixtures written by ``tests/golden/make_golden.py``.
+"""
+
+from __future__ import annotations
+
+import glob
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "mamba3-fused-triton-kernel_b200")
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built sm_100a library")
+
+
+def load_golden(name: str) -> dict:
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        d = {k: z[k] for k in z.files}
+    d["meta"] = json.loads(str(d["meta"]))
+    return d
+
+
+def golden_names(kind: str) -> list:
+    out = []
+    for f in sorted(glob.glob(os.path.join(GOLDEN, "*.npz"))):
+        name = os.path.basename(f)[:-4]
+        if load_golden(name)["meta"]["kind"] == kind:
+            out.append(name)
+    return out
+
+
+def layer_kwargs(kw: dict) -> dict:
+    keys = ("d_model", "d_state", "headdim", "rope_fraction", "is_mimo", "mimo_rank", "A_floor")
+    return {k: kw[k] for k in keys if k in kw}
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
