@@ -1,0 +1,148 @@
+/*
+ * mamba3_b200.h -- C ABI of the B200 (sm_100a) Mamba-3 single-token decode.
+ *
+ * One entry point per GPU routine of the reference's kernel package
+ * (michaelYZh/mamba3-fused-triton-kernel, src/kernels/*.py).  The reference
+ * binds those routines from Python; the Python package in this repository
+ * binds these symbols through ctypes with the same argument meaning.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers on the CURRENT device, owned by the
+ *     caller.  Nothing here allocates or frees memory, synchronises the host
+ *     or starts threads.  Work is enqueued on `stream` (0 = legacy default).
+ *   - Strides and sizes are in ELEMENTS, not bytes.
+ *   - The carried state (ssm_state / h, bx_prev, angle_state) is updated IN
+ *     PLACE and must be contiguous with a 16-byte aligned base.  A strided
+ *     state is rejected (M3_ERR_ALIGN) rather than copied, because a copy
+ *     would break the in-place contract.
+ *   - Arguments are validated on the host before any launch; an invalid call
+ *     returns a non-zero status and enqueues nothing.  Device code never traps.
+ *   - Calls are safe to capture in a CUDA graph after one eager call on the
+ *     device (the first call sets kernel attributes).
+ */
+#ifndef MAMBA3_B200_H
+#define MAMBA3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream. */
+typedef struct CUstream_st *m3_stream_t;
+
+/* Status codes. */
+enum {
+  M3_OK = 0,
+  M3_ERR_NULL = 1,   /* a required pointer is NULL                         */
+  M3_ERR_SHAPE = 2,  /* inconsistent or unsupported sizes                  */
+  M3_ERR_RANK = 3,   /* unsupported mimo_rank (supported: 1, 2, 4, 8)      */
+  M3_ERR_DTYPE = 4,  /* unsupported dtype code                             */
+  M3_ERR_ALIGN = 5,  /* state not contiguous / not 16-byte aligned         */
+  M3_ERR_LAUNCH = 6, /* the CUDA launch itself failed                      */
+  M3_ERR_DEVICE = 7  /* no usable CUDA device                              */
+};
+
+/* Element type codes. */
+enum { M3_F32 = 0, M3_BF16 = 1 };
+
+/* Geometry of one Mamba-3 layer (src/models/mamba3.py:87-114).
+ * d_inner must equal nheads * headdim; ngroups must be 1 (the reference
+ * decode path expands one B/C group over all heads, mamba3.py:209-210).
+ * d_state must be a multiple of 4 and at most 256; num_rope_angles <=
+ * d_state / 2 (the first 2*num_rope_angles state entries are rotated). */
+typedef struct m3_dims {
+  int32_t batch;           /* B                                  */
+  int32_t nheads;          /* H                                  */
+  int32_t headdim;         /* P                                  */
+  int32_t d_state;         /* D                                  */
+  int32_t mimo_rank;       /* R (1 for SISO)                     */
+  int32_t num_rope_angles; /* A (full-fused entry points only)   */
+  int32_t ngroups;         /* G, must be 1                       */
+  int32_t d_inner;         /* H * P                              */
+  float A_floor;           /* full-fused entry points only       */
+} m3_dims;
+
+/* Arguments of the state-update-only entry points (precomputed B/C/dt).
+ * Shapes follow the reference kernels:
+ *   x, z, y        (B, H, P)        any strides; x/z/y may be bf16
+ *   B_proj, C_proj SISO (B, H, D), MIMO (B, R, H, D)   any strides, f32
+ *   ADT, DT, trap  (B, H)           any strides, f32
+ *   D_skip         (H,)             any stride,  f32
+ *   mimo_x, mimo_o (H, R, P)        any strides, f32 (MIMO only)
+ *   h, bx_prev     SISO (B, H, P, D), MIMO (B, H, D)  contiguous f32, in place
+ * z == NULL selects the un-gated routines; the *_fused entry points require
+ * z and multiply y by silu(z). */
+typedef struct m3_ssm_args {
+  const void *x;  int64_t x_sb, x_sh, x_sp;  int32_t x_dtype;
+  const void *z;  int64_t z_sb, z_sh, z_sp;  int32_t z_dtype;
+  void *y;        int64_t y_sb, y_sh, y_sp;  int32_t y_dtype;
+  const float *B_proj; int64_t B_sb, B_sr, B_sh, B_sd;
+  const float *C_proj; int64_t C_sb, C_sr, C_sh, C_sd;
+  const float *ADT;    int64_t adt_sb, adt_sh;
+  const float *DT;     int64_t dt_sb, dt_sh;
+  const float *trap;   int64_t trap_sb, trap_sh;
+  const float *D_skip; int64_t D_sh;
+  const float *mimo_x; int64_t mx_sh, mx_sr, mx_sp;
+  const float *mimo_o; int64_t mo_sh, mo_sr, mo_sp;
+  float *h;
+  float *bx_prev;
+} m3_ssm_args;
+
+/* Arguments of the full-step fused entry points.
+ *   zx           (B, d_in_proj) row stride zx_stride_b, unit column stride;
+ *                the raw in_proj output [z | x | B | C | dd_dt | dd_A |
+ *                trap | angle] (mamba3.py:165-179); f32 or bf16
+ *   dt_bias, D   (H,)          param_dtype
+ *   B_norm_w, C_norm_w (D,)    param_dtype
+ *   B_bias, C_bias (H, R, D)   param_dtype, contiguous
+ *   mimo_x, mimo_o (H, R, P)   param_dtype, contiguous (MIMO only)
+ *   ssm_state    SISO (B, H, P, D), MIMO (B, H, D)   contiguous f32, in place
+ *   bx_prev      same shape as ssm_state                 contiguous f32, in place
+ *   angle_state  (B, H, A)                               contiguous f32, in place
+ *   y            (B, H*P) row stride y_stride_b; silu(z)-gated output;
+ *                f32 or bf16 (bf16 rounds to nearest even, like .to(bf16)) */
+typedef struct m3_full_args {
+  const void *zx;  int64_t zx_stride_b; int32_t zx_dtype;
+  int32_t param_dtype;
+  const void *dt_bias, *D, *B_norm_w, *C_norm_w, *B_bias, *C_bias, *mimo_x, *mimo_o;
+  float *ssm_state;
+  float *bx_prev;
+  float *angle_state;
+  void *y; int64_t y_stride_b; int32_t y_dtype;
+} m3_full_args;
+
+/* Replaces mamba3_siso_decode_triton (src/kernels/siso_decode.py:136-187). */
+int m3_siso_decode(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream);
+
+/* Replaces mamba3_mimo_decode_triton (src/kernels/mimo_decode.py:394-457);
+ * mimo_rank in {1, 2, 4, 8}, else M3_ERR_RANK (the reference raises
+ * ValueError, mimo_decode.py:426-430). */
+int m3_mimo_decode(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream);
+
+/* Replaces mamba3_siso_decode_fused_triton (src/kernels/siso_decode_fused.py:143-193). */
+int m3_siso_decode_fused(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream);
+
+/* Replaces mamba3_mimo_decode_fused_triton (src/kernels/mimo_decode_fused.py:114-170);
+ * lifts the reference's R == 4 restriction (mimo_decode_fused.py:144). */
+int m3_mimo_decode_fused(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream);
+
+/* Replaces mamba3_siso_full_fused_triton (src/kernels/fused_full_decode.py:228-289). */
+int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream);
+
+/* Replaces mamba3_mimo_full_fused_triton (src/kernels/fused_full_decode.py:569-636);
+ * lifts the reference's R == 4 restriction (fused_full_decode.py:600). */
+int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int m3_version(void);
+
+/* Static, NUL-terminated description of a status code. */
+const char *m3_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA3_B200_H */

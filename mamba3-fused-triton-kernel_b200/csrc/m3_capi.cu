@@ -1,0 +1,161 @@
+// extern "C" entry points declared in include/mamba3_b200.h.
+//
+// Each entry point validates its arguments on the host, fills the kernel
+// parameter block and enqueues exactly one kernel on the caller's stream.
+// No allocation, no synchronisation, no device-side traps.
+#include <cstdint>
+
+#include "m3_kernels.cuh"
+
+namespace {
+
+using m3::KParams;
+
+constexpr int kVersion = 10000;  // 1.0.0
+constexpr int kMaxHeaddim = 4096;
+
+bool dtype_ok(int32_t dt) { return dt == M3_F32 || dt == M3_BF16; }
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Sizes shared by every entry point.  batch == 0 is a valid empty call.
+int check_dims(const m3_dims *d, bool mimo) {
+  if (!d) return M3_ERR_NULL;
+  if (d->batch < 0 || d->nheads <= 0 || d->headdim <= 0 || d->d_state <= 0) return M3_ERR_SHAPE;
+  if (d->headdim > kMaxHeaddim) return M3_ERR_SHAPE;
+  if (d->d_state % 4 != 0 || d->d_state > 256) return M3_ERR_SHAPE;
+  if (mimo) {
+    const int r = d->mimo_rank;
+    if (r != 1 && r != 2 && r != 4 && r != 8) return M3_ERR_RANK;
+  }
+  return M3_OK;
+}
+
+int check_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    cudaGetLastError();
+    return M3_ERR_DEVICE;
+  }
+  return M3_OK;
+}
+
+int launch_status(cudaError_t e) { return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH; }
+
+int ssm_entry(const m3_dims *d, const m3_ssm_args *a, m3_stream_t stream, bool mimo, bool gated) {
+  int st = check_dims(d, mimo);
+  if (st != M3_OK) return st;
+  if (!a) return M3_ERR_NULL;
+  if (!a->x || !a->y || !a->B_proj || !a->C_proj || !a->ADT || !a->DT || !a->trap || !a->D_skip ||
+      !a->h || !a->bx_prev)
+    return M3_ERR_NULL;
+  if (mimo && (!a->mimo_x || !a->mimo_o)) return M3_ERR_NULL;
+  if (gated && !a->z) return M3_ERR_NULL;
+  if (!dtype_ok(a->x_dtype) || !dtype_ok(a->y_dtype) || (gated && !dtype_ok(a->z_dtype)))
+    return M3_ERR_DTYPE;
+  if (!aligned16(a->h) || !aligned16(a->bx_prev)) return M3_ERR_ALIGN;
+  if (d->batch == 0) return M3_OK;
+  st = check_device();
+  if (st != M3_OK) return st;
+
+  KParams kp = {};
+  kp.B = d->batch; kp.H = d->nheads; kp.P = d->headdim; kp.D = d->d_state;
+  kp.R = mimo ? d->mimo_rank : 1;
+  kp.heads_per_cta = m3::mimo_heads_per_cta(kp.H);
+  kp.x = a->x; kp.x_sb = a->x_sb; kp.x_sh = a->x_sh; kp.x_sp = a->x_sp; kp.x_dt = a->x_dtype;
+  kp.z = gated ? a->z : nullptr;
+  kp.z_sb = a->z_sb; kp.z_sh = a->z_sh; kp.z_sp = a->z_sp; kp.z_dt = a->z_dtype;
+  kp.y = a->y; kp.y_sb = a->y_sb; kp.y_sh = a->y_sh; kp.y_sp = a->y_sp; kp.y_dt = a->y_dtype;
+  kp.Bp = a->B_proj; kp.B_sb = a->B_sb; kp.B_sr = a->B_sr; kp.B_sh = a->B_sh; kp.B_sd = a->B_sd;
+  kp.Cp = a->C_proj; kp.C_sb = a->C_sb; kp.C_sr = a->C_sr; kp.C_sh = a->C_sh; kp.C_sd = a->C_sd;
+  kp.adt = a->ADT; kp.adt_sb = a->adt_sb; kp.adt_sh = a->adt_sh;
+  kp.dt = a->DT; kp.dt_sb = a->dt_sb; kp.dt_sh = a->dt_sh;
+  kp.trap = a->trap; kp.tr_sb = a->trap_sb; kp.tr_sh = a->trap_sh;
+  kp.Dsk = a->D_skip; kp.D_sh = a->D_sh;
+  kp.smx = a->mimo_x; kp.mx_sh = a->mx_sh; kp.mx_sr = a->mx_sr; kp.mx_sp = a->mx_sp;
+  kp.smo = a->mimo_o; kp.mo_sh = a->mo_sh; kp.mo_sr = a->mo_sr; kp.mo_sp = a->mo_sp;
+  kp.h = a->h; kp.bx = a->bx_prev;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return launch_status(mimo ? m3::launch_mimo(kp, false, s) : m3::launch_siso(kp, false, s));
+}
+
+int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool mimo) {
+  int st = check_dims(d, mimo);
+  if (st != M3_OK) return st;
+  if (!a) return M3_ERR_NULL;
+  if (d->ngroups != 1) return M3_ERR_SHAPE;
+  if (d->d_inner != d->nheads * d->headdim) return M3_ERR_SHAPE;
+  if (d->num_rope_angles <= 0 || 2 * d->num_rope_angles > d->d_state) return M3_ERR_SHAPE;
+  const int R = mimo ? d->mimo_rank : 1;
+  const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * R + 3LL * d->nheads + d->num_rope_angles;
+  if (a->zx_stride_b < d_in_proj) return M3_ERR_SHAPE;
+  if (a->y_stride_b < (int64_t)d->d_inner) return M3_ERR_SHAPE;
+  if (!a->zx || !a->dt_bias || !a->D || !a->B_norm_w || !a->C_norm_w || !a->B_bias || !a->C_bias ||
+      !a->ssm_state || !a->bx_prev || !a->angle_state || !a->y)
+    return M3_ERR_NULL;
+  if (mimo && (!a->mimo_x || !a->mimo_o)) return M3_ERR_NULL;
+  if (!dtype_ok(a->zx_dtype) || !dtype_ok(a->param_dtype) || !dtype_ok(a->y_dtype)) return M3_ERR_DTYPE;
+  if (!aligned16(a->ssm_state) || !aligned16(a->bx_prev)) return M3_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(a->angle_state) & 3u) != 0) return M3_ERR_ALIGN;
+  if (d->batch == 0) return M3_OK;
+  st = check_device();
+  if (st != M3_OK) return st;
+
+  KParams kp = {};
+  kp.B = d->batch; kp.H = d->nheads; kp.P = d->headdim; kp.D = d->d_state; kp.R = R;
+  kp.A = d->num_rope_angles; kp.A_floor = d->A_floor;
+  kp.d_inner = d->d_inner; kp.d_bc = d->d_state * R;
+  kp.heads_per_cta = m3::mimo_heads_per_cta(kp.H);
+  kp.zx = a->zx; kp.zx_sb = a->zx_stride_b; kp.zx_dt = a->zx_dtype; kp.par_dt = a->param_dtype;
+  kp.dt_bias = a->dt_bias; kp.Dp = a->D; kp.wB = a->B_norm_w; kp.wC = a->C_norm_w;
+  kp.bB = a->B_bias; kp.bC = a->C_bias; kp.mx = a->mimo_x; kp.mo = a->mimo_o;
+  kp.h = a->ssm_state; kp.bx = a->bx_prev; kp.ang = a->angle_state;
+  kp.y = a->y; kp.y_sb = a->y_stride_b; kp.y_sh = d->headdim; kp.y_sp = 1; kp.y_dt = a->y_dtype;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return launch_status(mimo ? m3::launch_mimo(kp, true, s) : m3::launch_siso(kp, true, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+int m3_siso_decode(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream) {
+  return ssm_entry(dims, args, stream, false, false);
+}
+
+int m3_mimo_decode(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream) {
+  return ssm_entry(dims, args, stream, true, false);
+}
+
+int m3_siso_decode_fused(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream) {
+  return ssm_entry(dims, args, stream, false, true);
+}
+
+int m3_mimo_decode_fused(const m3_dims *dims, const m3_ssm_args *args, m3_stream_t stream) {
+  return ssm_entry(dims, args, stream, true, true);
+}
+
+int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {
+  return full_entry(dims, args, stream, false);
+}
+
+int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {
+  return full_entry(dims, args, stream, true);
+}
+
+int m3_version(void) { return kVersion; }
+
+const char *m3_status_string(int status) {
+  switch (status) {
+    case M3_OK: return "ok";
+    case M3_ERR_NULL: return "a required pointer is NULL";
+    case M3_ERR_SHAPE: return "inconsistent or unsupported sizes";
+    case M3_ERR_RANK: return "unsupported mimo_rank (supported: 1, 2, 4, 8)";
+    case M3_ERR_DTYPE: return "unsupported dtype code";
+    case M3_ERR_ALIGN: return "state must be contiguous with a 16-byte aligned base";
+    case M3_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case M3_ERR_DEVICE: return "no usable CUDA device";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,601 @@
+// Mamba-3 single-token decode kernels for B200 (sm_100a).
+//
+// Two kernel families, each instantiated for the full-step fused variant
+// (reads the raw in_proj output) and the state-update-only variant (reads
+// precomputed B/C/dt/trap, as the reference's SSM kernels do):
+//
+//   siso_decode_kernel  one CTA per (batch, head).  The (P, D) state tile of
+//                       ssm_state and bx_prev is contiguous in HBM and is
+//                       streamed once in and once out with 128-bit accesses.
+//                       A group of S lanes owns one state row (S = D/4
+//                       float4 columns, capped at 32); the readout C.h is a
+//                       shuffle reduction inside that group.  The first
+//                       rows' state loads are issued before the per-head
+//                       prologue (RMSNorm, bias, RoPE, scalars) so their
+//                       latency overlaps it.
+//   mimo_decode_kernel  one CTA per (batch, group of heads), one warp per
+//                       head.  The (D,) state of a head is spread over the
+//                       warp's lanes (2 or 4 floats per lane, so every RoPE
+//                       pair is lane-local); RMSNorm of the rank-R B/C rows
+//                       is done once per CTA into shared memory; the rank-R
+//                       contractions are warp shuffles.
+//
+// Arithmetic follows the reference PyTorch decode (src/models/mamba3.py:
+// 160-217, 306-353; src/kernels/utils.py:31-148) operation by operation in
+// fp32, including the A = -(softplus(dd_A).clamp(max=-A_floor)) expression
+// (which evaluates to +A_floor) and the torch softplus threshold of 20.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "mamba3_b200.h"
+
+namespace m3 {
+
+constexpr float kRmsEps = 1e-5f;  // RMSNorm eps (src/models/mamba3.py:29)
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// Everything a launch needs; filled on the host by the C-ABI layer.
+struct KParams {
+  int B, H, P, D, R, A;
+  float A_floor;
+  int d_inner, d_bc;  // d_bc = D * ngroups * R
+  int heads_per_cta;  // MIMO only
+  // full-step fused sources
+  const void *zx; int64_t zx_sb; int zx_dt; int par_dt;
+  const void *dt_bias, *Dp, *wB, *wC, *bB, *bC, *mx, *mo;
+  // state-update-only sources
+  const void *x; int64_t x_sb, x_sh, x_sp; int x_dt;
+  const void *z; int64_t z_sb, z_sh, z_sp; int z_dt;
+  const float *Bp; int64_t B_sb, B_sr, B_sh, B_sd;
+  const float *Cp; int64_t C_sb, C_sr, C_sh, C_sd;
+  const float *adt; int64_t adt_sb, adt_sh;
+  const float *dt; int64_t dt_sb, dt_sh;
+  const float *trap; int64_t tr_sb, tr_sh;
+  const float *Dsk; int64_t D_sh;
+  const float *smx; int64_t mx_sh, mx_sr, mx_sp;
+  const float *smo; int64_t mo_sh, mo_sr, mo_sp;
+  // carried state (in place) and output
+  float *h, *bx, *ang;
+  void *y; int64_t y_sb, y_sh, y_sp; int y_dt;
+};
+
+// ---------------------------------------------------------------------------
+// scalar helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float ld_any(const void *p, int64_t i, int dt) {
+  return dt == M3_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i])
+                       : static_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void st_any(void *p, int64_t i, float v, int dt) {
+  if (dt == M3_BF16)
+    static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<float *>(p)[i] = v;
+}
+
+// torch.nn.functional.softplus(beta=1, threshold=20)
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
+// Sum over aligned groups of W lanes (W a power of two <= 32); every lane
+// of the warp must call it.
+template <int W>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+
+// 128-bit state accesses.  The state is touched exactly once per launch, so
+// loads skip L1 allocation; L2 keeps its default policy so that a state that
+// fits in L2 stays resident from one decode step to the next.
+__device__ __forceinline__ float4 ld_state4(const float *p) {
+  float4 v;
+  asm volatile("ld.global.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float2 ld_state2(const float *p) {
+  float2 v;
+  asm volatile("ld.global.L1::no_allocate.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_state4(float *p, float4 v) {
+  *reinterpret_cast<float4 *>(p) = v;
+}
+__device__ __forceinline__ void st_state2(float *p, float2 v) {
+  *reinterpret_cast<float2 *>(p) = v;
+}
+
+// One element of the exponential-trapezoidal update
+// (src/kernels/utils.py:95-99):  bx = x*B;  blend = (1-trap)*bx +
+// (trap*0.5)*(bx + bx_prev);  h = exp(ADT)*h + DT*blend.
+struct Coef {
+  float decay, DT, omt, htr;  // exp(ADT), DT, 1 - trap, trap * 0.5
+};
+
+__device__ __forceinline__ float trap_update(const Coef &c, float bx, float bx_prev, float h) {
+  const float blend = c.omt * bx + c.htr * (bx + bx_prev);
+  return c.decay * h + c.DT * blend;
+}
+
+// Per-(batch, head) scalars from the raw in_proj row
+// (src/models/mamba3.py:196-199; the scalar section starts at
+// 2*d_inner + 2*d_bc: dd_dt[H], dd_A[H], trap[H]).
+__device__ __forceinline__ void head_scalars_from_zx(const KParams &p, int64_t zr, int hh, Coef &c,
+                                                     float &dskip) {
+  const int so = 2 * p.d_inner + 2 * p.d_bc;
+  const float dd_dt = ld_any(p.zx, zr + so + hh, p.zx_dt);
+  const float dd_A = ld_any(p.zx, zr + so + p.H + hh, p.zx_dt);
+  const float tr_raw = ld_any(p.zx, zr + so + 2 * p.H + hh, p.zx_dt);
+  const float sp = softplus_f(dd_A);
+  // clamp(max=-A_floor) keeps a NaN, as torch.clamp does
+  const float A = -(sp > -p.A_floor ? -p.A_floor : sp);
+  c.DT = softplus_f(dd_dt + ld_any(p.dt_bias, hh, p.par_dt));
+  c.decay = expf(A * c.DT);
+  const float tr = sigmoid_f(tr_raw);
+  c.omt = 1.f - tr;
+  c.htr = tr * 0.5f;
+  dskip = ld_any(p.Dp, hh, p.par_dt);
+}
+
+__device__ __forceinline__ void head_scalars_given(const KParams &p, int b, int hh, Coef &c,
+                                                   float &dskip) {
+  c.DT = p.dt[(int64_t)b * p.dt_sb + (int64_t)hh * p.dt_sh];
+  c.decay = expf(p.adt[(int64_t)b * p.adt_sb + (int64_t)hh * p.adt_sh]);
+  const float tr = p.trap[(int64_t)b * p.tr_sb + (int64_t)hh * p.tr_sh];
+  c.omt = 1.f - tr;
+  c.htr = tr * 0.5f;
+  dskip = p.Dsk[(int64_t)hh * p.D_sh];
+}
+
+// ---------------------------------------------------------------------------
+// SISO: state (B, H, P, D); one CTA per (b, h)
+// ---------------------------------------------------------------------------
+
+template <int BD>
+struct SisoShape {
+  static constexpr int BG = BD / 4;               // float4 columns per row (padded)
+  static constexpr int S = BG < 32 ? BG : 32;     // lanes per row
+  static constexpr int FPL = BG / S;              // float4 per lane per row
+  static constexpr int RPW = 32 / S;              // rows per warp per pass
+  static constexpr int RPT = 4 / FPL;             // rows per thread per iteration
+  static constexpr int KPL = BD >= 32 ? BD / 32 : 1;  // prologue elements per lane
+};
+
+template <int BD, bool FULL>
+__global__ void __launch_bounds__(512) siso_decode_kernel(const KParams p) {
+  using Sh = SisoShape<BD>;
+  constexpr int S = Sh::S, FPL = Sh::FPL, RPW = Sh::RPW, RPT = Sh::RPT, KPL = Sh::KPL;
+
+  extern __shared__ __align__(16) float smem[];
+  float *sB = smem;           // [BD]  B after norm/bias/RoPE (or B_proj)
+  float *sC = smem + BD;      // [BD]
+  float *sX = smem + 2 * BD;  // [P]   x
+  float *sG = sX + p.P;       // [P]   silu(z)
+
+  const int bh = blockIdx.x;
+  const int b = bh / p.H;
+  const int hh = bh - b * p.H;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int P = p.P, D = p.D, G = D >> 2;
+  const int nslots = (nthr >> 5) * RPW;
+  const int slot = warp * RPW + lane / S;
+  const int j = lane % S;
+  const int rows_per_iter = nslots * RPT;
+  const int64_t tile = (int64_t)bh * P * D;
+  float *hs = p.h + tile;
+  float *bs = p.bx + tile;
+
+  float4 hv[RPT][FPL], bv[RPT][FPL];
+  auto load_rows = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < RPT; ++u) {
+      const int row = base + u * nslots + slot;
+#pragma unroll
+      for (int f = 0; f < FPL; ++f) {
+        const int col = j + S * f;
+        if (row < P && col < G) {
+          const int64_t o = ((int64_t)row * G + col) * 4;
+          hv[u][f] = ld_state4(hs + o);
+          bv[u][f] = ld_state4(bs + o);
+        } else {
+          hv[u][f] = make_float4(0.f, 0.f, 0.f, 0.f);
+          bv[u][f] = hv[u][f];
+        }
+      }
+    }
+  };
+  load_rows(0);  // in flight while the prologue runs
+
+  Coef c;
+  float dskip;
+  bool gate;
+  if constexpr (FULL) {
+    const int64_t zr = (int64_t)b * p.zx_sb;
+    head_scalars_from_zx(p, zr, hh, c, dskip);
+    gate = true;
+    if (warp == 0) {
+      // B and C rows of rank 0 (src/models/mamba3.py:202-215), RoPE on the
+      // first 2A entries (utils.py:31-44); angle_state += angle_raw * DT
+      // (mamba3.py:326-327) is written back by this warp only.
+      const int colB = 2 * p.d_inner, colC = 2 * p.d_inner + p.d_bc;
+      const int acol = 2 * p.d_inner + 2 * p.d_bc + 3 * p.H;
+      float vb[KPL], vc[KPL];
+      float ssb = 0.f, ssc = 0.f;
+#pragma unroll
+      for (int k = 0; k < KPL; ++k) {
+        const int d = lane + 32 * k;
+        vb[k] = d < D ? ld_any(p.zx, zr + colB + d, p.zx_dt) : 0.f;
+        vc[k] = d < D ? ld_any(p.zx, zr + colC + d, p.zx_dt) : 0.f;
+        ssb += vb[k] * vb[k];
+        ssc += vc[k] * vc[k];
+      }
+      ssb = group_sum<32>(ssb);
+      ssc = group_sum<32>(ssc);
+      const float rmsb = sqrtf(ssb / (float)D + kRmsEps);
+      const float rmsc = sqrtf(ssc / (float)D + kRmsEps);
+#pragma unroll
+      for (int k = 0; k < KPL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) {
+          const int64_t bi = (int64_t)hh * D + d;  // (H, R=1, D)
+          vb[k] = vb[k] / rmsb * ld_any(p.wB, d, p.par_dt) + ld_any(p.bB, bi, p.par_dt);
+          vc[k] = vc[k] / rmsc * ld_any(p.wC, d, p.par_dt) + ld_any(p.bC, bi, p.par_dt);
+        }
+        const bool rot = d < 2 * p.A;
+        float sn = 0.f, cs = 1.f, ang = 0.f;
+        if (rot) {
+          const int i = d >> 1;
+          ang = p.ang[(int64_t)bh * p.A + i] + ld_any(p.zx, zr + acol + i, p.zx_dt) * c.DT;
+          sincosf(ang, &sn, &cs);
+        }
+        const float ob = __shfl_xor_sync(kFullMask, vb[k], 1);
+        const float oc = __shfl_xor_sync(kFullMask, vc[k], 1);
+        if (rot) {
+          if (d & 1) {
+            vb[k] = ob * sn + vb[k] * cs;
+            vc[k] = oc * sn + vc[k] * cs;
+          } else {
+            vb[k] = vb[k] * cs - ob * sn;
+            vc[k] = vc[k] * cs - oc * sn;
+            p.ang[(int64_t)bh * p.A + (d >> 1)] = ang;
+          }
+        }
+        if (d < D) {
+          sB[d] = vb[k];
+          sC[d] = vc[k];
+        }
+      }
+    }
+    for (int t = tid; t < P; t += nthr) {
+      sX[t] = ld_any(p.zx, zr + p.d_inner + (int64_t)hh * P + t, p.zx_dt);
+      sG[t] = silu_f(ld_any(p.zx, zr + (int64_t)hh * P + t, p.zx_dt));
+    }
+  } else {
+    head_scalars_given(p, b, hh, c, dskip);
+    gate = p.z != nullptr;
+    for (int t = tid; t < D; t += nthr) {
+      sB[t] = p.Bp[(int64_t)b * p.B_sb + (int64_t)hh * p.B_sh + (int64_t)t * p.B_sd];
+      sC[t] = p.Cp[(int64_t)b * p.C_sb + (int64_t)hh * p.C_sh + (int64_t)t * p.C_sd];
+    }
+    for (int t = tid; t < P; t += nthr) {
+      sX[t] = ld_any(p.x, (int64_t)b * p.x_sb + (int64_t)hh * p.x_sh + (int64_t)t * p.x_sp, p.x_dt);
+      if (gate)
+        sG[t] = silu_f(ld_any(p.z, (int64_t)b * p.z_sb + (int64_t)hh * p.z_sh + (int64_t)t * p.z_sp,
+                              p.z_dt));
+    }
+  }
+  __syncthreads();
+
+  const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * p.y_sh;
+  for (int base = 0; base < P; base += rows_per_iter) {
+    if (base != 0) load_rows(base);
+#pragma unroll
+    for (int u = 0; u < RPT; ++u) {
+      const int row = base + u * nslots + slot;
+      const bool rok = row < P;
+      const float xp = rok ? sX[row] : 0.f;
+      float part = 0.f;
+#pragma unroll
+      for (int f = 0; f < FPL; ++f) {
+        const int col = j + S * f;
+        if (rok && col < G) {
+          const float4 Bq = reinterpret_cast<const float4 *>(sB)[col];
+          const float4 Cq = reinterpret_cast<const float4 *>(sC)[col];
+          const float4 ho = hv[u][f], bo = bv[u][f];
+          float4 bn, hn;
+          bn.x = xp * Bq.x; bn.y = xp * Bq.y; bn.z = xp * Bq.z; bn.w = xp * Bq.w;
+          hn.x = trap_update(c, bn.x, bo.x, ho.x);
+          hn.y = trap_update(c, bn.y, bo.y, ho.y);
+          hn.z = trap_update(c, bn.z, bo.z, ho.z);
+          hn.w = trap_update(c, bn.w, bo.w, ho.w);
+          part += Cq.x * hn.x;
+          part += Cq.y * hn.y;
+          part += Cq.z * hn.z;
+          part += Cq.w * hn.w;
+          const int64_t o = ((int64_t)row * G + col) * 4;
+          st_state4(hs + o, hn);
+          st_state4(bs + o, bn);
+        }
+      }
+      part = group_sum<S>(part);
+      if (j == 0 && rok) {
+        float yv = part + dskip * xp;
+        if (gate) yv = yv * sG[row];
+        st_any(p.y, ybase + (int64_t)row * p.y_sp, yv, p.y_dt);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// MIMO: state (B, H, D); one CTA per (b, group of heads), one warp per head
+// ---------------------------------------------------------------------------
+
+template <int VW> struct VecOf;
+template <> struct VecOf<4> { using T = float4; };
+template <> struct VecOf<2> { using T = float2; };
+
+template <int BD>
+struct MimoShape {
+  static constexpr int VW = BD >= 128 ? 4 : 2;     // floats per lane vector
+  static constexpr int NV = BD / VW;               // vectors per head row (padded)
+  static constexpr int F = NV > 32 ? NV / 32 : 1;  // vectors per lane
+  static constexpr int KPL = BD >= 32 ? BD / 32 : 1;
+};
+
+template <int VW>
+__device__ __forceinline__ void ld_vec(const float *p, float (&v)[VW]) {
+  if constexpr (VW == 4) {
+    const float4 t = ld_state4(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    const float2 t = ld_state2(p);
+    v[0] = t.x; v[1] = t.y;
+  }
+}
+template <int VW>
+__device__ __forceinline__ void st_vec(float *p, const float (&v)[VW]) {
+  if constexpr (VW == 4)
+    st_state4(p, make_float4(v[0], v[1], v[2], v[3]));
+  else
+    st_state2(p, make_float2(v[0], v[1]));
+}
+
+template <int BD, int R, bool FULL>
+__global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
+  using Sh = MimoShape<BD>;
+  constexpr int VW = Sh::VW, F = Sh::F, KPL = Sh::KPL, NPAIR = VW / 2;
+
+  extern __shared__ __align__(16) float smem[];  // FULL: [2R][BD] normalized B_r, C_r
+
+  const int hpc = p.heads_per_cta;
+  const int ngrp = (p.H + hpc - 1) / hpc;
+  const int b = blockIdx.x / ngrp;
+  const int hg = blockIdx.x - b * ngrp;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int hh = hg * hpc + warp;
+  const bool head_ok = warp < hpc && hh < p.H;
+  const int D = p.D, P = p.P;
+  const int64_t sbase = ((int64_t)b * p.H + hh) * D;
+  const int64_t zr = (int64_t)b * p.zx_sb;
+
+  // state of this warp's head, in flight during the prologue
+  float hv[F][VW], bv[F][VW];
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    const int col = (lane + 32 * f) * VW;
+    if (head_ok && col < D) {
+      ld_vec<VW>(p.h + sbase + col, hv[f]);
+      ld_vec<VW>(p.bx + sbase + col, bv[f]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VW; ++e) hv[f][e] = bv[f][e] = 0.f;
+    }
+  }
+
+  if constexpr (FULL) {
+    // RMSNorm of the R B-rows and R C-rows of this batch row, shared by
+    // every head of the CTA (src/models/mamba3.py:202-203; "(r g n)" layout).
+    for (int row = warp; row < 2 * R; row += nwarps) {
+      const int r = row % R;
+      const int col0 = 2 * p.d_inner + (row < R ? 0 : p.d_bc) + r * D;
+      const void *wn = row < R ? p.wB : p.wC;
+      float v[KPL];
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < KPL; ++k) {
+        const int d = lane + 32 * k;
+        v[k] = d < D ? ld_any(p.zx, zr + col0 + d, p.zx_dt) : 0.f;
+        ss += v[k] * v[k];
+      }
+      ss = group_sum<32>(ss);
+      const float rms = sqrtf(ss / (float)D + kRmsEps);
+#pragma unroll
+      for (int k = 0; k < KPL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) smem[row * BD + d] = v[k] / rms * ld_any(wn, d, p.par_dt);
+      }
+    }
+    __syncthreads();
+  }
+  if (!head_ok) return;
+
+  Coef c;
+  float dskip;
+  if constexpr (FULL)
+    head_scalars_from_zx(p, zr, hh, c, dskip);
+  else
+    head_scalars_given(p, b, hh, c, dskip);
+
+  // RoPE coefficients of this lane's pairs; pair i covers entries (2i, 2i+1)
+  // and is rotated iff i < A.  Each pair belongs to exactly one lane, which
+  // also writes the accumulated angle back.
+  float cs[F][NPAIR], sn[F][NPAIR];
+  if constexpr (FULL) {
+    const int acol = 2 * p.d_inner + 2 * p.d_bc + 3 * p.H;
+    const int64_t abase = ((int64_t)b * p.H + hh) * p.A;
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+#pragma unroll
+      for (int q = 0; q < NPAIR; ++q) {
+        const int i = (lane + 32 * f) * NPAIR + q;
+        cs[f][q] = 1.f;
+        sn[f][q] = 0.f;
+        if (i < p.A) {
+          const float ang = p.ang[abase + i] + ld_any(p.zx, zr + acol + i, p.zx_dt) * c.DT;
+          p.ang[abase + i] = ang;
+          sincosf(ang, &sn[f][q], &cs[f][q]);
+        }
+      }
+    }
+  }
+
+  // x_r = sum_p x_p * mimo_x[h, r, p]   (src/kernels/utils.py:130)
+  float xr[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) xr[r] = 0.f;
+  for (int p0 = 0; p0 < P; p0 += 32) {
+    const int pp = p0 + lane;
+    if (pp < P) {
+      float xp;
+      if constexpr (FULL)
+        xp = ld_any(p.zx, zr + p.d_inner + (int64_t)hh * P + pp, p.zx_dt);
+      else
+        xp = ld_any(p.x, (int64_t)b * p.x_sb + (int64_t)hh * p.x_sh + (int64_t)pp * p.x_sp, p.x_dt);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float m;
+        if constexpr (FULL)
+          m = ld_any(p.mx, ((int64_t)hh * R + r) * P + pp, p.par_dt);
+        else
+          m = p.smx[(int64_t)hh * p.mx_sh + (int64_t)r * p.mx_sr + (int64_t)pp * p.mx_sp];
+        xr[r] += xp * m;
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) xr[r] = group_sum<32>(xr[r]);
+
+  // B_r / C_r vector of this lane: FULL = RoPE(norm + bias[h, r]); else the
+  // precomputed projection.
+  auto bc_vec = [&](bool isC, int r, int f, float (&v)[VW]) {
+    const int col = (lane + 32 * f) * VW;
+    if constexpr (FULL) {
+      const float *nrow = smem + (isC ? R + r : r) * BD + col;
+      const void *bias = isC ? p.bC : p.bB;
+      const int64_t bi = ((int64_t)hh * R + r) * D + col;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) v[e] = nrow[e] + ld_any(bias, bi + e, p.par_dt);
+#pragma unroll
+      for (int q = 0; q < NPAIR; ++q) {
+        const float x1 = v[2 * q], x2 = v[2 * q + 1];
+        if ((lane + 32 * f) * NPAIR + q < p.A) {
+          v[2 * q] = x1 * cs[f][q] - x2 * sn[f][q];
+          v[2 * q + 1] = x1 * sn[f][q] + x2 * cs[f][q];
+        }
+      }
+    } else {
+      const float *src = isC ? p.Cp : p.Bp;
+      const int64_t sb = isC ? p.C_sb : p.B_sb, sr = isC ? p.C_sr : p.B_sr;
+      const int64_t sh = isC ? p.C_sh : p.B_sh, sd = isC ? p.C_sd : p.B_sd;
+      const int64_t o = (int64_t)b * sb + (int64_t)r * sr + (int64_t)hh * sh;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) v[e] = src[o + (int64_t)(col + e) * sd];
+    }
+  };
+
+  // Bx = sum_r x_r * B_r   (utils.py:133), then the trapezoidal update
+  float bxc[F][VW], hn[F][VW];
+#pragma unroll
+  for (int f = 0; f < F; ++f)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) bxc[f][e] = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      if ((lane + 32 * f) * VW < D) {
+        float v[VW];
+        bc_vec(false, r, f, v);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) bxc[f][e] += xr[r] * v[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int f = 0; f < F; ++f)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) hn[f][e] = trap_update(c, bxc[f][e], bv[f][e], hv[f][e]);
+
+  // y_r = sum_d C_r[d] h[d] + D * x_r   (utils.py:143-145)
+  float yr[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float part = 0.f;
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      if ((lane + 32 * f) * VW < D) {
+        float v[VW];
+        bc_vec(true, r, f, v);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) part += v[e] * hn[f][e];
+      }
+    }
+    yr[r] = group_sum<32>(part) + dskip * xr[r];
+  }
+
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    const int col = (lane + 32 * f) * VW;
+    if (col < D) {
+      st_vec<VW>(p.h + sbase + col, hn[f]);
+      st_vec<VW>(p.bx + sbase + col, bxc[f]);
+    }
+  }
+
+  // y_p = sum_r y_r * mimo_o[h, r, p]  (utils.py:146), then * silu(z)
+  const bool gate = FULL || p.z != nullptr;
+  const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * p.y_sh;
+  for (int p0 = 0; p0 < P; p0 += 32) {
+    const int pp = p0 + lane;
+    if (pp < P) {
+      float yv = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float m;
+        if constexpr (FULL)
+          m = ld_any(p.mo, ((int64_t)hh * R + r) * P + pp, p.par_dt);
+        else
+          m = p.smo[(int64_t)hh * p.mo_sh + (int64_t)r * p.mo_sr + (int64_t)pp * p.mo_sp];
+        yv += yr[r] * m;
+      }
+      if (gate) {
+        float zv;
+        if constexpr (FULL)
+          zv = ld_any(p.zx, zr + (int64_t)hh * P + pp, p.zx_dt);
+        else
+          zv = ld_any(p.z, (int64_t)b * p.z_sb + (int64_t)hh * p.z_sh + (int64_t)pp * p.z_sp, p.z_dt);
+        yv = yv * silu_f(zv);
+      }
+      st_any(p.y, ybase + (int64_t)pp * p.y_sp, yv, p.y_dt);
+    }
+  }
+}
+
+// Launchers (defined in m3_siso.cu / m3_mimo.cu); return the launch status.
+cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream);
+cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
+
+// Thread-block shape chosen by the launchers (exposed for the host checks).
+int siso_block_threads(int D, int P);
+int mimo_heads_per_cta(int H);
+
+}  // namespace m3

@@ -1,0 +1,247 @@
+"""Mamba-3 decoder with the sm_100a CUDA backends.
+
+``Mamba3Decoder`` keeps the reference's constructor flags, ``init_state``,
+``warmup_cuda_graph``, ``step`` and ``decode_sequence``
+(src/models/inference.py:19-582).  Backends:
+
+  use_triton_full_fused  in_proj -> ONE fused CUDA kernel -> out_proj
+                         (the kernel updates ssm_state, bx_prev and
+                         angle_state in place)
+  use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
+                         kernel -> out_proj
+  use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
+                         kernel -> silu -> out_proj
+  use_triton=False       PyTorch reference decode (``Mamba3.step``)
+
+The flag names are kept for drop-in compatibility; no Triton code exists in
+this package.  Differences from the reference, all deliberate:
+
+* A CUDA backend requested without a CUDA device raises instead of silently
+  falling back to PyTorch, and so does a missing native library.
+* ``use_compile`` / ``use_compile_cuda_graph`` are served by the fused CUDA
+  kernel (eager / captured) instead of generating code with torch.compile.
+* The two partially fused backends update ``angle_state`` in place, so the
+  angle keeps accumulating under CUDA-graph replay (the reference rebinds it
+  to a new tensor, which a captured graph never sees).
+* The static graph input is allocated in the weight dtype, so bf16 models
+  can be captured (the reference allocates it float32).
+* The fused kernel reads bf16 in_proj output and bf16 parameters directly and
+  writes its gated output in the weight dtype, fusing the reference's
+  ``.float()`` and ``.to(u.dtype)`` casts.
+* ``decode_sequence`` under graph replay keeps a copy of every step's output
+  (the reference stacks the same static buffer seq_len times).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from src import _native
+from src.kernels import _launch
+from src.kernels.mimo_decode import mamba3_mimo_decode_triton
+from src.kernels.mimo_decode_fused import mamba3_mimo_decode_fused_triton
+from src.kernels.siso_decode import mamba3_siso_decode_triton
+from src.kernels.siso_decode_fused import mamba3_siso_decode_fused_triton
+from src.kernels.utils import apply_rope
+from src.models.mamba3 import Mamba3
+
+
+class Mamba3Decoder:
+    """Autoregressive decoder around one ``Mamba3`` layer.
+
+    Usage::
+
+        decoder = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+        state = decoder.init_state(batch_size=8)
+        decoder.warmup_cuda_graph(state)        # only with use_cuda_graph
+        for u in token_embeddings:              # u: (batch, d_model)
+            out, state = decoder.step(u, state)
+    """
+
+    def __init__(self, model: Mamba3, use_triton: bool = True, use_cuda_graph: bool = False,
+                 use_compile: bool = False, use_triton_fused: bool = False,
+                 use_compile_cuda_graph: bool = False, use_triton_full_fused: bool = False):
+        self.model = model
+        # Flag resolution as in the reference (src/models/inference.py:52-57),
+        # minus the silent CPU fallback.
+        cuda_requested = use_triton or use_triton_fused or use_triton_full_fused or \
+            use_compile or use_compile_cuda_graph
+        if cuda_requested:
+            _native.require_cuda_available()
+            _native.load()  # fail loudly now if the library is missing
+        self.use_triton = bool(use_triton)
+        self.use_triton_fused = bool(use_triton_fused)
+        self.use_triton_full_fused = bool(use_triton_full_fused)
+        cuda_backend = self.use_triton or self.use_triton_fused or self.use_triton_full_fused
+        self.use_cuda_graph = bool(use_cuda_graph) and cuda_backend
+        self.use_compile = bool(use_compile) and not cuda_backend
+        self.use_compile_cuda_graph = bool(use_compile_cuda_graph) and not self.use_cuda_graph
+        if use_cuda_graph and not cuda_backend:
+            print("Warning: CUDA Graph requires a CUDA backend, disabling")
+        if use_compile and cuda_backend:
+            print("Warning: use_compile is ignored when a CUDA backend is selected")
+
+        self._cuda_graph = None
+        self._graph_input = None
+        self._graph_output = None
+        self._graph_state = None
+        self._fused_cache = None
+
+    # ------------------------------------------------------------------
+    # public API
+    # ------------------------------------------------------------------
+
+    def init_state(self, batch_size: int, device=None, dtype=None) -> dict:
+        """Zero decode state {angle_state, ssm_state, bx_prev} (float32)."""
+        angle_state, ssm_state, bx_prev = self.model.allocate_inference_cache(
+            batch_size, device=device, dtype=dtype)
+        return {"angle_state": angle_state, "ssm_state": ssm_state, "bx_prev": bx_prev}
+
+    def warmup_cuda_graph(self, state: dict, n_warmup: int = 10) -> None:
+        """Run ``n_warmup`` eager steps on a zero input, then capture one
+        whole decode step (in_proj, the CUDA kernel(s), out_proj) in a CUDA
+        graph that updates ``state`` in place (reference:
+        src/models/inference.py:97-160).  After this, ``step`` copies its
+        input into a static buffer and replays the graph; the returned output
+        tensor is the same static buffer every step."""
+        if not (self.use_cuda_graph or self.use_compile_cuda_graph):
+            return
+        batch = state["ssm_state"].shape[0]
+        device = state["ssm_state"].device
+        self._graph_input = torch.zeros(batch, self.model.d_model, device=device,
+                                        dtype=self.model.in_proj.weight.dtype)
+        step_fn = self._graph_step_fn()
+        for _ in range(n_warmup):
+            step_fn(self._graph_input, state)
+        torch.cuda.synchronize(device)
+        self._cuda_graph = torch.cuda.CUDAGraph()
+        self._graph_state = state
+        with torch.cuda.graph(self._cuda_graph):
+            self._graph_output, self._graph_state = step_fn(self._graph_input, self._graph_state)
+
+    def step(self, u: torch.Tensor, state: dict) -> tuple:
+        """One decode step: u (batch, d_model) -> (out (batch, d_model), state)."""
+        if self._cuda_graph is not None:
+            self._graph_input.copy_(u)
+            self._cuda_graph.replay()
+            return self._graph_output, self._graph_state
+        if self.use_triton_full_fused or self.use_compile or self.use_compile_cuda_graph:
+            return self._step_triton_full_fused(u, state)
+        if self.use_triton_fused:
+            return self._step_triton_fused(u, state)
+        if self.use_triton:
+            return self._step_triton(u, state)
+        return self._step_pytorch(u, state)
+
+    def decode_sequence(self, token_embeddings: torch.Tensor, state: dict = None) -> tuple:
+        """Decode (batch, seq_len, d_model) step by step; returns
+        (outputs (batch, seq_len, d_model), final state)."""
+        batch, seq_len, _ = token_embeddings.shape
+        if state is None:
+            state = self.init_state(batch, device=token_embeddings.device)
+        outs = []
+        for t in range(seq_len):
+            out, state = self.step(token_embeddings[:, t], state)
+            # graph replay returns one static buffer; keep each step's value
+            outs.append(out.clone() if self._cuda_graph is not None else out)
+        return torch.stack(outs, dim=1), state
+
+    # ------------------------------------------------------------------
+    # backends
+    # ------------------------------------------------------------------
+
+    def _graph_step_fn(self):
+        if self.use_triton_full_fused or self.use_compile_cuda_graph:
+            return self._step_triton_full_fused
+        if self.use_triton_fused:
+            return self._step_triton_fused
+        return self._step_triton
+
+    def _step_pytorch(self, u: torch.Tensor, state: dict) -> tuple:
+        """PyTorch reference decode (reference: src/models/inference.py:271-282)."""
+        out, a, h, bx = self.model.step(u, state["angle_state"], state["ssm_state"],
+                                        state["bx_prev"])
+        state["angle_state"], state["ssm_state"], state["bx_prev"] = a, h, bx
+        return out, state
+
+    def _fused_params(self):
+        """Per-head parameters as the fused kernel reads them (one dtype,
+        contiguous); parameters that already qualify are used as they are."""
+        m = self.model
+        key = tuple(None if p is None else (p.data_ptr(), p._version, p.dtype)
+                    for p in self._param_list())
+        if self._fused_cache is not None and self._fused_cache[0] == key:
+            return self._fused_cache[1]
+        code, tensors = _launch._param_set(self._param_list())
+        if not m.is_mimo:
+            tensors[4] = tensors[4][:, 0, :]
+            tensors[5] = tensors[5][:, 0, :]
+        self._fused_cache = (key, (code, tensors))
+        return code, tensors
+
+    def _param_list(self):
+        m = self.model
+        return [m.dt_bias, m.D, m.B_norm.weight, m.C_norm.weight, m.B_bias, m.C_bias,
+                m.mimo_x if m.is_mimo else None, m.mimo_o if m.is_mimo else None]
+
+    def _step_triton_full_fused(self, u: torch.Tensor, state: dict) -> tuple:
+        """in_proj -> fused CUDA step -> out_proj (reference:
+        src/models/inference.py:476-559).  The kernel writes its gated output
+        in the weight dtype, which is what out_proj consumes."""
+        m = self.model
+        zx = m.in_proj(u)
+        _, (dtb, dsk, wb, wc, bb, bc, mx, mo) = self._fused_params()
+        w_dtype = m.out_proj.weight.dtype
+        y_dtype = w_dtype if w_dtype in (torch.float32, torch.bfloat16) else torch.float32
+        y = torch.empty(u.shape[0], m.d_inner, device=u.device, dtype=y_dtype)
+        _launch.full_fused(
+            m.is_mimo, zx, dtb, dsk, wb, wc, bb, bc, mx, mo,
+            state["ssm_state"], state["bx_prev"], state["angle_state"],
+            d_inner=m.d_inner, d_state=m.d_state, ngroups=m.num_bc_heads,
+            mimo_rank=m.mimo_rank, nheads=m.nheads, headdim=m.headdim,
+            split_tensor_size=m.split_tensor_size, num_rope_angles=m.num_rope_angles,
+            A_floor=m.A_floor, y=y)
+        out = m.out_proj(y.to(u.dtype))
+        return out, state
+
+    def _prep_projections(self, u: torch.Tensor, state: dict):
+        """PyTorch split / norm / RoPE of the partially fused backends
+        (reference: src/models/inference.py:305-358), with the angle state
+        accumulated in place."""
+        m = self.model
+        zx = m.in_proj(u)
+        z, x, B_exp, C_exp, ADT, DT, trap, angle_raw = m._compute_params(zx, u.shape[0])
+        state["angle_state"].add_(angle_raw.float().unsqueeze(1) * DT.float().unsqueeze(-1))
+        B_proj, C_proj = m._rope_bc(B_exp, C_exp, state["angle_state"])
+        return z, x, B_proj, C_proj, ADT, DT, trap
+
+    def _step_triton(self, u: torch.Tensor, state: dict) -> tuple:
+        """PyTorch prep -> CUDA SSM kernel -> silu -> out_proj
+        (reference: src/models/inference.py:294-383)."""
+        m = self.model
+        z, x, B_proj, C_proj, ADT, DT, trap = self._prep_projections(u, state)
+        if m.is_mimo:
+            y, _, _ = mamba3_mimo_decode_triton(x, B_proj, C_proj, ADT, DT, trap, m.D,
+                                                m.mimo_x, m.mimo_o, state["ssm_state"],
+                                                state["bx_prev"])
+        else:
+            y, _, _ = mamba3_siso_decode_triton(x, B_proj[:, 0], C_proj[:, 0], ADT, DT, trap, m.D,
+                                                state["ssm_state"], state["bx_prev"])
+        y = (y * F.silu(z.float())).flatten(1)
+        return m.out_proj(y.to(u.dtype)), state
+
+    def _step_triton_fused(self, u: torch.Tensor, state: dict) -> tuple:
+        """PyTorch prep -> CUDA SSM+silu kernel -> out_proj
+        (reference: src/models/inference.py:385-474)."""
+        m = self.model
+        z, x, B_proj, C_proj, ADT, DT, trap = self._prep_projections(u, state)
+        if m.is_mimo:
+            y, _, _ = mamba3_mimo_decode_fused_triton(x, B_proj, C_proj, ADT, DT, trap, m.D,
+                                                      m.mimo_x, m.mimo_o, z.float(),
+                                                      state["ssm_state"], state["bx_prev"])
+        else:
+            y, _, _ = mamba3_siso_decode_fused_triton(x, B_proj[:, 0], C_proj[:, 0], ADT, DT,
+                                                      trap, m.D, z.float(), state["ssm_state"],
+                                                      state["bx_prev"])
+        return m.out_proj(y.flatten(1).to(u.dtype)), state

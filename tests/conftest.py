@@ -50,6 +50,23 @@ def layer_kwargs(kw: dict) -> dict:
     return {k: kw[k] for k in keys if k in kw}
 
 
+def load_params(model, params: dict) -> None:
+    """Load oracle-style numpy parameters into a ``Mamba3`` module."""
+    import torch
+
+    sd = {"in_proj.weight": params["in_proj_weight"], "out_proj.weight": params["out_proj_weight"],
+          "dt_bias": params["dt_bias"], "B_bias": params["B_bias"], "C_bias": params["C_bias"],
+          "B_norm.weight": params["B_norm_weight"], "C_norm.weight": params["C_norm_weight"],
+          "D": params["D"]}
+    for k in ("mimo_x", "mimo_z", "mimo_o"):
+        if k in params:
+            sd[k] = params[k]
+    dtype = model.in_proj.weight.dtype
+    dev = model.in_proj.weight.device
+    model.load_state_dict({k: torch.from_numpy(np.ascontiguousarray(v)).to(dev, dtype)
+                           for k, v in sd.items()})
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

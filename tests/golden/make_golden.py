@@ -198,6 +198,27 @@ def make_stack_case(mods, name, spec, out_dir):
     np.savez_compressed(os.path.join(out_dir, name + ".npz"), meta=json.dumps(meta), out=np.stack(outs))
 
 
+# parameter initialisation under torch.manual_seed(seed) on the CPU
+INIT_CASES = {
+    "init_siso_d256": (dict(d_model=256, d_state=64, headdim=32), 0),
+    "init_mimo_r4_d256": (dict(d_model=256, d_state=64, headdim=32, is_mimo=True, mimo_rank=4), 7),
+}
+
+
+def make_init_case(mods, name, spec, out_dir):
+    torch, Mamba3 = mods[0], mods[1]
+    kw, seed = spec
+    torch.manual_seed(seed)
+    model = Mamba3(**_layer_kwargs(kw))
+    rec = {}
+    for pname, prm in model.state_dict().items():
+        v = _to_np(prm).reshape(-1)
+        rec["sum." + pname] = np.array(v.astype(np.float64).sum())
+        rec["head." + pname] = v[:8].copy()
+    meta = dict(kind="init", layer=kw, seed=seed)
+    np.savez_compressed(os.path.join(out_dir, name + ".npz"), meta=json.dumps(meta), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -212,7 +233,10 @@ def main():
         make_ssm_case(mods, name, spec, args.out)
     for name, spec in STACK_CASES.items():
         make_stack_case(mods, name, spec, args.out)
-    print("wrote", len(LAYER_CASES) + len(SSM_CASES) + len(STACK_CASES), "fixtures to", args.out)
+    for name, spec in INIT_CASES.items():
+        make_init_case(mods, name, spec, args.out)
+    n = len(LAYER_CASES) + len(SSM_CASES) + len(STACK_CASES) + len(INIT_CASES)
+    print("wrote", n, "fixtures to", args.out)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,170 @@
+"""C-ABI checks that need no GPU.
+
+* the library loads and exports every function include/mamba3_b200.h declares;
+* the ctypes structures match the C layout (gcc compiles the header and
+  reports sizeof/offsetof);
+* host-side validation rejects bad calls before touching a device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+import torch
+
+from conftest import ROOT
+from src import _native as nat
+
+HEADER = os.path.join(ROOT, "include", "mamba3_b200.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char \*)\s*(m3_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = nat.load()
+    names = _declared_functions()
+    assert len(names) == 8, names
+    for n in names:
+        assert hasattr(lib, n), f"{n} not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
+    exported = set(re.findall(r"\bT (m3_\w+)", out.stdout))
+    assert set(names) <= exported
+    assert lib.m3_version() == 10000
+    assert nat.status_string(nat.M3_ERR_RANK).startswith("unsupported mimo_rank")
+
+
+_LAYOUT_C = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "mamba3_b200.h"
+#define P(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("m3_dims %zu\nm3_ssm_args %zu\nm3_full_args %zu\n",
+         sizeof(m3_dims), sizeof(m3_ssm_args), sizeof(m3_full_args));
+  P(m3_dims, A_floor) P(m3_ssm_args, z) P(m3_ssm_args, y_dtype) P(m3_ssm_args, B_sd)
+  P(m3_ssm_args, trap_sh) P(m3_ssm_args, mo_sp) P(m3_ssm_args, bx_prev)
+  P(m3_full_args, param_dtype) P(m3_full_args, mimo_o) P(m3_full_args, y_dtype)
+  return 0;
+}
+"""
+
+
+def test_ctypes_layout_matches_c_header():
+    with tempfile.TemporaryDirectory() as d:
+        src, exe = os.path.join(d, "l.c"), os.path.join(d, "l")
+        open(src, "w").write(_LAYOUT_C)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), src, "-o", exe], check=True)
+        lines = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = dict(l.rsplit(" ", 1) for l in lines if l)
+    assert int(got["m3_dims"]) == ctypes.sizeof(nat.Dims)
+    assert int(got["m3_ssm_args"]) == ctypes.sizeof(nat.SsmArgs)
+    assert int(got["m3_full_args"]) == ctypes.sizeof(nat.FullArgs)
+    pairs = {"m3_dims": nat.Dims, "m3_ssm_args": nat.SsmArgs, "m3_full_args": nat.FullArgs}
+    for key, val in got.items():
+        if "." in key:
+            struct, field = key.split(".")
+            assert getattr(pairs[struct], field).offset == int(val), key
+
+
+def _ssm_call(dims, args, mimo=False, fused=False):
+    lib = nat.load()
+    name = f"m3_{'mimo' if mimo else 'siso'}_decode{'_fused' if fused else ''}"
+    return getattr(lib, name)(dims, args, None)
+
+
+def _valid_ssm(mimo=False, fused=False):
+    """Argument blocks with fake but well-aligned device addresses (the
+    library never dereferences them on the host)."""
+    dims = nat.Dims(batch=2, nheads=4, headdim=16, d_state=64, mimo_rank=4 if mimo else 1,
+                    num_rope_angles=0, ngroups=1, d_inner=64, A_floor=0.0)
+    a = nat.SsmArgs()
+    fake = 0x7000_0000_0000
+    for i, f in enumerate(["x", "y", "B_proj", "C_proj", "ADT", "DT", "trap", "D_skip", "h",
+                           "bx_prev", "mimo_x", "mimo_o", "z"]):
+        setattr(a, f, fake + 4096 * i)
+    if not fused:
+        a.z = None
+    return dims, a
+
+
+def test_validation_null_and_shape():
+    lib = nat.load()
+    assert lib.m3_siso_decode(None, None, None) == nat.M3_ERR_NULL
+    dims, a = _valid_ssm()
+    a.h = None
+    assert _ssm_call(dims, a) == nat.M3_ERR_NULL
+    for field, bad in [("d_state", 6), ("d_state", 512), ("headdim", 0), ("nheads", -1)]:
+        dims, a = _valid_ssm()
+        setattr(dims, field, bad)
+        assert _ssm_call(dims, a) == nat.M3_ERR_SHAPE, (field, bad)
+
+
+def test_validation_rank_dtype_alignment():
+    dims, a = _valid_ssm(mimo=True)
+    dims.mimo_rank = 3
+    assert _ssm_call(dims, a, mimo=True) == nat.M3_ERR_RANK
+    dims, a = _valid_ssm()
+    a.x_dtype = 7
+    assert _ssm_call(dims, a) == nat.M3_ERR_DTYPE
+    dims, a = _valid_ssm()
+    a.h = a.h + 4
+    assert _ssm_call(dims, a) == nat.M3_ERR_ALIGN
+    dims, a = _valid_ssm(fused=True)
+    a.z = None
+    assert _ssm_call(dims, a, fused=True) == nat.M3_ERR_NULL
+
+
+def test_validation_full_fused():
+    lib = nat.load()
+    dims = nat.Dims(batch=1, nheads=16, headdim=32, d_state=64, mimo_rank=4, num_rope_angles=16,
+                    ngroups=1, d_inner=512, A_floor=1e-4)
+    a = nat.FullArgs()
+    fake = 0x7000_0000_0000
+    for i, f in enumerate(["zx", "dt_bias", "D", "B_norm_w", "C_norm_w", "B_bias", "C_bias",
+                           "mimo_x", "mimo_o", "ssm_state", "bx_prev", "angle_state", "y"]):
+        setattr(a, f, fake + 4096 * i)
+    a.zx_stride_b = 2 * 512 + 2 * 64 * 4 + 3 * 16 + 16 - 1  # one short of d_in_proj
+    a.y_stride_b = 512
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_SHAPE
+    a.zx_stride_b += 1
+    dims.ngroups = 2
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_SHAPE
+    dims.ngroups = 1
+    dims.num_rope_angles = 33
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_SHAPE
+    dims.num_rope_angles = 16
+    dims.d_inner = 511
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_SHAPE
+    dims.d_inner = 512
+    dims.mimo_rank = 16
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_RANK
+    dims.mimo_rank = 4
+    a.param_dtype = 5
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_ERR_DTYPE
+    a.param_dtype = nat.M3_F32
+    dims.batch = 0  # empty batch: valid, nothing enqueued
+    assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_OK
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_no_device_is_reported():
+    dims, a = _valid_ssm()
+    assert _ssm_call(dims, a) == nat.M3_ERR_DEVICE
+
+
+def test_status_mapping_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        nat.check(nat.M3_ERR_RANK, "x")
+    with pytest.raises(AssertionError):
+        nat.check(nat.M3_ERR_SHAPE, "x")
+    with pytest.raises(RuntimeError):
+        nat.check(nat.M3_ERR_LAUNCH, "x")
+    nat.check(nat.M3_OK, "x")
