@@ -1,0 +1,390 @@
+"""Benchmark of the Mamba-3 single-token decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {native,reference}]
+                    [--workload NAME]
+
+Default workload: one MIMO rank-4 Mamba-3 layer, d_model=256, d_inner=512,
+headdim=32 (16 heads), d_state=64, fp32 weights and state, 128 sequences per
+GPU (the reference's MIMO R4 d256 decode benchmark at its largest batch).
+Weights: torch.manual_seed(0), in_proj / out_proj ~ N(0, 0.02), the other
+parameters per the layer's own init; inputs u ~ N(0, 1) from seed 1;
+synthetic data, zero initial state.
+
+A step is one decode step of the whole batch through the captured CUDA graph
+(in_proj GEMM -> fused decode kernel -> out_proj GEMM).  Between timed steps
+L2 is flushed by writing a 256 MiB buffer; each step is timed with its own
+CUDA event pair on the launching stream (the flush is outside the pair).
+``value`` = tokens / (sum of step times), max over ranks, all ranks' tokens.
+
+``e2e`` times the public API end to end: per step, the pinned host input
+goes in through ``Mamba3Decoder.step`` (which copies it into the graph's
+input buffer), the graph replays, the output is copied back to pinned host
+memory and the stream is synchronised; the event pair brackets all of it,
+after an L2 flush that has completed.
+
+``roofline`` is for the fused decode kernel (the dominant kernel of the
+step): its algorithmic HBM bytes per launch over its mean duration in a K-launch
+event-timed loop with the same L2 flush, against the measured HBM copy
+bandwidth.  ``cpu_baseline`` times the numpy oracle (a restatement of the
+reference's PyTorch decode) on the host cores for a bounded sample.
+
+Multi-GPU (torchrun): every rank decodes its own 128 sequences with a full
+weight replica and its own graph; no collective runs on the decode path
+(NCCL is used for the barrier and the max-over-ranks timing only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "mamba3-fused-triton-kernel_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+# name -> (layer kwargs, batch per GPU, weight dtype)
+WORKLOADS = {
+    "mimo_r4_d256_b128": (dict(d_model=256, d_state=64, headdim=32, is_mimo=True, mimo_rank=4), 128, "f32"),
+    "siso_d256_b1": (dict(d_model=256, d_state=64, headdim=32), 1, "f32"),
+    "siso_d256_b1024": (dict(d_model=256, d_state=64, headdim=32), 1024, "f32"),
+    "siso_d512_b512_bf16": (dict(d_model=512, d_state=128, headdim=64), 512, "bf16"),
+    "mimo_r8_d512_b512_bf16": (dict(d_model=512, d_state=128, headdim=64, is_mimo=True, mimo_rank=8), 512, "bf16"),
+    "mimo_r4_d1024_b4096": (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 4096, "f32"),
+    "mimo_r1_d1024_b4096": (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=1), 4096, "f32"),
+    "mimo_r8_d1024_b4096": (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=8), 4096, "f32"),
+}
+DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
+# Published reference number for the default workload: MIMO d256 B=128
+# full-fused + CUDA graph P50 step latency 0.295 ms on an A100-PCIE-40GB
+# (reference README.md:229) -> 128 / 0.295 ms tokens/s.
+PUBLISHED = {"mimo_r4_d256_b128": 128 / 0.295e-3}
+FLUSH_BYTES = 256 * 1024 * 1024
+HBM_FALLBACK_GBS = 6650.0
+
+
+def fused_bytes_per_launch(m, batch: int, zx_bytes: int, y_bytes: int) -> int:
+    """Algorithmic HBM bytes of one fused decode launch: the in_proj output
+    row (read), ssm_state and bx_prev (read + write), angle_state (read +
+    write), the gated output (write) and the per-head parameters (read once)."""
+    H, P, D, R, A = m.nheads, m.headdim, m.d_state, m.mimo_rank, m.num_rope_angles
+    S = batch * H * (D if m.is_mimo else P * D)
+    params = 4 * (2 * H + 2 * D + 2 * H * R * D + (2 * H * R * P if m.is_mimo else 0))
+    return batch * m.d_in_proj * zx_bytes + 16 * S + 8 * batch * H * A + batch * m.d_inner * y_bytes + params
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def profile_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch recorded by an ncu capture summary under
+    profiles/ (line ``dram_bytes_per_launch: N``), or None."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    mt = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", txt)
+    return int(mt.group(1)) if mt else None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    FIELDS = ("index,timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.proc = None
+        self.gpu_ids = gpu_ids
+        self.marks = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ",".join(map(str, self.gpu_ids)), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def mark(self):
+        self.marks.append(time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                ts = time.mktime(time.strptime(f[1].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                ts += float("0." + f[1].split(".")[1]) if "." in f[1] else 0.0
+                rows.append((ts, int(f[2]), int(f[3]), f[5:9]))
+            except (ValueError, IndexError):
+                continue
+        if not rows:
+            return None
+        window = "timed"
+        sel = [r for r in rows if len(self.marks) >= 2 and self.marks[0] <= r[0] <= self.marks[-1]]
+        if not sel:
+            sel, window = rows, "whole run (timed region shorter than the sampling interval)"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in sel for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": int(np.median([r[1] for r in sel])), "sm_max_mhz": max(r[2] for r in sel),
+                "reasons": reasons, "samples": len(sel), "window": window}
+
+
+def cpu_oracle_rate(kw, batch, dtype_name, steps=None, budget_s=10.0, warmup=1):
+    """Time the numpy oracle decode step on the host cores; returns
+    (tokens/s, steps timed, cores used)."""
+    from oracle import mamba3_oracle as orc
+    dims = orc.layer_dims(**kw)
+    bf16 = dtype_name == "bf16"
+    params = orc.synthetic_params(dims, 0, bf16=bf16, randomize_small=False)
+    st = orc.init_state(dims, batch)
+    us = orc.synthetic_inputs(dims, batch, 16, 1, bf16=bf16)  # cycled, like the GPU side
+    for i in range(warmup):
+        _, st = orc.decode_step(us[i % 16], params, dims, st, bf16=bf16)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _, st = orc.decode_step(us[n % 16], params, dims, st, bf16=bf16)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and (el >= budget_s or n >= 10000)):
+            break
+    return batch * n / el, n, os.cpu_count() or 1
+
+
+def config_dict(workload, kw, batch, world, dtype_name):
+    published = PUBLISHED.get(workload)
+    return {"workload": workload, "batch_per_gpu": batch, "global_batch": batch * world,
+            **kw, "weights": dtype_name, "state": "f32",
+            "parallelism": f"batch-sharded x{world}, no collective on the decode path",
+            "l2": "flushed (256 MiB write) before every timed step; per-step CUDA events",
+            "step": "CUDA-graph replay of in_proj GEMM + fused decode kernel + out_proj GEMM",
+            "baseline": ("A100 full-fused+graph P50 0.295 ms at B=128 (reference README.md:229)"
+                         if published else None)}
+
+
+def run_reference(args, kw, batch, dtype_name, rank):
+    """--impl reference: the oracle port of the reference's CPU decode."""
+    if rank != 0:
+        return
+    cpu_oracle_rate(kw, batch, dtype_name, steps=max(args.warmup, 1), warmup=0)  # warm-up
+    rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=args.steps, warmup=0)
+    ms = 1000.0 * batch / rate
+    line = {
+        "metric": "decode tokens/s", "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_dict(args.workload, kw, batch, 1, dtype_name),
+        "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} oracle decode steps of {batch} sequences (numpy, host cores)"},
+        "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of oracle CPU timing")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    kw, batch, dtype_name = WORKLOADS[args.workload]
+
+    if args.impl == "reference":
+        run_reference(args, kw, batch, dtype_name, rank)
+        return
+
+    import datetime
+
+    import torch.distributed as dist
+
+    from src.kernels import _launch
+    from src.models.inference import Mamba3Decoder
+    from src.models.mamba3 import Mamba3
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+
+    torch.manual_seed(0)
+    model = Mamba3(**kw, device=dev, dtype=wdtype)
+    with torch.no_grad():
+        model.in_proj.weight.normal_(0.0, 0.02)
+        model.out_proj.weight.normal_(0.0, 0.02)
+    gen = torch.Generator(device="cpu").manual_seed(1 + rank)
+    K, W = args.steps, args.warmup
+    n_inputs = 64
+    u_host = torch.randn(n_inputs, batch, model.d_model, generator=gen).to(wdtype).pin_memory()
+    u_dev = u_host.to(dev)
+
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    state = dec.init_state(batch, device=dev)
+    dec.warmup_cuda_graph(state, n_warmup=3)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed_loop(fn, n, pre_sync=False):
+        """n iterations of fn, each bracketed by its own event pair after an
+        L2 flush; returns per-iteration milliseconds."""
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            if pre_sync:
+                stream.synchronize()
+            else:
+                torch.cuda._sleep(20000)  # keep the GPU busy while the host enqueues the step
+            ev[i][0].record(stream)
+            fn(i)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        return np.array([a.elapsed_time(b) for a, b in ev])
+
+    # ---- warm-up (graph replays) ----
+    with torch.no_grad():
+        for i in range(W):
+            dec.step(u_dev[i % n_inputs], state)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    try:
+        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
+    except ValueError:
+        gpus = list(range(world))
+    sampler = ClockSampler(gpus) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.2)
+
+    # ---- timed region: K decode steps ----
+    barrier()
+    if sampler:
+        sampler.mark()
+    with torch.no_grad():
+        step_ms = timed_loop(lambda i: dec.step(u_dev[i % n_inputs], state), K)
+    barrier()
+    if sampler:
+        sampler.mark()
+    total_ms = max_over_ranks(float(step_ms.sum()))
+    p50 = max_over_ranks(float(np.percentile(step_ms, 50)))
+    p99 = max_over_ranks(float(np.percentile(step_ms, 99)))
+    value = world * batch * K / (total_ms / 1000.0)
+    gpu_launches = K  # one fused decode kernel per step (the two GEMMs are cuBLAS)
+
+    # ---- fused kernel alone (roofline) and the two GEMMs, same flush ----
+    zx = model.in_proj(u_dev[0])
+    y = torch.empty(batch, model.d_inner, device=dev, dtype=wdtype)
+    launch = dec._fused_launch(state)
+    with torch.no_grad():
+        k_ms = timed_loop(lambda i: launch.run(zx, y), K)
+        gi_ms = timed_loop(lambda i: model.in_proj(u_dev[i % n_inputs]), min(K, 500))
+        go_ms = timed_loop(lambda i: model.out_proj(y), min(K, 500))
+    k_mean = max_over_ranks(float(k_ms.mean()))
+    nbytes = fused_bytes_per_launch(model, batch, 2 if wdtype == torch.bfloat16 else 4,
+                                    2 if wdtype == torch.bfloat16 else 4)
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes / (k_mean * 1e-3) / 1e9
+
+    # ---- end to end through the public API (pinned host in/out) ----
+    out_host = torch.empty(batch, model.d_model, dtype=wdtype).pin_memory()
+
+    def e2e_step(i):
+        out, _ = dec.step(u_host[i % n_inputs], state)
+        out_host.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    barrier()
+    with torch.no_grad():
+        e2e_ms = timed_loop(e2e_step, K, pre_sync=True)
+    barrier()
+    e2e_total = max_over_ranks(float(e2e_ms.sum()))
+    e2e_value = world * batch * K / (e2e_total / 1000.0)
+    clocks = sampler.stop() if sampler else None
+
+    cpu = None
+    if rank == 0 and world == 1:
+        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
+        cpu = {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} oracle decode steps of {batch} sequences (numpy float32 restatement "
+                         f"of the reference PyTorch decode; BLAS threads = host cores)"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        published = PUBLISHED.get(args.workload)
+        line = {
+            "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
+            "p50_step_ms": round(p50, 5), "p99_step_ms": round(p99, 5),
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(value / (world * published), 3) if published else None,
+            "dtype": dtype_name, "data": "synthetic",
+            "config": config_dict(args.workload, kw, batch, world, dtype_name),
+            "roofline": {"bound": "hbm", "kernel": "fused decode (m3_mimo_full_fused / m3_siso_full_fused)",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
+                         "mean_launch_ms": round(k_mean, 5),
+                         "traffic": profile_traffic("fused_decode", args.workload)},
+            "kernels_ms": {"in_proj_gemm": round(float(gi_ms.mean()), 5),
+                           "fused_decode": round(k_mean, 5),
+                           "out_proj_gemm": round(float(go_ms.mean()), 5)},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": batch * model.d_model * u_host.element_size(),
+                    "d2h_bytes_per_step": batch * model.d_model * out_host.element_size(),
+                    "ms_per_step": round(e2e_total / K, 5)},
+            "gpu_launches": gpu_launches,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    dec._cuda_graph = None
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -135,6 +135,20 @@ int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
  * lifts the reference's R == 4 restriction (fused_full_decode.py:600). */
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream);
 
+/* Device-side error word of the library's kernels: 0, or a bit mask of
+ * M3_DEVERR_* raised by a kernel that gave up a bounded wait (the kernel
+ * then skipped its remaining work and returned).  Synchronises the device.
+ * `reset` != 0 clears the word.  Returns -1 if it cannot be read.
+ * Diagnostics only; no counterpart in the reference. */
+enum { M3_DEVERR_TIMEOUT = 1 };
+int m3_device_error(int reset);
+
+/* Self test of the bounded waits: launches one CTA that waits on a barrier
+ * nothing completes, with a short bound, and returns.  Afterwards
+ * m3_device_error reports M3_DEVERR_TIMEOUT.  Diagnostics only; no
+ * counterpart in the reference. */
+int m3_selftest_wait_timeout(m3_stream_t stream);
+
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int m3_version(void);
 

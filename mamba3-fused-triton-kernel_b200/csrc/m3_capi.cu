@@ -11,7 +11,7 @@ namespace {
 
 using m3::KParams;
 
-constexpr int kVersion = 10000;  // 1.0.0
+constexpr int kVersion = 10100;  // 1.1.0
 constexpr int kMaxHeaddim = 4096;
 
 bool dtype_ok(int32_t dt) { return dt == M3_F32 || dt == M3_BF16; }
@@ -140,6 +140,19 @@ int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
 
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {
   return full_entry(dims, args, stream, true);
+}
+
+int m3_device_error(int reset) {
+  const int a = m3::siso_device_error(reset != 0);
+  const int b = m3::mimo_device_error(reset != 0);
+  if (a < 0 || b < 0) return -1;
+  return a | b;
+}
+
+int m3_selftest_wait_timeout(m3_stream_t stream) {
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  return launch_status(m3::launch_wait_timeout_probe(reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int m3_version(void) { return kVersion; }

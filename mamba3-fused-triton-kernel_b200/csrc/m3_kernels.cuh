@@ -4,15 +4,12 @@
 // (reads the raw in_proj output) and the state-update-only variant (reads
 // precomputed B/C/dt/trap, as the reference's SSM kernels do):
 //
-//   siso_decode_kernel  one CTA per (batch, head).  The (P, D) state tile of
-//                       ssm_state and bx_prev is contiguous in HBM and is
-//                       streamed once in and once out with 128-bit accesses.
-//                       A group of S lanes owns one state row (S = D/4
-//                       float4 columns, capped at 32); the readout C.h is a
-//                       shuffle reduction inside that group.  The first
-//                       rows' state loads are issued before the per-head
-//                       prologue (RMSNorm, bias, RoPE, scalars) so their
-//                       latency overlaps it.
+//   siso_stream_kernel  (m3_siso.cu) persistent CTAs stream the contiguous
+//                       (P, D) state tiles of ssm_state and bx_prev through
+//                       a ring of shared-memory stages filled by 1-D bulk
+//                       copies; a group of S lanes owns one state row
+//                       (S = D/4 float4 columns, capped at 32) and reduces
+//                       C.h with shuffles.
 //   mimo_decode_kernel  one CTA per (batch, group of heads), one warp per
 //                       head.  The (D,) state of a head is spread over the
 //                       warp's lanes (2 or 4 floats per lane, so every RoPE
@@ -165,175 +162,8 @@ struct SisoShape {
   static constexpr int S = BG < 32 ? BG : 32;     // lanes per row
   static constexpr int FPL = BG / S;              // float4 per lane per row
   static constexpr int RPW = 32 / S;              // rows per warp per pass
-  static constexpr int RPT = 4 / FPL;             // rows per thread per iteration
   static constexpr int KPL = BD >= 32 ? BD / 32 : 1;  // prologue elements per lane
 };
-
-template <int BD, bool FULL>
-__global__ void __launch_bounds__(512) siso_decode_kernel(const KParams p) {
-  using Sh = SisoShape<BD>;
-  constexpr int S = Sh::S, FPL = Sh::FPL, RPW = Sh::RPW, RPT = Sh::RPT, KPL = Sh::KPL;
-
-  extern __shared__ __align__(16) float smem[];
-  float *sB = smem;           // [BD]  B after norm/bias/RoPE (or B_proj)
-  float *sC = smem + BD;      // [BD]
-  float *sX = smem + 2 * BD;  // [P]   x
-  float *sG = sX + p.P;       // [P]   silu(z)
-
-  const int bh = blockIdx.x;
-  const int b = bh / p.H;
-  const int hh = bh - b * p.H;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
-  const int P = p.P, D = p.D, G = D >> 2;
-  const int nslots = (nthr >> 5) * RPW;
-  const int slot = warp * RPW + lane / S;
-  const int j = lane % S;
-  const int rows_per_iter = nslots * RPT;
-  const int64_t tile = (int64_t)bh * P * D;
-  float *hs = p.h + tile;
-  float *bs = p.bx + tile;
-
-  float4 hv[RPT][FPL], bv[RPT][FPL];
-  auto load_rows = [&](int base) {
-#pragma unroll
-    for (int u = 0; u < RPT; ++u) {
-      const int row = base + u * nslots + slot;
-#pragma unroll
-      for (int f = 0; f < FPL; ++f) {
-        const int col = j + S * f;
-        if (row < P && col < G) {
-          const int64_t o = ((int64_t)row * G + col) * 4;
-          hv[u][f] = ld_state4(hs + o);
-          bv[u][f] = ld_state4(bs + o);
-        } else {
-          hv[u][f] = make_float4(0.f, 0.f, 0.f, 0.f);
-          bv[u][f] = hv[u][f];
-        }
-      }
-    }
-  };
-  load_rows(0);  // in flight while the prologue runs
-
-  Coef c;
-  float dskip;
-  bool gate;
-  if constexpr (FULL) {
-    const int64_t zr = (int64_t)b * p.zx_sb;
-    head_scalars_from_zx(p, zr, hh, c, dskip);
-    gate = true;
-    if (warp == 0) {
-      // B and C rows of rank 0 (src/models/mamba3.py:202-215), RoPE on the
-      // first 2A entries (utils.py:31-44); angle_state += angle_raw * DT
-      // (mamba3.py:326-327) is written back by this warp only.
-      const int colB = 2 * p.d_inner, colC = 2 * p.d_inner + p.d_bc;
-      const int acol = 2 * p.d_inner + 2 * p.d_bc + 3 * p.H;
-      float vb[KPL], vc[KPL];
-      float ssb = 0.f, ssc = 0.f;
-#pragma unroll
-      for (int k = 0; k < KPL; ++k) {
-        const int d = lane + 32 * k;
-        vb[k] = d < D ? ld_any(p.zx, zr + colB + d, p.zx_dt) : 0.f;
-        vc[k] = d < D ? ld_any(p.zx, zr + colC + d, p.zx_dt) : 0.f;
-        ssb += vb[k] * vb[k];
-        ssc += vc[k] * vc[k];
-      }
-      ssb = group_sum<32>(ssb);
-      ssc = group_sum<32>(ssc);
-      const float rmsb = sqrtf(ssb / (float)D + kRmsEps);
-      const float rmsc = sqrtf(ssc / (float)D + kRmsEps);
-#pragma unroll
-      for (int k = 0; k < KPL; ++k) {
-        const int d = lane + 32 * k;
-        if (d < D) {
-          const int64_t bi = (int64_t)hh * D + d;  // (H, R=1, D)
-          vb[k] = vb[k] / rmsb * ld_any(p.wB, d, p.par_dt) + ld_any(p.bB, bi, p.par_dt);
-          vc[k] = vc[k] / rmsc * ld_any(p.wC, d, p.par_dt) + ld_any(p.bC, bi, p.par_dt);
-        }
-        const bool rot = d < 2 * p.A;
-        float sn = 0.f, cs = 1.f, ang = 0.f;
-        if (rot) {
-          const int i = d >> 1;
-          ang = p.ang[(int64_t)bh * p.A + i] + ld_any(p.zx, zr + acol + i, p.zx_dt) * c.DT;
-          sincosf(ang, &sn, &cs);
-        }
-        const float ob = __shfl_xor_sync(kFullMask, vb[k], 1);
-        const float oc = __shfl_xor_sync(kFullMask, vc[k], 1);
-        if (rot) {
-          if (d & 1) {
-            vb[k] = ob * sn + vb[k] * cs;
-            vc[k] = oc * sn + vc[k] * cs;
-          } else {
-            vb[k] = vb[k] * cs - ob * sn;
-            vc[k] = vc[k] * cs - oc * sn;
-            p.ang[(int64_t)bh * p.A + (d >> 1)] = ang;
-          }
-        }
-        if (d < D) {
-          sB[d] = vb[k];
-          sC[d] = vc[k];
-        }
-      }
-    }
-    for (int t = tid; t < P; t += nthr) {
-      sX[t] = ld_any(p.zx, zr + p.d_inner + (int64_t)hh * P + t, p.zx_dt);
-      sG[t] = silu_f(ld_any(p.zx, zr + (int64_t)hh * P + t, p.zx_dt));
-    }
-  } else {
-    head_scalars_given(p, b, hh, c, dskip);
-    gate = p.z != nullptr;
-    for (int t = tid; t < D; t += nthr) {
-      sB[t] = p.Bp[(int64_t)b * p.B_sb + (int64_t)hh * p.B_sh + (int64_t)t * p.B_sd];
-      sC[t] = p.Cp[(int64_t)b * p.C_sb + (int64_t)hh * p.C_sh + (int64_t)t * p.C_sd];
-    }
-    for (int t = tid; t < P; t += nthr) {
-      sX[t] = ld_any(p.x, (int64_t)b * p.x_sb + (int64_t)hh * p.x_sh + (int64_t)t * p.x_sp, p.x_dt);
-      if (gate)
-        sG[t] = silu_f(ld_any(p.z, (int64_t)b * p.z_sb + (int64_t)hh * p.z_sh + (int64_t)t * p.z_sp,
-                              p.z_dt));
-    }
-  }
-  __syncthreads();
-
-  const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * p.y_sh;
-  for (int base = 0; base < P; base += rows_per_iter) {
-    if (base != 0) load_rows(base);
-#pragma unroll
-    for (int u = 0; u < RPT; ++u) {
-      const int row = base + u * nslots + slot;
-      const bool rok = row < P;
-      const float xp = rok ? sX[row] : 0.f;
-      float part = 0.f;
-#pragma unroll
-      for (int f = 0; f < FPL; ++f) {
-        const int col = j + S * f;
-        if (rok && col < G) {
-          const float4 Bq = reinterpret_cast<const float4 *>(sB)[col];
-          const float4 Cq = reinterpret_cast<const float4 *>(sC)[col];
-          const float4 ho = hv[u][f], bo = bv[u][f];
-          float4 bn, hn;
-          bn.x = xp * Bq.x; bn.y = xp * Bq.y; bn.z = xp * Bq.z; bn.w = xp * Bq.w;
-          hn.x = trap_update(c, bn.x, bo.x, ho.x);
-          hn.y = trap_update(c, bn.y, bo.y, ho.y);
-          hn.z = trap_update(c, bn.z, bo.z, ho.z);
-          hn.w = trap_update(c, bn.w, bo.w, ho.w);
-          part += Cq.x * hn.x;
-          part += Cq.y * hn.y;
-          part += Cq.z * hn.z;
-          part += Cq.w * hn.w;
-          const int64_t o = ((int64_t)row * G + col) * 4;
-          st_state4(hs + o, hn);
-          st_state4(bs + o, bn);
-        }
-      }
-      part = group_sum<S>(part);
-      if (j == 0 && rok) {
-        float yv = part + dskip * xp;
-        if (gate) yv = yv * sG[row];
-        st_any(p.y, ybase + (int64_t)row * p.y_sp, yv, p.y_dt);
-      }
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------
 // MIMO: state (B, H, D); one CTA per (b, group of heads), one warp per head
@@ -593,9 +423,13 @@ __global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
 // Launchers (defined in m3_siso.cu / m3_mimo.cu); return the launch status.
 cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
+cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 
-// Thread-block shape chosen by the launchers (exposed for the host checks).
-int siso_block_threads(int D, int P);
+// Device error words of the kernel translation units (read, optionally clear).
+int siso_device_error(bool reset);
+int mimo_device_error(bool reset);
+
+// Heads handled by one CTA of the MIMO kernels.
 int mimo_heads_per_cta(int H);
 
 }  // namespace m3

@@ -1,48 +1,503 @@
-// Launchers of the SISO decode kernels (see m3_kernels.cuh).
+// SISO decode: persistent streaming kernel over (batch, head) tiles.
+//
+// The SISO state of one (b, h) is a contiguous (P, D) fp32 tile in both
+// ssm_state and bx_prev.  Each CTA walks its tiles in row-chunks of RT rows;
+// a ring of NSTAGE shared-memory stages is kept full by 1-D bulk (TMA)
+// copies, so up to NSTAGE chunks per CTA are in flight without holding
+// registers.  Consumers read a chunk from shared memory, apply the
+// exponential-trapezoidal update, write h and bx straight back to global
+// memory with 128-bit stores and reduce C.h per row inside a lane group.
+// Per-tile parameters (RMSNorm + bias + RoPE of B/C, scalars, x, silu(z))
+// are computed while the following chunks are still landing.
+//
+// Reference arithmetic: src/kernels/fused_full_decode.py:37-225 (full step)
+// and src/kernels/siso_decode.py:21-132 (state update only), in the
+// operation order of src/kernels/utils.py:73-102.
+#include "m3_async.cuh"
 #include "m3_kernels.cuh"
 
 namespace m3 {
 
 namespace {
 
+constexpr int kSisoThreads = 256;
+constexpr int kChunkFloats = 4096;  // state floats per tensor per stage (16 KB)
+constexpr int kMaxSmem = 200 * 1024;
+
+struct StreamPlan {
+  int rt;           // rows per chunk
+  int nchunk;       // chunks per (b, h) tile
+  int nstage;       // ring depth
+  int stage_bytes;  // bytes per stage
+  int par_off;      // byte offset of the per-CTA parameter block
+  int ring_off;     // byte offset of the ring
+  // byte offsets inside a stage: state chunk, then (staged path) the tile header
+  int o_h, o_bx, o_raw, o_x, o_z, o_scal, o_ang, o_bb, o_bc;
+};
+
+// Scalars of the current tile, kept in shared memory.
+enum { kDecay = 0, kDT, kOmt, kHtr, kDskip, kGate, kNScalar = 8 };
+
+// Shared-memory parameter block: tile parameters, then (full step) the
+// norm weights, dt_bias and D of every head, loaded once per CTA.
+struct ParBlock {
+  float *sB, *sC, *sX, *sG, *sS, *wB, *wC, *dtb, *dsk;
+};
+
 template <int BD>
-int siso_warps(int P) {
-  using Sh = SisoShape<BD>;
-  const int rows_per_warp = Sh::RPW * Sh::RPT;  // rows one warp covers per iteration
-  int w = (P + rows_per_warp - 1) / rows_per_warp;
-  return w < 2 ? 2 : (w > 16 ? 16 : w);
+__device__ ParBlock par_block(unsigned char *base, const KParams &p) {
+  ParBlock q;
+  q.sB = reinterpret_cast<float *>(base);
+  q.sC = q.sB + BD;
+  q.sX = q.sC + BD;
+  q.sG = q.sX + p.P;
+  q.sS = q.sG + p.P;
+  q.wB = q.sS + kNScalar;
+  q.wC = q.wB + BD;
+  q.dtb = q.wC + BD;
+  q.dsk = q.dtb + p.H;
+  return q;
 }
 
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// RMSNorm + weight + bias + RoPE of the rank-0 B and C rows of one tile,
+// into q.sB / q.sC, by one warp.  raw(d) / bias(d) fetch the inputs;
+// ang_old(i) / ang_raw(i) the angle state and increment of pair i; the
+// accumulated angle is written back to angle_state (src/models/mamba3.py:
+// 202-215, 326-333; src/kernels/utils.py:31-44).
+template <int BD, typename RawB, typename RawC, typename BiasB, typename BiasC, typename AngOld, typename AngRaw>
+__device__ __forceinline__ void bc_rows(const KParams &p, const ParBlock &q, int t, float DT, RawB rawB, RawC rawC,
+                                        BiasB biasB, BiasC biasC, AngOld ang_old, AngRaw ang_raw) {
+  constexpr int KPL = SisoShape<BD>::KPL;
+  const int lane = threadIdx.x & 31, D = p.D;
+  float vb[KPL], vc[KPL];
+  float ssb = 0.f, ssc = 0.f;
+#pragma unroll
+  for (int k = 0; k < KPL; ++k) {
+    const int d = lane + 32 * k;
+    vb[k] = d < D ? rawB(d) : 0.f;
+    vc[k] = d < D ? rawC(d) : 0.f;
+    ssb += vb[k] * vb[k];
+    ssc += vc[k] * vc[k];
+  }
+  ssb = group_sum<32>(ssb);
+  ssc = group_sum<32>(ssc);
+  const float rmsb = sqrtf(ssb / (float)D + kRmsEps);
+  const float rmsc = sqrtf(ssc / (float)D + kRmsEps);
+#pragma unroll
+  for (int k = 0; k < KPL; ++k) {
+    const int d = lane + 32 * k;
+    if (d < D) {
+      vb[k] = vb[k] / rmsb * q.wB[d] + biasB(d);
+      vc[k] = vc[k] / rmsc * q.wC[d] + biasC(d);
+    }
+    const bool rot = d < 2 * p.A;
+    float sn = 0.f, cs = 1.f, ang = 0.f;
+    if (rot) {
+      ang = ang_old(d >> 1) + ang_raw(d >> 1) * DT;
+      sincosf(ang, &sn, &cs);
+    }
+    const float ob = __shfl_xor_sync(kFullMask, vb[k], 1);
+    const float oc = __shfl_xor_sync(kFullMask, vc[k], 1);
+    if (rot) {
+      if (d & 1) {
+        vb[k] = ob * sn + vb[k] * cs;
+        vc[k] = oc * sn + vc[k] * cs;
+      } else {
+        vb[k] = vb[k] * cs - ob * sn;
+        vc[k] = vc[k] * cs - oc * sn;
+        p.ang[(int64_t)t * p.A + (d >> 1)] = ang;
+      }
+    }
+    if (d < D) {
+      q.sB[d] = vb[k];
+      q.sC[d] = vc[k];
+    }
+  }
+}
+
+// Scalars of head hh from dd_dt / dd_A / trap_raw (src/models/mamba3.py:196-199).
+__device__ __forceinline__ void scalars_to_smem(const KParams &p, const ParBlock &q, int hh, float dd_dt,
+                                                float dd_A, float tr_raw) {
+  const float sp = softplus_f(dd_A);
+  const float A = -(sp > -p.A_floor ? -p.A_floor : sp);  // clamp keeps NaN like torch
+  const float DT = softplus_f(dd_dt + q.dtb[hh]);
+  const float tr = sigmoid_f(tr_raw);
+  q.sS[kDecay] = expf(A * DT);
+  q.sS[kDT] = DT;
+  q.sS[kOmt] = 1.f - tr;
+  q.sS[kHtr] = tr * 0.5f;
+  q.sS[kDskip] = q.dsk[hh];
+  q.sS[kGate] = 1.f;
+}
+
+// Tile parameters of the full step from the header staged with chunk 0.
+template <int BD, typename T>
+__device__ void tile_params_staged(const KParams &p, const ParBlock &q, const StreamPlan &sp,
+                                   const unsigned char *stage, int hh, int t) {
+  const int tid = threadIdx.x, warp = tid >> 5, nthr = blockDim.x;
+  const int H = p.H, D = p.D, P = p.P;
+  const T *raw = reinterpret_cast<const T *>(stage + sp.o_raw);   // [B row | C row]
+  const T *xs = reinterpret_cast<const T *>(stage + sp.o_x);
+  const T *zs = reinterpret_cast<const T *>(stage + sp.o_z);
+  const T *scal = reinterpret_cast<const T *>(stage + sp.o_scal);  // dd_dt[H] dd_A[H] trap[H] angle[A]
+  const float *ang = reinterpret_cast<const float *>(stage + sp.o_ang);
+  const unsigned char *bb = stage + sp.o_bb, *bc = stage + sp.o_bc;
+  if (warp == 0) {
+    const float dd_dt = to_f(scal[hh]);
+    const float DT = softplus_f(dd_dt + q.dtb[hh]);
+    if ((tid & 31) == 0) scalars_to_smem(p, q, hh, dd_dt, to_f(scal[H + hh]), to_f(scal[2 * H + hh]));
+    bc_rows<BD>(
+        p, q, t, DT, [&](int d) { return to_f(raw[d]); }, [&](int d) { return to_f(raw[D + d]); },
+        [&](int d) { return ld_any(bb, d, p.par_dt); }, [&](int d) { return ld_any(bc, d, p.par_dt); },
+        [&](int i) { return ang[i]; }, [&](int i) { return to_f(scal[3 * H + i]); });
+  }
+  for (int i = tid; i < P; i += nthr) {
+    q.sX[i] = to_f(xs[i]);
+    q.sG[i] = silu_f(to_f(zs[i]));
+  }
+}
+
+// Tile parameters read straight from global memory (full step on shapes
+// the staged path cannot copy, and the state-update-only entry points).
 template <int BD, bool FULL>
+__device__ void tile_params_global(const KParams &p, const ParBlock &q, int b, int hh, int t) {
+  const int tid = threadIdx.x, warp = tid >> 5, nthr = blockDim.x;
+  const int P = p.P, D = p.D;
+  if constexpr (FULL) {
+    const int64_t zr = (int64_t)b * p.zx_sb;
+    const int so = 2 * p.d_inner + 2 * p.d_bc;
+    if (warp == 0) {
+      const float dd_dt = ld_any(p.zx, zr + so + hh, p.zx_dt);
+      const float DT = softplus_f(dd_dt + q.dtb[hh]);
+      if ((tid & 31) == 0)
+        scalars_to_smem(p, q, hh, dd_dt, ld_any(p.zx, zr + so + p.H + hh, p.zx_dt),
+                        ld_any(p.zx, zr + so + 2 * p.H + hh, p.zx_dt));
+      const int64_t colB = zr + 2 * p.d_inner, colC = zr + 2 * p.d_inner + p.d_bc;
+      const int64_t acol = zr + so + 3 * p.H;
+      bc_rows<BD>(
+          p, q, t, DT, [&](int d) { return ld_any(p.zx, colB + d, p.zx_dt); },
+          [&](int d) { return ld_any(p.zx, colC + d, p.zx_dt); },
+          [&](int d) { return ld_any(p.bB, (int64_t)hh * D + d, p.par_dt); },
+          [&](int d) { return ld_any(p.bC, (int64_t)hh * D + d, p.par_dt); },
+          [&](int i) { return p.ang[(int64_t)t * p.A + i]; },
+          [&](int i) { return ld_any(p.zx, acol + i, p.zx_dt); });
+    }
+    for (int i = tid; i < P; i += nthr) {
+      q.sX[i] = ld_any(p.zx, zr + p.d_inner + (int64_t)hh * P + i, p.zx_dt);
+      q.sG[i] = silu_f(ld_any(p.zx, zr + (int64_t)hh * P + i, p.zx_dt));
+    }
+  } else {
+    if (tid == 0) {
+      Coef c;
+      float dskip;
+      head_scalars_given(p, b, hh, c, dskip);
+      q.sS[kDecay] = c.decay; q.sS[kDT] = c.DT; q.sS[kOmt] = c.omt; q.sS[kHtr] = c.htr;
+      q.sS[kDskip] = dskip; q.sS[kGate] = p.z != nullptr ? 1.f : 0.f;
+    }
+    for (int i = tid; i < D; i += nthr) {
+      q.sB[i] = p.Bp[(int64_t)b * p.B_sb + (int64_t)hh * p.B_sh + (int64_t)i * p.B_sd];
+      q.sC[i] = p.Cp[(int64_t)b * p.C_sb + (int64_t)hh * p.C_sh + (int64_t)i * p.C_sd];
+    }
+    for (int i = tid; i < P; i += nthr) {
+      q.sX[i] = ld_any(p.x, (int64_t)b * p.x_sb + (int64_t)hh * p.x_sh + (int64_t)i * p.x_sp, p.x_dt);
+      if (p.z != nullptr)
+        q.sG[i] = silu_f(ld_any(p.z, (int64_t)b * p.z_sb + (int64_t)hh * p.z_sh + (int64_t)i * p.z_sp, p.z_dt));
+    }
+  }
+}
+
+__device__ __forceinline__ void st_global4(float *p, float4 v) {
+  asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// FULL: full step (else state-update only).  STAGED: the tile header comes
+// with chunk 0 through the ring (T = element type of the in_proj output).
+template <int BD, bool FULL, bool STAGED, typename T>
+__global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams p, const StreamPlan sp) {
+  using Sh = SisoShape<BD>;
+  constexpr int S = Sh::S, FPL = Sh::FPL, RPW = Sh::RPW;
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
+  const ParBlock q = par_block<BD>(smem_raw + sp.par_off, p);
+  unsigned char *ring = smem_raw + sp.ring_off;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int P = p.P, D = p.D, G = D >> 2;
+  const int ntiles = p.B * p.H;
+  const int nslots = (blockDim.x >> 5) * RPW;
+  const int slot = warp * RPW + lane / S;
+  const int j = lane % S;
+
+  // k-th chunk of this CTA: tile blockIdx.x + (k / nchunk) * gridDim.x, chunk k % nchunk
+  auto tile_of = [&](int k) { return (int)blockIdx.x + (k / sp.nchunk) * (int)gridDim.x; };
+
+  if (tid == 0) {
+    for (int s = 0; s < sp.nstage; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  auto issue = [&](int k) {
+    const int t = tile_of(k);
+    if (t >= ntiles) return;
+    const int c = k % sp.nchunk;
+    const int r0 = c * sp.rt;
+    const int nr = min(sp.rt, P - r0);
+    const int s = k % sp.nstage;
+    const uint32_t bytes = (uint32_t)nr * (uint32_t)D * 4u;
+    const uint32_t bar = smem_addr(&bars[s]);
+    const size_t goff = ((size_t)t * P + r0) * D;
+    unsigned char *st = ring + (size_t)s * sp.stage_bytes;
+    uint32_t tx = 2 * bytes;
+    if constexpr (STAGED) {
+      if (c == 0) {
+        const int b = t / p.H, hh = t - b * p.H, H = p.H;
+        const T *row = static_cast<const T *>(p.zx) + (int64_t)b * p.zx_sb;
+        const uint32_t es = sizeof(T), pes = p.par_dt == M3_BF16 ? 2 : 4;
+        const uint32_t n_raw = 2u * D * es, n_xz = (uint32_t)P * es, n_scal = (uint32_t)(3 * H + p.A) * es;
+        const uint32_t n_ang = (uint32_t)p.A * 4, n_bias = (uint32_t)D * pes;
+        tx += n_raw + 2 * n_xz + n_scal + n_ang + 2 * n_bias;
+        mbar_arrive_expect_tx(bar, tx);
+        bulk_g2s(smem_addr(st + sp.o_raw), row + 2 * p.d_inner, n_raw, bar);
+        bulk_g2s(smem_addr(st + sp.o_x), row + p.d_inner + (int64_t)hh * P, n_xz, bar);
+        bulk_g2s(smem_addr(st + sp.o_z), row + (int64_t)hh * P, n_xz, bar);
+        bulk_g2s(smem_addr(st + sp.o_scal), row + 2 * p.d_inner + 2 * p.d_bc, n_scal, bar);
+        bulk_g2s(smem_addr(st + sp.o_ang), p.ang + (int64_t)t * p.A, n_ang, bar);
+        bulk_g2s(smem_addr(st + sp.o_bb), static_cast<const unsigned char *>(p.bB) + (size_t)hh * n_bias, n_bias, bar);
+        bulk_g2s(smem_addr(st + sp.o_bc), static_cast<const unsigned char *>(p.bC) + (size_t)hh * n_bias, n_bias, bar);
+      } else {
+        mbar_arrive_expect_tx(bar, tx);
+      }
+    } else {
+      mbar_arrive_expect_tx(bar, tx);
+    }
+    bulk_g2s(smem_addr(st + sp.o_h), p.h + goff, bytes, bar);
+    bulk_g2s(smem_addr(st + sp.o_bx), p.bx + goff, bytes, bar);
+  };
+  if (tid == 0)
+    for (int k = 0; k < sp.nstage; ++k) issue(k);
+
+  if constexpr (FULL) {  // per-CTA constants: norm weights, dt_bias, D
+    for (int i = tid; i < D; i += blockDim.x) {
+      q.wB[i] = ld_any(p.wB, i, p.par_dt);
+      q.wC[i] = ld_any(p.wC, i, p.par_dt);
+    }
+    for (int i = tid; i < p.H; i += blockDim.x) {
+      q.dtb[i] = ld_any(p.dt_bias, i, p.par_dt);
+      q.dsk[i] = ld_any(p.Dp, i, p.par_dt);
+    }
+    __syncthreads();
+  }
+
+  int k = 0;
+  for (;; ++k) {
+    const int t = tile_of(k);
+    if (t >= ntiles) break;
+    const int c = k % sp.nchunk;
+    const int b = t / p.H, hh = t - b * p.H;
+    const int s = k % sp.nstage;
+    const unsigned char *st = ring + (size_t)s * sp.stage_bytes;
+    if constexpr (STAGED) {
+      const bool ok = mbar_wait(smem_addr(&bars[s]), (uint32_t)((k / sp.nstage) & 1));
+      if (__syncthreads_or(!ok)) break;  // a lost copy: stop and drain
+      if (c == 0) {
+        tile_params_staged<BD, T>(p, q, sp, st, hh, t);
+        __syncthreads();
+      }
+    } else {
+      if (c == 0) {
+        tile_params_global<BD, FULL>(p, q, b, hh, t);
+        __syncthreads();
+      }
+      const bool ok = mbar_wait(smem_addr(&bars[s]), (uint32_t)((k / sp.nstage) & 1));
+      if (__syncthreads_or(!ok)) break;
+    }
+
+    const float *sh = reinterpret_cast<const float *>(st + sp.o_h);
+    const float *sbx = reinterpret_cast<const float *>(st + sp.o_bx);
+    const int r0 = c * sp.rt;
+    const int nr = min(sp.rt, P - r0);
+    const Coef cf = {q.sS[kDecay], q.sS[kDT], q.sS[kOmt], q.sS[kHtr]};
+    const float dskip = q.sS[kDskip];
+    const bool gate = q.sS[kGate] != 0.f;
+    float *hg = p.h + ((size_t)t * P + r0) * D;
+    float *bg = p.bx + ((size_t)t * P + r0) * D;
+    const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * p.y_sh;
+    for (int rb = 0; rb < nr; rb += nslots) {
+      const int row = rb + slot;
+      const bool rok = row < nr;
+      const float xp = rok ? q.sX[r0 + row] : 0.f;
+      float part = 0.f;
+#pragma unroll
+      for (int f = 0; f < FPL; ++f) {
+        const int col = j + S * f;
+        if (rok && col < G) {
+          const int o = row * G + col;
+          const float4 ho = reinterpret_cast<const float4 *>(sh)[o];
+          const float4 bo = reinterpret_cast<const float4 *>(sbx)[o];
+          const float4 Bq = reinterpret_cast<const float4 *>(q.sB)[col];
+          const float4 Cq = reinterpret_cast<const float4 *>(q.sC)[col];
+          float4 bn, hn;
+          bn.x = xp * Bq.x; bn.y = xp * Bq.y; bn.z = xp * Bq.z; bn.w = xp * Bq.w;
+          hn.x = trap_update(cf, bn.x, bo.x, ho.x);
+          hn.y = trap_update(cf, bn.y, bo.y, ho.y);
+          hn.z = trap_update(cf, bn.z, bo.z, ho.z);
+          hn.w = trap_update(cf, bn.w, bo.w, ho.w);
+          part += Cq.x * hn.x;
+          part += Cq.y * hn.y;
+          part += Cq.z * hn.z;
+          part += Cq.w * hn.w;
+          st_global4(hg + (size_t)o * 4, hn);
+          st_global4(bg + (size_t)o * 4, bn);
+        }
+      }
+      part = group_sum<S>(part);
+      if (j == 0 && rok) {
+        float yv = part + dskip * xp;
+        if (gate) yv = yv * q.sG[r0 + row];
+        st_any(p.y, ybase + (int64_t)(r0 + row) * p.y_sp, yv, p.y_dt);
+      }
+    }
+    __syncthreads();  // stage s and the tile parameters are free again
+    if (tid == 0) issue(k + sp.nstage);
+  }
+  // Normal exit: every issued chunk was consumed.  After a lost copy, wait
+  // (bounded) for whatever this CTA still has in flight before leaving.
+  if (tid == 0) {
+    for (int q2 = k; q2 < k + sp.nstage; ++q2)
+      if (tile_of(q2) < ntiles)
+        mbar_wait(smem_addr(&bars[q2 % sp.nstage]), (uint32_t)((q2 / sp.nstage) & 1), 1 << 16);
+  }
+}
+
+int align128(int x) { return (x + 127) / 128 * 128; }
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether every header copy of the staged path starts on a 16-byte boundary
+// and moves a multiple of 16 bytes.
+bool staged_eligible(const KParams &kp) {
+  const int es = kp.zx_dt == M3_BF16 ? 2 : 4, pes = kp.par_dt == M3_BF16 ? 2 : 4;
+  if (!aligned16(kp.zx) || !aligned16(kp.ang) || !aligned16(kp.bB) || !aligned16(kp.bC)) return false;
+  if ((kp.zx_sb * es) % 16 || (kp.d_inner * es) % 16 || (2 * kp.D * es) % 16) return false;
+  if ((kp.P * es) % 16 || ((3 * kp.H + kp.A) * es) % 16 || (kp.A % 4) || (kp.D * pes) % 16) return false;
+  return true;
+}
+
+StreamPlan make_plan(const KParams &kp, int BD, bool staged, int nstage, int *smem_bytes) {
+  const int D = kp.D, P = kp.P;
+  StreamPlan sp;
+  sp.rt = kChunkFloats / D;
+  if (sp.rt < 1) sp.rt = 1;
+  if (sp.rt > P) sp.rt = P;
+  sp.nchunk = (P + sp.rt - 1) / sp.rt;
+  sp.nstage = nstage;
+  int o = 0;
+  sp.o_h = o; o += align128(sp.rt * D * 4);
+  sp.o_bx = o; o += align128(sp.rt * D * 4);
+  sp.o_raw = sp.o_x = sp.o_z = sp.o_scal = sp.o_ang = sp.o_bb = sp.o_bc = 0;
+  if (staged) {
+    const int es = kp.zx_dt == M3_BF16 ? 2 : 4, pes = kp.par_dt == M3_BF16 ? 2 : 4;
+    sp.o_raw = o; o += align128(2 * D * es);
+    sp.o_x = o; o += align128(P * es);
+    sp.o_z = o; o += align128(P * es);
+    sp.o_scal = o; o += align128((3 * kp.H + kp.A) * es);
+    sp.o_ang = o; o += align128(kp.A * 4);
+    sp.o_bb = o; o += align128(D * pes);
+    sp.o_bc = o; o += align128(D * pes);
+  }
+  sp.stage_bytes = o;
+  sp.par_off = 128;  // after the barriers
+  const int par_floats = 2 * BD + 2 * P + kNScalar + 2 * BD + 2 * kp.H;
+  sp.ring_off = sp.par_off + align128(par_floats * 4);
+  *smem_bytes = sp.ring_off + sp.nstage * sp.stage_bytes;
+  return sp;
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int BD, bool FULL, bool STAGED, typename T>
 cudaError_t launch_t(const KParams &kp, cudaStream_t stream) {
-  const int threads = siso_warps<BD>(kp.P) * 32;
-  const size_t smem = (size_t)(2 * BD + 2 * kp.P) * sizeof(float);
-  const unsigned grid = (unsigned)((int64_t)kp.B * kp.H);
-  siso_decode_kernel<BD, FULL><<<grid, threads, smem, stream>>>(kp);
+  int smem = 0;
+  StreamPlan sp = make_plan(kp, BD, STAGED, 3, &smem);
+  if (smem > kMaxSmem) sp = make_plan(kp, BD, STAGED, 2, &smem);
+  if (smem > kMaxSmem) return cudaErrorInvalidValue;
+  auto kern = siso_stream_kernel<BD, FULL, STAGED, T>;
+  // Once per kernel: opt in to the largest ring any call may need.  Then
+  // CTAs per SM for this ring size (cached for the last size seen).
+  static bool attr = false;
+  static int last_smem = -1, last_per_sm = 1;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  if (smem != last_smem) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSisoThreads, smem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    last_smem = smem;
+    last_per_sm = per_sm;
+  }
+  const int ntiles = kp.B * kp.H;
+  int grid = num_sms() * last_per_sm;
+  if (grid > ntiles) grid = ntiles;
+  kern<<<grid, kSisoThreads, smem, stream>>>(kp, sp);
   return cudaGetLastError();
 }
 
-template <bool FULL>
-cudaError_t launch_bd(const KParams &kp, cudaStream_t stream) {
-  if (kp.D <= 16) return launch_t<16, FULL>(kp, stream);
-  if (kp.D <= 32) return launch_t<32, FULL>(kp, stream);
-  if (kp.D <= 64) return launch_t<64, FULL>(kp, stream);
-  if (kp.D <= 128) return launch_t<128, FULL>(kp, stream);
-  return launch_t<256, FULL>(kp, stream);
+template <int BD>
+cudaError_t launch_mode(const KParams &kp, bool full, cudaStream_t stream) {
+  if (!full) return launch_t<BD, false, false, float>(kp, stream);
+  if (staged_eligible(kp))
+    return kp.zx_dt == M3_BF16 ? launch_t<BD, true, true, __nv_bfloat16>(kp, stream)
+                               : launch_t<BD, true, true, float>(kp, stream);
+  return launch_t<BD, true, false, float>(kp, stream);
+}
+
+// Waits on an mbarrier that nothing completes, with a short bound: the
+// bounded-wait self test (the error word must read M3_DEVERR_TIMEOUT after).
+__global__ void wait_timeout_probe_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar), 1);
+    mbar_init_fence();
+    mbar_wait(smem_addr(&bar), 0, 1000);
+  }
 }
 
 }  // namespace
 
-int siso_block_threads(int D, int P) {
-  if (D <= 16) return siso_warps<16>(P) * 32;
-  if (D <= 32) return siso_warps<32>(P) * 32;
-  if (D <= 64) return siso_warps<64>(P) * 32;
-  if (D <= 128) return siso_warps<128>(P) * 32;
-  return siso_warps<256>(P) * 32;
+cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream) {
+  if (kp.D <= 16) return launch_mode<16>(kp, full, stream);
+  if (kp.D <= 32) return launch_mode<32>(kp, full, stream);
+  if (kp.D <= 64) return launch_mode<64>(kp, full, stream);
+  if (kp.D <= 128) return launch_mode<128>(kp, full, stream);
+  return launch_mode<256>(kp, full, stream);
 }
 
-cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream) {
-  return full ? launch_bd<true>(kp, stream) : launch_bd<false>(kp, stream);
+int siso_device_error(bool reset) { return device_error_of_this_unit(reset); }
+
+cudaError_t launch_wait_timeout_probe(cudaStream_t stream) {
+  wait_timeout_probe_kernel<<<1, 32, 0, stream>>>();
+  return cudaGetLastError();
 }
 
 }  // namespace m3

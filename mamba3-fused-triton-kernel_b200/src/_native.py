@@ -89,12 +89,25 @@ def load(path: str = LIB_PATH):
             fn = getattr(lib, name)
             fn.argtypes = [POINTER(Dims), POINTER(argt), c_void_p]
             fn.restype = c_int
+        lib.m3_device_error.argtypes = [c_int]
+        lib.m3_device_error.restype = c_int
+        lib.m3_selftest_wait_timeout.argtypes = [c_void_p]
+        lib.m3_selftest_wait_timeout.restype = c_int
         lib.m3_version.argtypes = []
         lib.m3_version.restype = c_int
         lib.m3_status_string.argtypes = [c_int]
         lib.m3_status_string.restype = ctypes.c_char_p
         _lib = lib
     return _lib
+
+
+M3_DEVERR_TIMEOUT = 1
+
+
+def device_error(reset: bool = False) -> int:
+    """Device error word of the library's kernels (synchronises the device):
+    0, or M3_DEVERR_* bits of kernels that gave up a bounded wait."""
+    return load().m3_device_error(1 if reset else 0)
 
 
 def status_string(status: int) -> str:

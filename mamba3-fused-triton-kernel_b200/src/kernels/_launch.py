@@ -121,25 +121,43 @@ def _param_set(tensors):
     return code, out
 
 
-def full_fused(mimo: bool, zx, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bias,
-               mimo_x, mimo_o, h, bx_prev, angle_state, *, d_inner, d_state, ngroups,
-               mimo_rank, nheads, headdim, split_tensor_size, num_rope_angles, A_floor,
-               y: torch.Tensor | None = None) -> torch.Tensor:
-    """One full decode step between in_proj and out_proj.
+class FullFusedLaunch:
+    """A full-fused launch whose arguments are marshalled once.
 
-    Updates ``h``, ``bx_prev`` and ``angle_state`` in place.  Writes the
-    gated output into ``y`` ((B, H*P) rows, f32 or bf16) when given, else
-    into a new (B, H, P) float32 tensor, and returns it.
+    ``run(zx, y)`` re-points the in_proj output and the output buffer (both
+    may change between steps) and enqueues the kernel on the current stream
+    of the state's device: one ctypes call, no re-validation of the
+    unchanged state and parameters.  The caller keeps every tensor passed to
+    ``prepare_full_fused`` alive while the object is used.
     """
-    Bsz = zx.shape[0]
+
+    __slots__ = ("dims", "args", "fn", "device", "keep", "zx_dtype", "y_dtype", "batch", "d_in_proj", "d_inner")
+
+    def __init__(self, dims, args, fn, device, keep, batch, d_in_proj, d_inner):
+        self.dims, self.args, self.fn, self.device, self.keep = dims, args, fn, device, keep
+        self.batch, self.d_in_proj, self.d_inner = batch, d_in_proj, d_inner
+
+    def run(self, zx: torch.Tensor, y: torch.Tensor) -> None:
+        assert zx.shape == (self.batch, self.d_in_proj) and zx.stride(1) == 1 and zx.device == self.device
+        assert y.shape == (self.batch, self.d_inner) and y.stride(1) == 1 and y.device == self.device
+        a = self.args
+        a.zx = zx.data_ptr(); a.zx_stride_b = zx.stride(0); a.zx_dtype = nat.dtype_code(zx)
+        a.y = y.data_ptr(); a.y_stride_b = y.stride(0); a.y_dtype = nat.dtype_code(y)
+        with nat.device_guard(self.device):
+            st = self.fn(self.dims, a, nat.stream_handle(self.device))
+        nat.check(st, self.fn.__name__)
+
+
+def prepare_full_fused(mimo: bool, batch: int, device, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias,
+                       C_bias, mimo_x, mimo_o, h, bx_prev, angle_state, *, d_inner, d_state, ngroups,
+                       mimo_rank, nheads, headdim, split_tensor_size, num_rope_angles,
+                       A_floor) -> FullFusedLaunch:
+    """Validate the state and parameters once and return a reusable launch."""
+    Bsz = batch
     H, P, D = nheads, headdim, d_state
     R = mimo_rank if mimo else 1
-    if y is None:
-        y = torch.empty(Bsz, H, P, device=zx.device, dtype=torch.float32)
-    if Bsz == 0:
-        return y
     dev = h.device
-    assert zx.is_cuda and h.is_cuda
+    assert h.is_cuda
     check_state("ssm_state", h)
     check_state("bx_prev", bx_prev)
     check_state("angle_state", angle_state)
@@ -148,10 +166,7 @@ def full_fused(mimo: bool, zx, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bi
     if mimo and R not in nat.SUPPORTED_RANKS:
         raise ValueError(f"Unsupported mimo_rank={R}. Supported values: {list(nat.SUPPORTED_RANKS)}")
     d_in_proj = 2 * d_inner + 2 * D * ngroups * R + 3 * H + num_rope_angles
-    assert zx.dim() == 2 and zx.shape[1] == d_in_proj, \
-        f"zxBCdtAtrap must be (B, {d_in_proj}); got {tuple(zx.shape)}"
-    _same_device(dev, zx, bx_prev, angle_state, y)
-
+    _same_device(dev, bx_prev, angle_state)
     shapes = [("dt_bias", dt_bias, (H,)), ("D", D_skip, (H,)), ("B_norm_weight", B_norm_w, (D,)),
               ("C_norm_weight", C_norm_w, (D,)),
               ("B_bias", B_bias, (H, R, D) if mimo else (H, D)),
@@ -163,32 +178,55 @@ def full_fused(mimo: bool, zx, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bi
         _same_device(dev, t)
     assert tuple(angle_state.shape) == (Bsz, H, num_rope_angles)
     assert tuple(h.shape) == tuple(bx_prev.shape) == ((Bsz, H, D) if mimo else (Bsz, H, P, D))
-
-    zz = _io(zx)
-    if zz.stride(1) != 1:
-        zz = zz.contiguous()
-    code, (dtb, dsk, wb, wc, bb, bc, mx, mo) = _param_set(
-        [dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bias,
-         mimo_x if mimo else None, mimo_o if mimo else None])
-    y2 = y.view(Bsz, -1) if y.dim() == 3 else y
-    assert y2.shape[0] == Bsz and y2.shape[1] == d_inner and y2.stride(1) == 1
-
+    code, keep = _param_set([dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bias,
+                             mimo_x if mimo else None, mimo_o if mimo else None])
+    dtb, dsk, wb, wc, bb, bc, mx, mo = keep
     dims = nat.Dims(batch=Bsz, nheads=H, headdim=P, d_state=D, mimo_rank=R,
                     num_rope_angles=num_rope_angles, ngroups=ngroups, d_inner=d_inner,
                     A_floor=float(A_floor))
     a = nat.FullArgs()
-    a.zx = zz.data_ptr(); a.zx_stride_b = zz.stride(0); a.zx_dtype = nat.dtype_code(zz)
     a.param_dtype = code
     a.dt_bias, a.D, a.B_norm_w, a.C_norm_w = dtb.data_ptr(), dsk.data_ptr(), wb.data_ptr(), wc.data_ptr()
     a.B_bias, a.C_bias = bb.data_ptr(), bc.data_ptr()
     if mimo:
         a.mimo_x, a.mimo_o = mx.data_ptr(), mo.data_ptr()
     a.ssm_state, a.bx_prev, a.angle_state = h.data_ptr(), bx_prev.data_ptr(), angle_state.data_ptr()
-    a.y = y2.data_ptr(); a.y_stride_b = y2.stride(0); a.y_dtype = nat.dtype_code(y2)
-
     lib = nat.load()
     fn = lib.m3_mimo_full_fused if mimo else lib.m3_siso_full_fused
-    with nat.device_guard(dev):
-        st = fn(dims, a, nat.stream_handle(dev))
-    nat.check(st, fn.__name__)
+    return FullFusedLaunch(dims, a, fn, dev, keep + [h, bx_prev, angle_state], Bsz, d_in_proj, d_inner)
+
+
+def full_fused(mimo: bool, zx, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bias,
+               mimo_x, mimo_o, h, bx_prev, angle_state, *, d_inner, d_state, ngroups,
+               mimo_rank, nheads, headdim, split_tensor_size, num_rope_angles, A_floor,
+               y: torch.Tensor | None = None) -> torch.Tensor:
+    """One full decode step between in_proj and out_proj.
+
+    Updates ``h``, ``bx_prev`` and ``angle_state`` in place.  Writes the
+    gated output into ``y`` ((B, H*P) rows, f32 or bf16) when given, else
+    into a new (B, H, P) float32 tensor, and returns it.
+    """
+    Bsz = zx.shape[0]
+    H, P = nheads, headdim
+    if y is None:
+        y = torch.empty(Bsz, H, P, device=zx.device, dtype=torch.float32)
+    if Bsz == 0:
+        return y
+    assert zx.is_cuda and h.is_cuda
+    if mimo and mimo_rank not in nat.SUPPORTED_RANKS:
+        raise ValueError(f"Unsupported mimo_rank={mimo_rank}. "
+                         f"Supported values: {list(nat.SUPPORTED_RANKS)}")
+    launch = prepare_full_fused(
+        mimo, Bsz, h.device, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias, C_bias, mimo_x, mimo_o,
+        h, bx_prev, angle_state, d_inner=d_inner, d_state=d_state, ngroups=ngroups,
+        mimo_rank=mimo_rank, nheads=nheads, headdim=headdim, split_tensor_size=split_tensor_size,
+        num_rope_angles=num_rope_angles, A_floor=A_floor)
+    assert zx.dim() == 2 and zx.shape[1] == launch.d_in_proj, \
+        f"zxBCdtAtrap must be (B, {launch.d_in_proj}); got {tuple(zx.shape)}"
+    _same_device(h.device, zx, y)
+    zz = _io(zx)
+    if zz.stride(1) != 1:
+        zz = zz.contiguous()
+    y2 = y.view(Bsz, -1) if y.dim() == 3 else y
+    launch.run(zz, y2)
     return y

@@ -165,25 +165,34 @@ class Mamba3Decoder:
         state["angle_state"], state["ssm_state"], state["bx_prev"] = a, h, bx
         return out, state
 
-    def _fused_params(self):
-        """Per-head parameters as the fused kernel reads them (one dtype,
-        contiguous); parameters that already qualify are used as they are."""
-        m = self.model
-        key = tuple(None if p is None else (p.data_ptr(), p._version, p.dtype)
-                    for p in self._param_list())
-        if self._fused_cache is not None and self._fused_cache[0] == key:
-            return self._fused_cache[1]
-        code, tensors = _launch._param_set(self._param_list())
-        if not m.is_mimo:
-            tensors[4] = tensors[4][:, 0, :]
-            tensors[5] = tensors[5][:, 0, :]
-        self._fused_cache = (key, (code, tensors))
-        return code, tensors
-
     def _param_list(self):
         m = self.model
         return [m.dt_bias, m.D, m.B_norm.weight, m.C_norm.weight, m.B_bias, m.C_bias,
                 m.mimo_x if m.is_mimo else None, m.mimo_o if m.is_mimo else None]
+
+    def _fused_launch(self, state: dict):
+        """Prepared fused launch for this state and the current parameters.
+
+        Rebuilt when a parameter is replaced or modified in place (its
+        ``_version`` changes) or another state is passed; otherwise reused,
+        so an eager step costs one ctypes call for the kernel."""
+        m = self.model
+        params = self._param_list()
+        key = (tuple(None if p is None else (p.data_ptr(), p._version, p.dtype) for p in params),
+               tuple((t.data_ptr(), tuple(t.shape)) for t in
+                     (state["ssm_state"], state["bx_prev"], state["angle_state"])))
+        if self._fused_cache is not None and self._fused_cache[0] == key:
+            return self._fused_cache[1]
+        if not m.is_mimo:  # (H, 1, D) -> (H, D)
+            params[4], params[5] = params[4][:, 0, :], params[5][:, 0, :]
+        h = state["ssm_state"]
+        launch = _launch.prepare_full_fused(
+            m.is_mimo, h.shape[0], h.device, *params, h, state["bx_prev"], state["angle_state"],
+            d_inner=m.d_inner, d_state=m.d_state, ngroups=m.num_bc_heads, mimo_rank=m.mimo_rank,
+            nheads=m.nheads, headdim=m.headdim, split_tensor_size=m.split_tensor_size,
+            num_rope_angles=m.num_rope_angles, A_floor=m.A_floor)
+        self._fused_cache = (key, launch)
+        return launch
 
     def _step_triton_full_fused(self, u: torch.Tensor, state: dict) -> tuple:
         """in_proj -> fused CUDA step -> out_proj (reference:
@@ -191,17 +200,12 @@ class Mamba3Decoder:
         in the weight dtype, which is what out_proj consumes."""
         m = self.model
         zx = m.in_proj(u)
-        _, (dtb, dsk, wb, wc, bb, bc, mx, mo) = self._fused_params()
+        if zx.dtype not in (torch.float32, torch.bfloat16) or zx.stride(1) != 1:
+            zx = zx.float().contiguous()
         w_dtype = m.out_proj.weight.dtype
         y_dtype = w_dtype if w_dtype in (torch.float32, torch.bfloat16) else torch.float32
         y = torch.empty(u.shape[0], m.d_inner, device=u.device, dtype=y_dtype)
-        _launch.full_fused(
-            m.is_mimo, zx, dtb, dsk, wb, wc, bb, bc, mx, mo,
-            state["ssm_state"], state["bx_prev"], state["angle_state"],
-            d_inner=m.d_inner, d_state=m.d_state, ngroups=m.num_bc_heads,
-            mimo_rank=m.mimo_rank, nheads=m.nheads, headdim=m.headdim,
-            split_tensor_size=m.split_tensor_size, num_rope_angles=m.num_rope_angles,
-            A_floor=m.A_floor, y=y)
+        self._fused_launch(state).run(zx, y)
         out = m.out_proj(y.to(u.dtype))
         return out, state
 

@@ -42,7 +42,7 @@ def round_bf16(a) -> np.ndarray:
     bits = a.view(np.uint32).astype(np.uint64)
     rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16) << 16
     out = (rounded & 0xFFFFFFFF).astype(np.uint32).view(F32)
-    return np.where(np.isnan(a), a, out).astype(F32)
+    return np.where(np.isnan(a), a, out).astype(F32, copy=False)
 
 
 # ---------------------------------------------------------------------------
@@ -85,27 +85,27 @@ def softplus(x):
     x = np.asarray(x, dtype=F32)
     safe = np.minimum(x, F32(SOFTPLUS_THRESHOLD))
     with np.errstate(over="ignore"):
-        sp = np.log1p(np.exp(safe)).astype(F32)
-    return np.where(x > F32(SOFTPLUS_THRESHOLD), x, sp).astype(F32)
+        sp = np.log1p(np.exp(safe)).astype(F32, copy=False)
+    return np.where(x > F32(SOFTPLUS_THRESHOLD), x, sp).astype(F32, copy=False)
 
 
 def sigmoid(x):
     x = np.asarray(x, dtype=F32)
     with np.errstate(over="ignore"):
-        return (F32(1.0) / (F32(1.0) + np.exp(-x))).astype(F32)
+        return (F32(1.0) / (F32(1.0) + np.exp(-x))).astype(F32, copy=False)
 
 
 def silu(x):
     x = np.asarray(x, dtype=F32)
-    return (x * sigmoid(x)).astype(F32)
+    return (x * sigmoid(x)).astype(F32, copy=False)
 
 
 def rms_norm(x, weight, eps: float = RMS_EPS):
     """src/models/mamba3.py:34-36: x / sqrt(mean(x^2) + eps) * weight."""
     x = np.asarray(x, dtype=F32)
     ms = np.mean(x * x, axis=-1, keepdims=True, dtype=F32)
-    rms = np.sqrt(ms + F32(eps)).astype(F32)
-    return (x / rms * np.asarray(weight, dtype=F32)).astype(F32)
+    rms = np.sqrt(ms + F32(eps)).astype(F32, copy=False)
+    return (x / rms * np.asarray(weight, dtype=F32)).astype(F32, copy=False)
 
 
 def apply_rope(x, angles):
@@ -113,11 +113,11 @@ def apply_rope(x, angles):
     by angles[..., i]."""
     x = np.asarray(x, dtype=F32)
     angles = np.asarray(angles, dtype=F32)
-    c = np.cos(angles).astype(F32)
-    s = np.sin(angles).astype(F32)
+    c = np.cos(angles).astype(F32, copy=False)
+    s = np.sin(angles).astype(F32, copy=False)
     x1 = x[..., 0::2]
     x2 = x[..., 1::2]
-    out = np.empty_like(x)
+    out = np.empty(np.broadcast_shapes(x.shape, x.shape[:-1] + (2 * c.shape[-1],)), dtype=F32)
     out[..., 0::2] = x1 * c - x2 * s
     out[..., 1::2] = x1 * s + x2 * c
     return out
@@ -129,7 +129,7 @@ def trapezoidal_blend(bx_curr, bx_prev, trap):
     bx_prev = np.asarray(bx_prev, dtype=F32)
     trap = np.asarray(trap, dtype=F32)
     return ((F32(1.0) - trap) * bx_curr
-            + trap * F32(0.5) * (bx_curr + bx_prev)).astype(F32)
+            + trap * F32(0.5) * (bx_curr + bx_prev)).astype(F32, copy=False)
 
 
 # ---------------------------------------------------------------------------
@@ -147,11 +147,11 @@ def siso_decode(x, B_proj, C_proj, ADT, DT, trap, D_skip, h, bx_prev):
     decay = np.exp(np.asarray(ADT, F32))[..., None, None]
     dt_e = np.asarray(DT, F32)[..., None, None]
     tr_e = np.asarray(trap, F32)[..., None, None]
-    bx_curr = (x[..., :, None] * np.asarray(B_proj, F32)[..., None, :]).astype(F32)
+    bx_curr = (x[..., :, None] * np.asarray(B_proj, F32)[..., None, :]).astype(F32, copy=False)
     blended = trapezoidal_blend(bx_curr, bx_prev, tr_e)
-    h_new = (decay * np.asarray(h, F32) + dt_e * blended).astype(F32)
-    y = np.einsum("bhd,bhpd->bhp", np.asarray(C_proj, F32), h_new).astype(F32)
-    y = (y + np.asarray(D_skip, F32)[None, :, None] * x).astype(F32)
+    h_new = (decay * np.asarray(h, F32) + dt_e * blended).astype(F32, copy=False)
+    y = np.einsum("bhd,bhpd->bhp", np.asarray(C_proj, F32), h_new).astype(F32, copy=False)
+    y = (y + np.asarray(D_skip, F32)[None, :, None] * x).astype(F32, copy=False)
     return y, h_new, bx_curr
 
 
@@ -163,16 +163,16 @@ def mimo_decode(x, B_proj, C_proj, ADT, DT, trap, D_skip, mimo_x, mimo_o,
     mimo_x, mimo_o (H,R,P); h, bx_prev (B,H,D).
     """
     x = np.asarray(x, dtype=F32)
-    x_r = np.einsum("bhp,hrp->bhr", x, np.asarray(mimo_x, F32)).astype(F32)
-    bx_curr = np.einsum("bhr,brhd->bhd", x_r, np.asarray(B_proj, F32)).astype(F32)
+    x_r = np.einsum("bhp,hrp->bhr", x, np.asarray(mimo_x, F32)).astype(F32, copy=False)
+    bx_curr = np.einsum("bhr,brhd->bhd", x_r, np.asarray(B_proj, F32)).astype(F32, copy=False)
     tr_e = np.asarray(trap, F32)[..., None]
     blended = trapezoidal_blend(bx_curr, bx_prev, tr_e)
     h_new = (np.exp(np.asarray(ADT, F32))[..., None] * np.asarray(h, F32)
-             + np.asarray(DT, F32)[..., None] * blended).astype(F32)
-    y_r = np.einsum("brhd,bhd->brh", np.asarray(C_proj, F32), h_new).astype(F32)
-    skip = (np.asarray(D_skip, F32)[None, None, :] * x_r.transpose(0, 2, 1)).astype(F32)
-    y = np.einsum("brh,hrp->bhp", (y_r + skip).astype(F32),
-                  np.asarray(mimo_o, F32)).astype(F32)
+             + np.asarray(DT, F32)[..., None] * blended).astype(F32, copy=False)
+    y_r = np.einsum("brhd,bhd->brh", np.asarray(C_proj, F32), h_new).astype(F32, copy=False)
+    skip = (np.asarray(D_skip, F32)[None, None, :] * x_r.transpose(0, 2, 1)).astype(F32, copy=False)
+    y = np.einsum("brh,hrp->bhp", (y_r + skip).astype(F32, copy=False),
+                  np.asarray(mimo_o, F32)).astype(F32, copy=False)
     return y, h_new, bx_curr
 
 
@@ -209,7 +209,7 @@ def compute_params(zx, params: dict, dims: dict):
     # A = -(softplus(dd_A).clamp(max=-A_floor)); clamp(max=m) == min(., m)
     A = -np.minimum(softplus(dd_A), -A_floor)
     DT = softplus(dd_dt + np.asarray(params["dt_bias"], F32))
-    ADT = (A * DT).astype(F32)
+    ADT = (A * DT).astype(F32, copy=False)
     trap = sigmoid(trap_raw)
     B_n = rms_norm(B_raw, params["B_norm_weight"])      # (B,R,G,D)
     C_n = rms_norm(C_raw, params["C_norm_weight"])
@@ -218,8 +218,8 @@ def compute_params(zx, params: dict, dims: dict):
     B_exp = np.broadcast_to(B_n, (B_n.shape[0], B_n.shape[1], H, B_n.shape[3]))
     C_exp = np.broadcast_to(C_n, (C_n.shape[0], C_n.shape[1], H, C_n.shape[3]))
     # rearrange(B_bias, "h r d -> r h d")
-    B_exp = (B_exp + np.transpose(np.asarray(params["B_bias"], F32), (1, 0, 2))).astype(F32)
-    C_exp = (C_exp + np.transpose(np.asarray(params["C_bias"], F32), (1, 0, 2))).astype(F32)
+    B_exp = np.ascontiguousarray(B_exp + np.transpose(np.asarray(params["B_bias"], F32), (1, 0, 2)), F32)
+    C_exp = np.ascontiguousarray(C_exp + np.transpose(np.asarray(params["C_bias"], F32), (1, 0, 2)), F32)
     return z, x, B_exp, C_exp, ADT, DT, trap, angle_raw
 
 
@@ -233,9 +233,9 @@ def ssm_from_zx(zx, params: dict, dims: dict, angle_state, ssm_state, bx_prev):
     z, x, B_exp, C_exp, ADT, DT, trap, angle_raw = compute_params(zx, params, dims)
     split = dims["split"]
     R = dims["mimo_rank"]
-    delta = (np.asarray(angle_raw, F32)[:, None, :] * DT[:, :, None]).astype(F32)
-    angle_state = (np.asarray(angle_state, F32) + delta).astype(F32)
-    ang = np.broadcast_to(angle_state[:, None], (angle_state.shape[0], R) + angle_state.shape[1:])
+    delta = (np.asarray(angle_raw, F32)[:, None, :] * DT[:, :, None]).astype(F32, copy=False)
+    angle_state = (np.asarray(angle_state, F32) + delta).astype(F32, copy=False)
+    ang = angle_state[:, None]  # (B, 1, H, A): broadcasts over the R ranks
     B_proj = np.concatenate([apply_rope(B_exp[..., :split], ang), B_exp[..., split:]], axis=-1)
     C_proj = np.concatenate([apply_rope(C_exp[..., :split], ang), C_exp[..., split:]], axis=-1)
     if dims["is_mimo"]:
@@ -245,7 +245,7 @@ def ssm_from_zx(zx, params: dict, dims: dict, angle_state, ssm_state, bx_prev):
     else:
         y, h_new, bx_new = siso_decode(x, B_proj[:, 0], C_proj[:, 0], ADT, DT, trap,
                                        params["D"], ssm_state, bx_prev)
-    y = (y * silu(z)).astype(F32)
+    y = (y * silu(z)).astype(F32, copy=False)
     return y, angle_state, h_new, bx_new
 
 
@@ -261,7 +261,7 @@ def decode_step(u, params: dict, dims: dict, state: dict, bf16: bool = False):
     u = np.asarray(u, dtype=F32)
     W_in = np.asarray(params["in_proj_weight"], F32)
     W_out = np.asarray(params["out_proj_weight"], F32)
-    zx = (u @ W_in.T).astype(F32)
+    zx = (u @ W_in.T).astype(F32, copy=False)
     if bf16:
         zx = round_bf16(zx)
     y, a, h, bx = ssm_from_zx(zx, params, dims, state["angle_state"],
@@ -269,7 +269,7 @@ def decode_step(u, params: dict, dims: dict, state: dict, bf16: bool = False):
     y = y.reshape(y.shape[0], -1)
     if bf16:
         y = round_bf16(y)
-    out = (y @ W_out.T).astype(F32)
+    out = (y @ W_out.T).astype(F32, copy=False)
     if bf16:
         out = round_bf16(out)
     return out, {"angle_state": a, "ssm_state": h, "bx_prev": bx}
@@ -292,7 +292,7 @@ def residual_block_step(x, norm_weight, params, dims, state, bf16=False):
     if bf16:
         xn = round_bf16(xn)
     out, st = decode_step(xn, params, dims, state, bf16=bf16)
-    res = (x + out).astype(F32)
+    res = (x + out).astype(F32, copy=False)
     if bf16:
         res = round_bf16(res)
     return res, st
@@ -356,7 +356,7 @@ def synthetic_inputs(dims: dict, batch: int, steps: int, seed: int,
                      bf16: bool = False) -> np.ndarray:
     """Token embeddings u_t ~ N(0, 1), shape (steps, batch, d_model)."""
     rng = np.random.default_rng(seed)
-    u = rng.standard_normal((steps, batch, dims["d_model"])).astype(F32)
+    u = rng.standard_normal((steps, batch, dims["d_model"])).astype(F32, copy=False)
     return round_bf16(u) if bf16 else u
 
 
@@ -367,13 +367,13 @@ def ssm_kernel_inputs(kind: str, B: int, H: int, P: int, D: int, R: int,
     negative A_log * dt decay, softmax dt + 0.01, sigmoid gate, random state.
     """
     rng = np.random.default_rng(seed)
-    g = lambda *s: rng.standard_normal(s).astype(F32)
-    A_log = (-rng.random(H) * 2).astype(F32)
+    g = lambda *s: rng.standard_normal(s).astype(F32, copy=False)
+    A_log = (-rng.random(H) * 2).astype(F32, copy=False)
     logits = g(B, H)
     e = np.exp(logits - logits.max(axis=-1, keepdims=True))
-    dt = (e / e.sum(axis=-1, keepdims=True) + 0.01).astype(F32)
+    dt = (e / e.sum(axis=-1, keepdims=True) + 0.01).astype(F32, copy=False)
     trap = sigmoid(g(B, H)) if trap_value is None else np.full((B, H), trap_value, F32)
-    d = {"x": g(B, H, P), "ADT": (A_log[None, :] * dt).astype(F32), "DT": dt,
+    d = {"x": g(B, H, P), "ADT": (A_log[None, :] * dt).astype(F32, copy=False), "DT": dt,
          "trap": trap, "D_skip": g(H), "z": g(B, H, P)}
     if kind == "siso":
         d.update(B_proj=g(B, H, D), C_proj=g(B, H, D), h=g(B, H, P, D), bx_prev=g(B, H, P, D))

@@ -79,6 +79,7 @@ LAYERS = [
     (dict(d_model=64, d_state=256, headdim=32), 1),
     (dict(d_model=96, d_state=48, headdim=24), 2),                           # non-power-of-two D, P
     (dict(d_model=40, d_state=96, headdim=20, rope_fraction=1.0), 2),
+    (dict(d_model=48, d_state=16, headdim=32), 3),                           # 3 heads: unaligned sections
 ]
 
 
@@ -99,6 +100,36 @@ def test_mimo_full_fused(kw, batch, R):
 def test_bf16_in_proj_output_and_params(mimo):
     dims = orc.layer_dims(d_model=128, d_state=64, headdim=32, is_mimo=mimo, mimo_rank=4)
     _compare(dims, orc.synthetic_params(dims, 5, bf16=True), 3, steps=3, seed=6, zx_bf16=True)
+
+
+@pytest.mark.parametrize("mimo", [False, True])
+def test_mixed_dtypes_bf16_zx_f32_params(mimo):
+    """bf16 in_proj output with fp32 parameters (the generic MIMO path)."""
+    dims = orc.layer_dims(d_model=128, d_state=64, headdim=32, is_mimo=mimo, mimo_rank=2)
+    params = orc.synthetic_params(dims, 21)
+    rng = np.random.default_rng(22)
+    st_np = _random_state(dims, 3, rng)
+    st = {k: _t(v) for k, v in st_np.items()}
+    zx = orc.round_bf16((rng.standard_normal((3, dims["d_in_proj"])) * 0.6).astype(np.float32))
+    y = _kernel(dims, params, _t(zx, torch.bfloat16), st, torch.float32)
+    ye, a, h, bx = orc.ssm_from_zx(zx, params, dims, st_np["angle_state"], st_np["ssm_state"],
+                                   st_np["bx_prev"])
+    np.testing.assert_allclose(y.cpu().numpy(), ye, **TOL)
+    np.testing.assert_allclose(st["ssm_state"].cpu().numpy(), h, **TOL)
+
+
+def test_bounded_wait_reports_timeout():
+    """A wait on a barrier nothing completes gives up and sets the device
+    error word instead of hanging; the context stays usable."""
+    from src import _native as nat
+    lib = nat.load()
+    assert nat.device_error(reset=True) == 0
+    assert lib.m3_selftest_wait_timeout(torch.cuda.current_stream().cuda_stream) == nat.M3_OK
+    torch.cuda.synchronize()
+    assert nat.device_error(reset=True) == nat.M3_DEVERR_TIMEOUT
+    assert nat.device_error() == 0
+    x = torch.ones(4, device="cuda")
+    assert (x + 1).sum().item() == 8.0
 
 
 @pytest.mark.parametrize("name", [n for n in golden_names("layer") if load_golden(n)["meta"]["bf16"]])
