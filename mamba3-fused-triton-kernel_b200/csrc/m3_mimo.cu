@@ -1,23 +1,28 @@
 // MIMO decode kernels.
 //
-// mimo_stream_kernel (full-step fused, aligned shapes): one CTA owns a group
-// of heads (one warp per head) and a chunk of consecutive batch rows.  The
-// per-head parameters (B/C biases, the rank projections mimo_x / mimo_o,
-// dt_bias, D, norm weights) are staged in shared memory once per CTA and
-// reused for every row of the chunk.  For each batch row a ring stage is
-// filled by 1-D bulk (TMA) copies of the row's B/C/x/z/scalar/angle sections
-// of the in_proj output and of the heads' ssm_state / bx_prev / angle_state;
-// the next rows land while the current one is computed.  Per row:
-//   * RMSNorm of the R B-rows and R C-rows, shared by the CTA's heads;
-//   * per head: x_r = mimo_x x (one warp transpose-reduction for all ranks),
-//     Bx = RoPE(sum_r x_r (Bn_r + bias_r)) -- RoPE is linear, so rotating
-//     the rank sum equals summing the rotated ranks (src/kernels/utils.py:
-//     133 with B_proj from src/models/mamba3.py:330-332);
-//     the trapezoidal update; y_r = <Cn_r + cbias_r, RoPE^-1(h)> (a
-//     rotation is orthogonal, so <RoPE(c), h> = <c, RoPE^-1(h)>);
-//     y = sum_r (y_r + D x_r) mimo_o[r] * silu(z).
+// mimo_row_kernel (full-step fused).  One CTA owns 8 heads (one warp per
+// head) and a chunk of consecutive batch rows; each thread issues all of a
+// row's independent loads before using any of them, and four CTAs share an
+// SM so that their rows hide each other's latency.  Per row:
+//   A (all threads)  RMSNorm of the R B-rows and R C-rows (shared by every
+//                    head of the CTA), the head scalars DT / exp(A DT) /
+//                    trap (lane = head), and the accumulated RoPE angles
+//                    (one sincosf per thread and angle, written back to
+//                    angle_state), into a double-buffered shared block, so
+//                    one barrier per row suffices;
+//   B (warp / head)  x_r = mimo_x x (one transpose-reduction for all ranks);
+//                    Bx = RoPE(sum_r x_r (Bn_r + bias_r)) -- RoPE is linear,
+//                    so rotating the rank sum equals summing the rotated
+//                    ranks (src/kernels/utils.py:133 with B_proj from
+//                    src/models/mamba3.py:330-332); the trapezoidal update;
+//                    y_r = <Cn_r + cbias_r, RoPE^-1(h)> (a rotation is
+//                    orthogonal: <RoPE(c), h> = <c, RoPE^-1(h)>);
+//                    y = sum_r (y_r + D x_r) mimo_o[r] * silu(z).
+// Parameters are read through the read-only cache, where a CTA's 8 heads
+// stay resident across its rows.
 // mimo_decode_kernel (m3_kernels.cuh) serves everything else: the
-// state-update-only entry points and shapes the aligned path does not take.
+// state-update-only entry points and shapes the row kernel does not take
+// (head counts that are not a multiple of 8, headdim > 128, mixed dtypes).
 #include "m3_async.cuh"
 #include "m3_kernels.cuh"
 
@@ -57,31 +62,36 @@ __device__ __forceinline__ void warp_allreduce_ranks(float (&v)[R]) {
   for (int r = 0; r < R; ++r) v[r] = __shfl_sync(kFullMask, t, r << (5 - LR));
 }
 
-struct MimoPlan {
-  int rows_per_cta;  // consecutive batch rows per CTA
-  int nstage;
-  // byte offsets
-  int par_off, nbc_off, ring_off, stage_bytes;
-  // byte offsets inside a stage
-  int o_raw, o_x, o_z, o_scal, o_h, o_bx, o_ang;
-};
-
-// Shared-memory parameter block (fp32) of a CTA with hpc heads.
-template <int BD, int R>
-struct ParLayout {
-  int bB, bC, mx, mo, dtb, dsk, wB, wC, total;  // float offsets
-  __host__ __device__ ParLayout(int hpc, int P) {
-    bB = 0;
-    bC = bB + hpc * R * BD;
-    mx = bC + hpc * R * BD;
-    mo = mx + hpc * R * P;
-    dtb = mo + hpc * R * P;
-    dsk = dtb + hpc;
-    wB = dsk + hpc;
-    wC = wB + BD;
-    total = wC + BD;
+// Loads through the non-coherent (read-only) path: parameters and the
+// in_proj output are never written by the kernel.
+template <typename T> __device__ __forceinline__ float ldg_f(const T *p);
+template <> __device__ __forceinline__ float ldg_f<float>(const float *p) { return __ldg(p); }
+template <> __device__ __forceinline__ float ldg_f<__nv_bfloat16>(const __nv_bfloat16 *p) {
+  return __bfloat162float(__ldg(p));
+}
+template <int VW, typename T>
+__device__ __forceinline__ void ldg_vec(const T *p, float (&v)[VW]) {
+  if constexpr (sizeof(T) == 4) {
+    if constexpr (VW == 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      const float2 t = __ldg(reinterpret_cast<const float2 *>(p));
+      v[0] = t.x; v[1] = t.y;
+    }
+  } else {
+    if constexpr (VW == 4) {
+      const uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const unsigned t = __ldg(reinterpret_cast<const unsigned *>(p));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t));
+      v[0] = a.x; v[1] = a.y;
+    }
   }
-};
+}
 
 __device__ __forceinline__ void st_vec_global(float *p, const float (&v)[4]) {
   asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
@@ -91,164 +101,174 @@ __device__ __forceinline__ void st_vec_global(float *p, const float (&v)[2]) {
   asm volatile("st.global.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(v[0]), "f"(v[1]) : "memory");
 }
 
-template <int BD, int R, typename T>
-__global__ void __launch_bounds__(256) mimo_stream_kernel(const KParams p, const MimoPlan mp) {
+constexpr int kRowWarps = 8;  // heads per CTA of the row kernel
+
+// Everything one thread needs from one batch row, loaded before first use.
+template <int BD, int R, int KP>
+struct RowRegs {
+  static constexpr int VW = MimoShape<BD>::VW, F = MimoShape<BD>::F, KPL = MimoShape<BD>::KPL;
+  static constexpr int NRW = (2 * R + kRowWarps - 1) / kRowWarps;  // norm rows per warp
+  static constexpr int NA = BD / 64 > 0 ? BD / 64 : 1;             // angles per thread
+  float h[F][VW], bx[F][VW];  // this warp's head state
+  float x[KP];                // x of this warp's head, lanes over headdim
+  float raw[NRW][KPL];        // B/C rows this warp normalizes
+  float sc[3];                // warp 0, lane < heads: dd_dt, dd_A, trap_raw of head `lane`
+  float ang[NA], araw[NA];    // angle state + increment of this thread's angles
+};
+
+// The row kernel: see the file comment.  One CTA = kRowWarps heads x a chunk
+// of consecutive batch rows; every warp owns one head.
+template <int BD, int R, typename T, int KP>
+__global__ void __launch_bounds__(kRowWarps * 32, 4) mimo_row_kernel(const KParams p, const int rows_per_cta) {
   using Sh = MimoShape<BD>;
-  constexpr int VW = Sh::VW, F = Sh::F, KPL = Sh::KPL, NPAIR = VW / 2;
+  using RR = RowRegs<BD, R, KP>;
+  constexpr int VW = Sh::VW, F = Sh::F, KPL = Sh::KPL, NPAIR = VW / 2, NRW = RR::NRW, NA = RR::NA;
   using V = typename VecOf<VW>::T;
 
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
-  float *par = reinterpret_cast<float *>(smem_raw + mp.par_off);
-  float *nBC = reinterpret_cast<float *>(smem_raw + mp.nbc_off);  // [2R][BD]
+  // double-buffered per-row work block: normalized rows [2R][BD], head
+  // scalars [8][4], cos/sin [8][A][2]
+  extern __shared__ __align__(16) float smem[];
+  const int A = p.A;
+  const int wstride = 2 * R * BD + 4 * kRowWarps + 2 * kRowWarps * A;
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-  const int H = p.H, P = p.P, D = p.D, A = p.A;
-  const int hpc = p.heads_per_cta;
-  const int ngrp = (H + hpc - 1) / hpc;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = p.H, P = p.P, D = p.D;
+  const int ngrp = H / kRowWarps;
   const int grp = blockIdx.x % ngrp;
-  const int b0 = (blockIdx.x / ngrp) * mp.rows_per_cta;
-  const int b1 = min(p.B, b0 + mp.rows_per_cta);
-  const int h0 = grp * hpc;
-  const int nh = min(hpc, H - h0);
-  const ParLayout<BD, R> L(hpc, P);
+  const int b0 = (blockIdx.x / ngrp) * rows_per_cta;
+  const int b1 = min(p.B, b0 + rows_per_cta);
+  const int h0 = grp * kRowWarps;
+  const int hh = h0 + warp;
   const T *zx = static_cast<const T *>(p.zx);
-  const int so = 2 * p.d_inner + 2 * p.d_bc;  // scalar section: dd_dt[H] dd_A[H] trap[H] angle[A]
+  const int so = 2 * p.d_inner + 2 * p.d_bc;  // dd_dt[H] dd_A[H] trap[H] angle[A]
 
-  if (tid == 0) {
-    for (int s = 0; s < mp.nstage; ++s) mbar_init(smem_addr(&bars[s]), 1);
-    mbar_init_fence();
-  }
-  __syncthreads();
-
-  constexpr int es = sizeof(T);
-  auto issue = [&](int k) {
-    const int b = b0 + k;
-    if (b >= b1) return;
-    const int s = k % mp.nstage;
-    unsigned char *st = smem_raw + mp.ring_off + (size_t)s * mp.stage_bytes;
-    const uint32_t bar = smem_addr(&bars[s]);
+  auto load_row = [&](int b, RR &r) {
     const T *row = zx + (int64_t)b * p.zx_sb;
-    const uint32_t n_raw = 2u * R * D * es, n_xz = (uint32_t)nh * P * es, n_scal = (uint32_t)(3 * H + A) * es;
-    const uint32_t n_hd = (uint32_t)nh * D * 4, n_ang = (uint32_t)nh * A * 4;
-    mbar_arrive_expect_tx(bar, n_raw + 2 * n_xz + n_scal + 2 * n_hd + n_ang);
-    const int64_t sb = ((int64_t)b * H + h0);
-    bulk_g2s(smem_addr(st + mp.o_raw), row + 2 * p.d_inner, n_raw, bar);
-    bulk_g2s(smem_addr(st + mp.o_x), row + p.d_inner + (int64_t)h0 * P, n_xz, bar);
-    bulk_g2s(smem_addr(st + mp.o_z), row + (int64_t)h0 * P, n_xz, bar);
-    bulk_g2s(smem_addr(st + mp.o_scal), row + so, n_scal, bar);
-    bulk_g2s(smem_addr(st + mp.o_h), p.h + sb * D, n_hd, bar);
-    bulk_g2s(smem_addr(st + mp.o_bx), p.bx + sb * D, n_hd, bar);
-    bulk_g2s(smem_addr(st + mp.o_ang), p.ang + sb * A, n_ang, bar);
-  };
-  if (tid == 0)
-    for (int k = 0; k < mp.nstage; ++k) issue(k);
-
-  // ---- parameters of this CTA's heads -> shared memory (fp32) ----
-  {
-    const T *bB = static_cast<const T *>(p.bB), *bC = static_cast<const T *>(p.bC);
-    const T *mx = static_cast<const T *>(p.mx), *mo = static_cast<const T *>(p.mo);
-    const int nbias = nh * R * D;
-    for (int i = tid; i < nbias; i += blockDim.x) {
-      const int w = i / (R * D), rd = i - w * (R * D), r = rd / D, d = rd - r * D;
-      const int64_t g = (int64_t)(h0 + w) * R * D + rd;
-      par[L.bB + (w * R + r) * BD + d] = to_f(bB[g]);
-      par[L.bC + (w * R + r) * BD + d] = to_f(bC[g]);
-    }
-    const int nm = nh * R * P;
-    for (int i = tid; i < nm; i += blockDim.x) {
-      const int64_t g = (int64_t)h0 * R * P + i;
-      par[L.mx + i] = to_f(mx[g]);
-      par[L.mo + i] = to_f(mo[g]);
-    }
-    for (int i = tid; i < nh; i += blockDim.x) {
-      par[L.dtb + i] = to_f(static_cast<const T *>(p.dt_bias)[h0 + i]);
-      par[L.dsk + i] = to_f(static_cast<const T *>(p.Dp)[h0 + i]);
-    }
-    for (int i = tid; i < D; i += blockDim.x) {
-      par[L.wB + i] = to_f(static_cast<const T *>(p.wB)[i]);
-      par[L.wC + i] = to_f(static_cast<const T *>(p.wC)[i]);
-    }
-  }
-  __syncthreads();  // parameters staged (the first rows are already in flight)
-
-  int k = 0;
-  for (; b0 + k < b1; ++k) {
-    const int b = b0 + k;
-    const int s = k % mp.nstage;
-    const bool ok = mbar_wait(smem_addr(&bars[s]), (uint32_t)((k / mp.nstage) & 1));
-    if (__syncthreads_or(!ok)) break;
-    const unsigned char *st = smem_raw + mp.ring_off + (size_t)s * mp.stage_bytes;
-    const T *sRaw = reinterpret_cast<const T *>(st + mp.o_raw);
-    const T *sX = reinterpret_cast<const T *>(st + mp.o_x);
-    const T *sZ = reinterpret_cast<const T *>(st + mp.o_z);
-    const T *sScal = reinterpret_cast<const T *>(st + mp.o_scal);
-    const float *sH = reinterpret_cast<const float *>(st + mp.o_h);
-    const float *sBx = reinterpret_cast<const float *>(st + mp.o_bx);
-    const float *sAng = reinterpret_cast<const float *>(st + mp.o_ang);
-
-    // RMSNorm of the 2R B/C rows of this batch row (src/models/mamba3.py:202-203)
-    for (int row = warp; row < 2 * R; row += nwarps) {
-      const float *w = par + (row < R ? L.wB : L.wC);
-      float v[KPL];
-      float ss = 0.f;
+    const int64_t sbase = ((int64_t)b * H + hh) * D;
 #pragma unroll
-      for (int q = 0; q < KPL; ++q) {
-        const int d = lane + 32 * q;
-        v[q] = d < D ? to_f(sRaw[row * D + d]) : 0.f;
-        ss += v[q] * v[q];
+    for (int f = 0; f < F; ++f) {
+      const int col = (lane + 32 * f) * VW;
+      if (col < D) {
+        ld_vec<VW>(p.h + sbase + col, r.h[f]);
+        ld_vec<VW>(p.bx + sbase + col, r.bx[f]);
       }
-      ss = group_sum<32>(ss);
-      const float rms = sqrtf(ss / (float)D + kRmsEps);
+    }
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      const int pp = lane + 32 * k;
+      r.x[k] = pp < P ? ldg_f(row + p.d_inner + (int64_t)hh * P + pp) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < NRW; ++j) {
+      const int rr = warp + kRowWarps * j;
+      const int col0 = 2 * p.d_inner + (rr < R ? 0 : p.d_bc) + (rr % R) * D;
 #pragma unroll
       for (int q = 0; q < KPL; ++q) {
         const int d = lane + 32 * q;
-        if (d < D) nBC[row * BD + d] = v[q] / rms * w[d];
+        r.raw[j][q] = (rr < 2 * R && d < D) ? ldg_f(row + col0 + d) : 0.f;
+      }
+    }
+    if (warp == 0 && lane < kRowWarps) {
+      r.sc[0] = ldg_f(row + so + h0 + lane);
+      r.sc[1] = ldg_f(row + so + H + h0 + lane);
+      r.sc[2] = ldg_f(row + so + 2 * H + h0 + lane);
+    }
+#pragma unroll
+    for (int n = 0; n < NA; ++n) {
+      const int i = tid + n * kRowWarps * 32;
+      const int w = i / A, a = i - w * A;
+      if (w < kRowWarps) {
+        r.ang[n] = p.ang[((int64_t)b * H + h0 + w) * A + a];
+        r.araw[n] = ldg_f(row + so + 3 * H + a);
+      }
+    }
+  };
+
+  RR cur;
+  for (int b = b0; b < b1; ++b) {
+    load_row(b, cur);
+    const T *row = zx + (int64_t)b * p.zx_sb;
+    float *wk = smem + ((b - b0) & 1) * wstride;
+    float *nBC = wk, *wsc = wk + 2 * R * BD, *wrot = wsc + 4 * kRowWarps;
+
+    // ---- phase A ----
+    // RMSNorm of the 2R B/C rows (src/models/mamba3.py:202-203)
+#pragma unroll
+    for (int j = 0; j < NRW; ++j) {
+      const int rr = warp + kRowWarps * j;
+      if (rr < 2 * R) {
+        const void *wn = rr < R ? p.wB : p.wC;
+        float ss = 0.f;
+#pragma unroll
+        for (int q = 0; q < KPL; ++q) ss += cur.raw[j][q] * cur.raw[j][q];
+        ss = group_sum<32>(ss);
+        const float rms = sqrtf(ss / (float)D + kRmsEps);
+#pragma unroll
+        for (int q = 0; q < KPL; ++q) {
+          const int d = lane + 32 * q;
+          if (d < D) nBC[rr * BD + d] = cur.raw[j][q] / rms * ldg_f(static_cast<const T *>(wn) + d);
+        }
+      }
+    }
+    // head scalars, lane = head (src/models/mamba3.py:196-199)
+    if (warp == 0 && lane < kRowWarps) {
+      const float dd_A = cur.sc[1];
+      float A_val;
+      if (p.A_floor > 0.f) {
+        // softplus(.) >= 0 > -A_floor for every non-NaN input, so the
+        // clamp returns -A_floor; a NaN propagates as in torch.clamp
+        A_val = dd_A != dd_A ? dd_A : p.A_floor;
+      } else {
+        const float sp = softplus_f(dd_A);
+        A_val = -(sp > -p.A_floor ? -p.A_floor : sp);
+      }
+      const float DT = softplus_f(cur.sc[0] + ldg_f(static_cast<const T *>(p.dt_bias) + h0 + lane));
+      const float tr = sigmoid_f(cur.sc[2]);
+      float *sc = wsc + 4 * lane;
+      sc[0] = expf(A_val * DT);
+      sc[1] = DT;
+      sc[2] = 1.f - tr;
+      sc[3] = tr * 0.5f;
+    }
+    // accumulated angles -> cos/sin, written back (src/models/mamba3.py:326-327)
+#pragma unroll
+    for (int n = 0; n < NA; ++n) {
+      const int i = tid + n * kRowWarps * 32;
+      const int w = i / A, a = i - w * A;
+      if (w < kRowWarps) {
+        const float dd_dt = ldg_f(row + so + h0 + w);  // L1 hit: warp 0 loaded it
+        const float DT = softplus_f(dd_dt + ldg_f(static_cast<const T *>(p.dt_bias) + h0 + w));
+        const float ang = cur.ang[n] + cur.araw[n] * DT;
+        p.ang[((int64_t)b * H + h0 + w) * A + a] = ang;
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        wrot[2 * i] = cs;
+        wrot[2 * i + 1] = sn;
       }
     }
     __syncthreads();
 
-    if (warp < nh) {
-      const int w = warp, hh = h0 + w;
-      // scalars (src/models/mamba3.py:196-199)
-      const float dd_dt = to_f(sScal[hh]), dd_A = to_f(sScal[H + hh]), tr_raw = to_f(sScal[2 * H + hh]);
-      const float sp = softplus_f(dd_A);
-      const float Aval = -(sp > -p.A_floor ? -p.A_floor : sp);
-      Coef c;
-      c.DT = softplus_f(dd_dt + par[L.dtb + w]);
-      c.decay = expf(Aval * c.DT);
-      const float tr = sigmoid_f(tr_raw);
-      c.omt = 1.f - tr;
-      c.htr = tr * 0.5f;
-      const float dskip = par[L.dsk + w];
-
-      // angles of this lane's RoPE pairs (angle_state += angle_raw * DT)
-      float cs[F][NPAIR], sn[F][NPAIR];
-      const int64_t abase = ((int64_t)b * H + hh) * A;
-#pragma unroll
-      for (int f = 0; f < F; ++f)
-#pragma unroll
-        for (int q = 0; q < NPAIR; ++q) {
-          const int i = (lane + 32 * f) * NPAIR + q;
-          cs[f][q] = 1.f;
-          sn[f][q] = 0.f;
-          if (i < A) {
-            const float ang = sAng[w * A + i] + to_f(sScal[3 * H + i]) * c.DT;
-            p.ang[abase + i] = ang;
-            sincosf(ang, &sn[f][q], &cs[f][q]);
-          }
-        }
+    // ---- phase B: this warp's head ----
+    {
+      const float *sc = wsc + 4 * warp;
+      const Coef c = {sc[0], sc[1], sc[2], sc[3]};
+      const float dskip = ldg_f(static_cast<const T *>(p.Dp) + hh);
+      const float *rot = wrot + 2 * warp * A;
+      const T *mx = static_cast<const T *>(p.mx) + (int64_t)hh * R * P;
+      const T *mo = static_cast<const T *>(p.mo) + (int64_t)hh * R * P;
+      const T *bB = static_cast<const T *>(p.bB) + (int64_t)hh * R * D;
+      const T *bC = static_cast<const T *>(p.bC) + (int64_t)hh * R * D;
 
       // x_r = sum_p x_p mimo_x[h, r, p]
       float xr[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) xr[r] = 0.f;
-      for (int p0 = 0; p0 < P; p0 += 32) {
-        const int pp = p0 + lane;
-        if (pp < P) {
-          const float xp = to_f(sX[w * P + pp]);
 #pragma unroll
-          for (int r = 0; r < R; ++r) xr[r] += xp * par[L.mx + (w * R + r) * P + pp];
+      for (int k = 0; k < KP; ++k) {
+        const int pp = lane + 32 * k;
+        if (pp < P) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) xr[r] += cur.x[k] * ldg_f(mx + r * P + pp);
         }
       }
       warp_allreduce_ranks<R>(xr);
@@ -262,15 +282,23 @@ __global__ void __launch_bounds__(256) mimo_stream_kernel(const KParams p, const
 #pragma unroll
         for (int e = 0; e < VW; ++e) hr[f][e] = 0.f;
         if (col < D) {
+          float cs[NPAIR], sn[NPAIR];
+#pragma unroll
+          for (int q = 0; q < NPAIR; ++q) {
+            const int i = col / 2 + q;
+            const bool on = i < A;
+            cs[q] = on ? rot[2 * i] : 1.f;
+            sn[q] = on ? rot[2 * i + 1] : 0.f;
+          }
           float acc[VW];
 #pragma unroll
           for (int e = 0; e < VW; ++e) acc[e] = 0.f;
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const V nv = *reinterpret_cast<const V *>(nBC + r * BD + col);
-            const V bv = *reinterpret_cast<const V *>(par + L.bB + (w * R + r) * BD + col);
+            float bb[VW];
+            ldg_vec<VW>(bB + r * D + col, bb);
             const float *n = reinterpret_cast<const float *>(&nv);
-            const float *bb = reinterpret_cast<const float *>(&bv);
 #pragma unroll
             for (int e = 0; e < VW; ++e) acc[e] += xr[r] * (n[e] + bb[e]);
           }
@@ -278,22 +306,18 @@ __global__ void __launch_bounds__(256) mimo_stream_kernel(const KParams p, const
 #pragma unroll
           for (int q = 0; q < NPAIR; ++q) {
             const float x1 = acc[2 * q], x2 = acc[2 * q + 1];
-            bxv[2 * q] = x1 * cs[f][q] - x2 * sn[f][q];
-            bxv[2 * q + 1] = x1 * sn[f][q] + x2 * cs[f][q];
+            bxv[2 * q] = x1 * cs[q] - x2 * sn[q];
+            bxv[2 * q + 1] = x1 * sn[q] + x2 * cs[q];
           }
-          const V ho = *reinterpret_cast<const V *>(sH + w * D + col);
-          const V bo = *reinterpret_cast<const V *>(sBx + w * D + col);
-          const float *hov = reinterpret_cast<const float *>(&ho);
-          const float *bov = reinterpret_cast<const float *>(&bo);
 #pragma unroll
-          for (int e = 0; e < VW; ++e) hn[e] = trap_update(c, bxv[e], bov[e], hov[e]);
+          for (int e = 0; e < VW; ++e) hn[e] = trap_update(c, bxv[e], cur.bx[f][e], cur.h[f][e]);
           st_vec_global(p.h + sbase + col, hn);
           st_vec_global(p.bx + sbase + col, bxv);
 #pragma unroll
           for (int q = 0; q < NPAIR; ++q) {
             const float x1 = hn[2 * q], x2 = hn[2 * q + 1];
-            hr[f][2 * q] = x1 * cs[f][q] + x2 * sn[f][q];
-            hr[f][2 * q + 1] = x2 * cs[f][q] - x1 * sn[f][q];
+            hr[f][2 * q] = x1 * cs[q] + x2 * sn[q];
+            hr[f][2 * q + 1] = x2 * cs[q] - x1 * sn[q];
           }
         }
       }
@@ -308,9 +332,9 @@ __global__ void __launch_bounds__(256) mimo_stream_kernel(const KParams p, const
           const int col = (lane + 32 * f) * VW;
           if (col < D) {
             const V nv = *reinterpret_cast<const V *>(nBC + (R + r) * BD + col);
-            const V cv = *reinterpret_cast<const V *>(par + L.bC + (w * R + r) * BD + col);
+            float cc[VW];
+            ldg_vec<VW>(bC + r * D + col, cc);
             const float *n = reinterpret_cast<const float *>(&nv);
-            const float *cc = reinterpret_cast<const float *>(&cv);
 #pragma unroll
             for (int e = 0; e < VW; ++e) part += (n[e] + cc[e]) * hr[f][e];
           }
@@ -323,27 +347,20 @@ __global__ void __launch_bounds__(256) mimo_stream_kernel(const KParams p, const
 
       // y_p = sum_r y_r mimo_o[h, r, p], gated by silu(z)
       const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * P;
-      for (int p0 = 0; p0 < P; p0 += 32) {
-        const int pp = p0 + lane;
+#pragma unroll
+      for (int k = 0; k < KP; ++k) {
+        const int pp = lane + 32 * k;
         if (pp < P) {
           float yv = 0.f;
 #pragma unroll
-          for (int r = 0; r < R; ++r) yv += yr[r] * par[L.mo + (w * R + r) * P + pp];
-          yv = yv * silu_f(to_f(sZ[w * P + pp]));
-          st_any(p.y, ybase + pp, yv, p.y_dt);
+          for (int r = 0; r < R; ++r) yv += yr[r] * ldg_f(mo + r * P + pp);
+          const float zv = ldg_f(row + (int64_t)hh * P + pp);
+          st_any(p.y, ybase + pp, yv * silu_f(zv), p.y_dt);
         }
       }
     }
-    __syncthreads();  // stage s and nBC are free again
-    if (tid == 0) issue(k + mp.nstage);
-  }
-  if (tid == 0) {  // only after a lost copy: bounded wait for what is still in flight
-    for (int q = k; q < k + mp.nstage; ++q)
-      if (b0 + q < b1) mbar_wait(smem_addr(&bars[q % mp.nstage]), (uint32_t)((q / mp.nstage) & 1), 1 << 16);
   }
 }
-
-int align128(int x) { return (x + 127) / 128 * 128; }
 
 int num_sms() {
   static int cached[64] = {0};
@@ -357,88 +374,64 @@ int num_sms() {
   return cached[dev];
 }
 
-constexpr int kMaxSmem = 200 * 1024;
+bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-// Shared-memory plan of the aligned path; returns false if it does not fit.
-template <int BD, int R>
-bool mimo_plan(const KParams &kp, int es, int nstage, MimoPlan &mp, int *smem) {
-  const int hpc = kp.heads_per_cta, P = kp.P, D = kp.D, A = kp.A, H = kp.H;
-  const ParLayout<BD, R> L(hpc, P);
-  mp.nstage = nstage;
-  mp.par_off = 128;
-  mp.nbc_off = mp.par_off + align128(L.total * 4);
-  mp.ring_off = mp.nbc_off + align128(2 * R * BD * 4);
-  int o = 0;
-  mp.o_raw = o; o += align128(2 * R * D * es);
-  mp.o_x = o; o += align128(hpc * P * es);
-  mp.o_z = o; o += align128(hpc * P * es);
-  mp.o_scal = o; o += align128((3 * H + A) * es);
-  mp.o_h = o; o += align128(hpc * D * 4);
-  mp.o_bx = o; o += align128(hpc * D * 4);
-  mp.o_ang = o; o += align128(hpc * A * 4);
-  mp.stage_bytes = o;
-  *smem = mp.ring_off + nstage * mp.stage_bytes;
-  return *smem <= kMaxSmem;
-}
-
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-// Whether the aligned path can take this call: every bulk copy must start
-// on a 16-byte boundary and move a multiple of 16 bytes.
-bool stream_eligible(const KParams &kp, int es) {
+// Whether the row kernel can take this call: whole groups of 8 heads, one
+// dtype for the in_proj output and the parameters, vector-aligned state
+// and parameter rows, and headdim <= 32 * KP.
+bool row_eligible(const KParams &kp, int es, int VW) {
   if (kp.zx_dt != kp.par_dt) return false;
-  const int64_t zrow = kp.zx_sb * es;
-  if (zrow % 16 || !aligned16(kp.zx) || !aligned16(kp.ang) || !aligned16(kp.h) || !aligned16(kp.bx)) return false;
-  if ((kp.d_inner * es) % 16 || (kp.d_bc * es) % 16 || (kp.P * es) % 16) return false;
-  if (((3 * kp.H + kp.A) * es) % 16 || (kp.A % 4) != 0) return false;
+  if (kp.H % kRowWarps != 0 || kp.P > 128) return false;
+  if (!aligned(kp.h, 16) || !aligned(kp.bx, 16) || !aligned(kp.bB, VW * es) || !aligned(kp.bC, VW * es)) return false;
+  if ((kp.D * es) % (VW * es) != 0) return false;
   return true;
 }
 
-template <int BD, int R, typename T>
-cudaError_t launch_stream(KParams kp, cudaStream_t stream, bool *taken) {
-  *taken = false;
-  const int es = sizeof(T);
-  if (!stream_eligible(kp, es)) return cudaSuccess;
-  kp.heads_per_cta = kp.H < (R == 8 ? 4 : 8) ? kp.H : (R == 8 ? 4 : 8);
-  MimoPlan mp;
-  int smem = 0;
-  if (!mimo_plan<BD, R>(kp, es, 3, mp, &smem) && !mimo_plan<BD, R>(kp, es, 2, mp, &smem)) return cudaSuccess;
-  auto kern = mimo_stream_kernel<BD, R, T>;
+template <int BD, int R, typename T, int KP>
+cudaError_t launch_row_kp(const KParams &kp, cudaStream_t stream) {
+  auto kern = mimo_row_kernel<BD, R, T, KP>;
+  const size_t smem = 2 * (size_t)(2 * R * BD + 4 * kRowWarps + 2 * kRowWarps * kp.A) * sizeof(float);
   static bool attr = false;
-  static int last_smem = -1, last_per_sm = 1, last_threads = 0;
+  static size_t last_smem = (size_t)-1;
+  static int last_per_sm = 1;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int threads = kp.heads_per_cta * 32;
-  if (smem != last_smem || threads != last_threads) {
+  if (smem != last_smem) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, smem) != cudaSuccess ||
+        per_sm < 1)
       per_sm = 1;
     last_smem = smem;
-    last_threads = threads;
     last_per_sm = per_sm;
   }
-  // batch rows per CTA: enough CTAs to fill every SM once, each reusing its
-  // staged parameters over as many rows as that allows
-  const int ngrp = (kp.H + kp.heads_per_cta - 1) / kp.heads_per_cta;
+  const int ngrp = kp.H / kRowWarps;
   const int slots = num_sms() * last_per_sm;
   const int64_t items = (int64_t)kp.B * ngrp;
   int rows = (int)((items + slots - 1) / slots);
   if (rows < 1) rows = 1;
-  mp.rows_per_cta = rows;
   const int64_t grid = (int64_t)ngrp * ((kp.B + rows - 1) / rows);
-  kern<<<(unsigned)grid, threads, smem, stream>>>(kp, mp);
-  *taken = true;
+  kern<<<(unsigned)grid, kRowWarps * 32, smem, stream>>>(kp, rows);
   return cudaGetLastError();
+}
+
+template <int BD, int R, typename T>
+cudaError_t launch_row(const KParams &kp, cudaStream_t stream, bool *taken) {
+  *taken = false;
+  if (!row_eligible(kp, sizeof(T), MimoShape<BD>::VW)) return cudaSuccess;
+  *taken = true;
+  if (kp.P <= 32) return launch_row_kp<BD, R, T, 1>(kp, stream);
+  if (kp.P <= 64) return launch_row_kp<BD, R, T, 2>(kp, stream);
+  return launch_row_kp<BD, R, T, 4>(kp, stream);
 }
 
 template <int BD, int R>
 cudaError_t launch_full_t(const KParams &kp, cudaStream_t stream) {
   bool taken = false;
-  cudaError_t e = kp.zx_dt == M3_BF16 ? launch_stream<BD, R, __nv_bfloat16>(kp, stream, &taken)
-                                      : launch_stream<BD, R, float>(kp, stream, &taken);
+  cudaError_t e = kp.zx_dt == M3_BF16 ? launch_row<BD, R, __nv_bfloat16>(kp, stream, &taken)
+                                      : launch_row<BD, R, float>(kp, stream, &taken);
   if (e != cudaSuccess || taken) return e;
   // generic path
   const int ngrp = (kp.H + kp.heads_per_cta - 1) / kp.heads_per_cta;
