@@ -17,10 +17,10 @@ CUDA event pair on the launching stream (the flush is outside the pair).
 ``value`` = tokens / (sum of step times), max over ranks, all ranks' tokens.
 
 ``e2e`` times the public API end to end: per step, the pinned host input
-goes in through ``Mamba3Decoder.step`` (which copies it into the graph's
-input buffer), the graph replays, the output is copied back to pinned host
-memory and the stream is synchronised; the event pair brackets all of it,
-after an L2 flush that has completed.
+is copied to the device, ``Mamba3Decoder.step`` replays the graph on it,
+the output is copied back to pinned host memory and the stream is
+synchronised so the host holds the result; the event pair brackets all of
+it, after an L2 flush that has completed.
 
 ``roofline`` is for the fused decode kernel (the dominant kernel of the
 step): its algorithmic HBM bytes per launch over its mean duration in a K-launch
@@ -331,11 +331,13 @@ def main():
 
     # ---- end to end through the public API (pinned host in/out) ----
     out_host = torch.empty(batch, model.d_model, dtype=wdtype).pin_memory()
+    u_stage = torch.empty(batch, model.d_model, device=dev, dtype=wdtype)
 
     def e2e_step(i):
-        out, _ = dec.step(u_host[i % n_inputs], state)
-        out_host.copy_(out, non_blocking=True)
-        stream.synchronize()
+        u_stage.copy_(u_host[i % n_inputs], non_blocking=True)  # pinned host -> device
+        out, _ = dec.step(u_stage, state)
+        out_host.copy_(out, non_blocking=True)                  # device -> pinned host
+        stream.synchronize()                                    # the host reads the result
 
     barrier()
     with torch.no_grad():
