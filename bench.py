@@ -88,16 +88,17 @@ def hbm_peak():
         return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch recorded by an ncu capture summary under
-    profiles/ (line ``dram_bytes_per_launch: N``), or None."""
-    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
-    try:
-        txt = open(path).read()
-    except OSError:
-        return None
-    mt = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", txt)
-    return int(mt.group(1)) if mt else None
+def profile_traffic(workload: str):
+    """DRAM bytes per launch of the fused kernel recorded by the ncu capture
+    summary of this workload under profiles/ (line ``dram_bytes_per_launch:
+    N``), or None."""
+    import glob
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"*{workload}*.md"))):
+        with open(path) as f:
+            mt = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read())
+        if mt:
+            return int(mt.group(1))
+    return None
 
 
 class ClockSampler:
@@ -370,7 +371,7 @@ def main():
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
                          "mean_launch_ms": round(k_mean, 5),
-                         "traffic": profile_traffic("fused_decode", args.workload)},
+                         "traffic": profile_traffic(args.workload)},
             "kernels_ms": {"in_proj_gemm": round(float(gi_ms.mean()), 5),
                            "fused_decode": round(k_mean, 5),
                            "out_proj_gemm": round(float(go_ms.mean()), 5)},
