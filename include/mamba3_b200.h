@@ -135,6 +135,15 @@ int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
  * lifts the reference's R == 4 restriction (fused_full_decode.py:600). */
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream);
 
+/* Small-batch fp32 linear layer of the decode step's projections (in_proj /
+ * out_proj, nn.Linear without bias, src/models/mamba3.py:115,158, called at
+ * src/models/inference.py:489,553):  C[m, n] = sum_k A[m, k] * W[n, k].
+ * A: (M, K) row stride lda, W: (N, K) row stride ldw, C: (M, N) row stride
+ * ldc; fp32, 16-byte aligned bases, K, lda, ldw multiples of 4.  Tuned for
+ * M (the batch) up to a few hundred; fp32 accumulation. */
+int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
+                  int32_t M, int32_t N, int32_t K, m3_stream_t stream);
+
 /* Device-side error word of the library's kernels: 0, or a bit mask of
  * M3_DEVERR_* raised by a kernel that gave up a bounded wait (the kernel
  * then skipped its remaining work and returned).  Synchronises the device.

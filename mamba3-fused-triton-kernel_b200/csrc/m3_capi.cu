@@ -142,6 +142,19 @@ int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
   return full_entry(dims, args, stream, true);
 }
 
+int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc, int32_t M,
+                  int32_t N, int32_t K, m3_stream_t stream) {
+  if (!A || !W || !C) return M3_ERR_NULL;
+  if (M < 0 || N <= 0 || K <= 0 || lda < K || ldw < K || ldc < N) return M3_ERR_SHAPE;
+  if (K % 4 || lda % 4 || ldw % 4) return M3_ERR_ALIGN;
+  if (!aligned16(A) || !aligned16(W) || (reinterpret_cast<uintptr_t>(C) & 3u)) return M3_ERR_ALIGN;
+  if (M == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  return launch_status(
+      m3::launch_linear_small_m(A, lda, W, ldw, C, ldc, M, N, K, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int m3_device_error(int reset) {
   const int a = m3::siso_device_error(reset != 0);
   const int b = m3::mimo_device_error(reset != 0);

@@ -424,6 +424,8 @@ __global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
 cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
+cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
+                                  int M, int N, int K, cudaStream_t stream);
 
 // Device error words of the kernel translation units (read, optionally clear).
 int siso_device_error(bool reset);

@@ -1,0 +1,111 @@
+// Small-batch fp32 linear layer for the decode step's projections:
+//   C[m, n] = sum_k A[m, k] * W[n, k]      (A: M x K, W: N x K, both K-contiguous)
+// i.e. nn.Linear(x) = x @ W^T without bias, for M (the batch) up to a few
+// hundred rows.  At these sizes the GEMM is latency-bound, not FLOP-bound:
+// one CTA owns 16 output rows x 16 output columns; its 16 A rows of a K
+// chunk are staged in shared memory, each warp keeps the K-slices of its two
+// W rows in registers (lane l holds k = 4l + 128t), every load of a chunk is
+// issued before any is used, and the 32 partial sums of a warp (16 rows x 2
+// columns) are combined across lanes with one transpose-butterfly (31
+// shuffles) after which lane l owns output l.  Summation is in fp32.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "m3_kernels.cuh"
+
+namespace m3 {
+
+namespace {
+
+constexpr int kLinWarps = 8;            // 2 output columns per warp
+constexpr int kLinRows = 16;            // output rows per CTA
+constexpr int kLinCols = 2 * kLinWarps;  // output columns per CTA
+
+__device__ __forceinline__ float4 ldg4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+
+// Sum each of the 32 values over the warp; afterwards lane l holds the total
+// of v[l] (halving exchange at offsets 16, 8, 4, 2, 1).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int lvl = 0; lvl < 5; ++lvl) {
+    const int off = 16 >> lvl;
+    const int half = 16 >> lvl;  // live values after this level
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float send = upper ? v[q] : v[q + half];
+      const float keep = upper ? v[q + half] : v[q];
+      v[q] = keep + __shfl_xor_sync(kFullMask, send, off);
+    }
+  }
+  return v[0];
+}
+
+// KT float4 per lane per W row and chunk: a chunk spans KT * 128 columns.
+template <int KT>
+__global__ void __launch_bounds__(kLinWarps * 32) linear_small_m_kernel(const float *__restrict__ A, int64_t lda,
+                                                                        const float *__restrict__ W, int64_t ldw,
+                                                                        float *__restrict__ C, int64_t ldc, int M,
+                                                                        int N, int K) {
+  constexpr int KC = KT * 128;
+  __shared__ __align__(16) float4 As[kLinRows * KT * 32];  // [16 rows][KC / 4]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m0 = blockIdx.y * kLinRows;
+  const int n0 = blockIdx.x * kLinCols + 2 * warp;
+  const int mrows = min(kLinRows, M - m0);
+
+  float acc[32];  // acc[j * 16 + i]: row m0 + i, column n0 + j
+#pragma unroll
+  for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+
+  for (int kc = 0; kc < K; kc += KC) {
+    float4 w[2][KT];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int t = 0; t < KT; ++t) {
+        const int k = kc + 4 * lane + 128 * t;
+        w[j][t] = (n0 + j < N && k < K) ? ldg4(W + (int64_t)(n0 + j) * ldw + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    for (int v = tid; v < kLinRows * KT * 32; v += kLinWarps * 32) {
+      const int i = v / (KT * 32), k = kc + (v - i * (KT * 32)) * 4;
+      As[v] = (i < mrows && k < K) ? ldg4(A + (int64_t)(m0 + i) * lda + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kLinRows; ++i) {
+#pragma unroll
+      for (int t = 0; t < KT; ++t) {
+        const float4 a = As[i * (KT * 32) + lane + 32 * t];
+        acc[i] += a.x * w[0][t].x + a.y * w[0][t].y + a.z * w[0][t].z + a.w * w[0][t].w;
+        acc[16 + i] += a.x * w[1][t].x + a.y * w[1][t].y + a.z * w[1][t].z + a.w * w[1][t].w;
+      }
+    }
+    __syncthreads();
+  }
+  const float v = warp_transpose_sum32(acc);
+  const int i = lane & 15, j = lane >> 4;
+  if (i < mrows && n0 + j < N) C[(int64_t)(m0 + i) * ldc + n0 + j] = v;
+}
+
+template <int KT>
+cudaError_t launch_kt(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc, int M, int N,
+                      int K, cudaStream_t stream) {
+  const dim3 grid((unsigned)((N + kLinCols - 1) / kLinCols), (unsigned)((M + kLinRows - 1) / kLinRows));
+  linear_small_m_kernel<KT><<<grid, kLinWarps * 32, 0, stream>>>(A, lda, W, ldw, C, ldc, M, N, K);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
+                                  int M, int N, int K, cudaStream_t stream) {
+  if (K <= 128) return launch_kt<1>(A, lda, W, ldw, C, ldc, M, N, K, stream);
+  if (K <= 256) return launch_kt<2>(A, lda, W, ldw, C, ldc, M, N, K, stream);
+  if (K <= 384) return launch_kt<3>(A, lda, W, ldw, C, ldc, M, N, K, stream);
+  return launch_kt<4>(A, lda, W, ldw, C, ldc, M, N, K, stream);
+}
+
+}  // namespace m3

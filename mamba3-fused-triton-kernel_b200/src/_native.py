@@ -89,6 +89,9 @@ def load(path: str = LIB_PATH):
             fn = getattr(lib, name)
             fn.argtypes = [POINTER(Dims), POINTER(argt), c_void_p]
             fn.restype = c_int
+        lib.m3_linear_f32.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                      c_int32, c_int32, c_int32, c_void_p]
+        lib.m3_linear_f32.restype = c_int
         lib.m3_device_error.argtypes = [c_int]
         lib.m3_device_error.restype = c_int
         lib.m3_selftest_wait_timeout.argtypes = [c_void_p]

@@ -6,7 +6,8 @@
 
   use_triton_full_fused  in_proj -> ONE fused CUDA kernel -> out_proj
                          (the kernel updates ssm_state, bx_prev and
-                         angle_state in place)
+                         angle_state in place; small fp32 batches run both
+                         projections on the library's small-batch GEMM)
   use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
                          kernel -> out_proj
   use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
@@ -39,6 +40,7 @@ import torch.nn.functional as F
 
 from src import _native
 from src.kernels import _launch
+from src.kernels.linear import linear
 from src.kernels.mimo_decode import mamba3_mimo_decode_triton
 from src.kernels.mimo_decode_fused import mamba3_mimo_decode_fused_triton
 from src.kernels.siso_decode import mamba3_siso_decode_triton
@@ -199,14 +201,14 @@ class Mamba3Decoder:
         src/models/inference.py:476-559).  The kernel writes its gated output
         in the weight dtype, which is what out_proj consumes."""
         m = self.model
-        zx = m.in_proj(u)
+        zx = linear(u, m.in_proj.weight)
         if zx.dtype not in (torch.float32, torch.bfloat16) or zx.stride(1) != 1:
             zx = zx.float().contiguous()
         w_dtype = m.out_proj.weight.dtype
         y_dtype = w_dtype if w_dtype in (torch.float32, torch.bfloat16) else torch.float32
         y = torch.empty(u.shape[0], m.d_inner, device=u.device, dtype=y_dtype)
         self._fused_launch(state).run(zx, y)
-        out = m.out_proj(y.to(u.dtype))
+        out = linear(y.to(u.dtype), m.out_proj.weight)
         return out, state
 
     def _prep_projections(self, u: torch.Tensor, state: dict):

@@ -31,7 +31,7 @@ def _declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 10, names
+    assert len(names) == 11, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
@@ -152,6 +152,17 @@ def test_validation_full_fused():
     a.param_dtype = nat.M3_F32
     dims.batch = 0  # empty batch: valid, nothing enqueued
     assert lib.m3_mimo_full_fused(dims, a, None) == nat.M3_OK
+
+
+def test_validation_linear():
+    lib = nat.load()
+    fake = 0x7000_0000_0000
+    ok = (fake, 256, fake + 4096, 256, fake + 8192, 64, 8, 64, 256, None)
+    assert lib.m3_linear_f32(None, *ok[1:]) == nat.M3_ERR_NULL
+    assert lib.m3_linear_f32(fake, 255, fake + 4096, 256, fake + 8192, 64, 8, 64, 256, None) == nat.M3_ERR_SHAPE
+    assert lib.m3_linear_f32(fake, 258, fake + 4096, 258, fake + 8192, 64, 8, 64, 258, None) == nat.M3_ERR_ALIGN
+    assert lib.m3_linear_f32(fake + 4, *ok[1:]) == nat.M3_ERR_ALIGN
+    assert lib.m3_linear_f32(fake, 256, fake + 4096, 256, fake + 8192, 64, 0, 64, 256, None) == nat.M3_OK
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")

@@ -1,0 +1,51 @@
+"""GPU checks of the small-batch projection kernel (``m3_linear_f32``):
+x @ W^T against a float64 product, over batch sizes, widths and depths that
+do and do not fill the 16 x 16 CTA tile and the 128-wide K slices, strided
+rows, and the size-based dispatch to cuBLAS."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from src.kernels.linear import SMALL_M_MAX, linear, uses_small_m_kernel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 100, 128, 256])
+@pytest.mark.parametrize("N,K", [(1600, 256), (256, 512), (1, 4), (3, 100), (257, 128), (48, 1024), (40, 2048)])
+def test_matches_float64(M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M * 1000 + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.05
+    assert uses_small_m_kernel(x, w)
+    y = linear(x, w)
+    ref = (x.double() @ w.double().T).float()
+    torch.testing.assert_close(y, ref, rtol=2e-5, atol=2e-5 * K ** 0.5)
+
+
+def test_strided_rows_and_views():
+    x_big = torch.randn(64, 300, device="cuda")
+    x = x_big[:, :256]  # row stride 300
+    w_big = torch.randn(96, 260, device="cuda")
+    w = w_big[:, :256]
+    assert uses_small_m_kernel(x, w)
+    torch.testing.assert_close(linear(x, w), (x.double() @ w.double().T).float(), rtol=2e-5, atol=4e-4)
+
+
+def test_dispatch_to_cublas_outside_the_small_batch_regime():
+    w = torch.randn(64, 128, device="cuda")
+    big = torch.randn(SMALL_M_MAX + 1, 128, device="cuda")
+    assert not uses_small_m_kernel(big, w)
+    torch.testing.assert_close(linear(big, w), big @ w.T)
+    xb = torch.randn(8, 128, device="cuda").bfloat16()
+    assert not uses_small_m_kernel(xb, w.bfloat16())
+    torch.testing.assert_close(linear(xb, w.bfloat16()), xb @ w.bfloat16().T)
+    odd = torch.randn(8, 130, device="cuda")
+    assert not uses_small_m_kernel(odd, torch.randn(4, 130, device="cuda"))
+
+
+def test_empty_batch():
+    out = linear(torch.zeros(0, 256, device="cuda"), torch.randn(32, 256, device="cuda"))
+    assert out.shape == (0, 32)
