@@ -144,6 +144,16 @@ int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
 int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
                   int32_t M, int32_t N, int32_t K, m3_stream_t stream);
 
+/* Residual add + RMSNorm between the blocks of a stack (x <- x +
+ * mixer(RMSNorm(x)), src/models/mamba3.py:412-421 with RMSNorm :26-36):
+ *   x_out = x + o            (o may be NULL: x_out = x; x_out may be NULL)
+ *   xn    = x_out / sqrt(mean(x_out^2) + eps) * w   (xn may be NULL)
+ * x, o, x_out, xn: (M, N) rows of `dtype` (f32 or bf16; the add rounds to
+ * dtype like torch's add), w: (N,) f32.  N <= 8192.  One launch. */
+int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o, int64_t ldo,
+                        const float *w, void *x_out, int64_t ldxo, void *xn, int64_t ldn,
+                        int32_t M, int32_t N, float eps, m3_stream_t stream);
+
 /* Device-side error word of the library's kernels: 0, or a bit mask of
  * M3_DEVERR_* raised by a kernel that gave up a bounded wait (the kernel
  * then skipped its remaining work and returned).  Synchronises the device.

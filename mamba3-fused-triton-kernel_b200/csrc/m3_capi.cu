@@ -155,6 +155,21 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
       m3::launch_linear_small_m(A, lda, W, ldw, C, ldc, M, N, K, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o, int64_t ldo, const float *w,
+                        void *x_out, int64_t ldxo, void *xn, int64_t ldn, int32_t M, int32_t N, float eps,
+                        m3_stream_t stream) {
+  if (!x || (xn && !w) || (!x_out && !xn)) return M3_ERR_NULL;
+  if (!dtype_ok(dtype)) return M3_ERR_DTYPE;
+  if (M < 0 || N <= 0 || N > m3::residual_rmsnorm_max_width() || ldx < N || (o && ldo < N) ||
+      (x_out && ldxo < N) || (xn && ldn < N))
+    return M3_ERR_SHAPE;
+  if (M == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  return launch_status(m3::launch_residual_rmsnorm(dtype, x, o, w, x_out, xn, M, N, ldx, ldo, ldxo, ldn, eps,
+                                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int m3_device_error(int reset) {
   const int a = m3::siso_device_error(reset != 0);
   const int b = m3::mimo_device_error(reset != 0);

@@ -27,6 +27,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "mamba3_b200.h"
 
 namespace m3 {
@@ -58,6 +60,40 @@ struct KParams {
   float *h, *bx, *ang;
   void *y; int64_t y_sb, y_sh, y_sp; int y_dt;
 };
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch
+// ---------------------------------------------------------------------------
+// Every kernel of the library is launched with programmatic stream
+// serialisation: it may start while the preceding kernel on the stream is
+// still running.  Before reading anything that kernel produces (the in_proj
+// output, the projection input) it executes pdl_wait(), which returns once
+// the preceding grid has completed and its writes are visible; it calls
+// pdl_wait() before pdl_trigger(), so a kernel's completion implies the
+// completion of everything before it, and data written two or more kernels
+// back (the carried state) may be read before the wait.  Without a
+// preceding dependent launch both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch `kernel` with programmatic stream serialisation.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
 
 // ---------------------------------------------------------------------------
 // scalar helpers
@@ -230,6 +266,9 @@ __global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
       for (int e = 0; e < VW; ++e) hv[f][e] = bv[f][e] = 0.f;
     }
   }
+
+  pdl_wait();
+  pdl_trigger();
 
   if constexpr (FULL) {
     // RMSNorm of the R B-rows and R C-rows of this batch row, shared by
@@ -424,6 +463,10 @@ __global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
 cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
+cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
+                                    int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,
+                                    cudaStream_t stream);
+int residual_rmsnorm_max_width();
 cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
                                   int M, int N, int K, cudaStream_t stream);
 

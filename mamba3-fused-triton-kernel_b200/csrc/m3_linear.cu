@@ -69,6 +69,10 @@ __global__ void __launch_bounds__(kLinWarps * 32) linear_small_m_kernel(const fl
         const int k = kc + 4 * lane + 128 * t;
         w[j][t] = (n0 + j < N && k < K) ? ldg4(W + (int64_t)(n0 + j) * ldw + k) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+    if (kc == 0) {  // the weights are in flight; A is produced by the preceding kernel
+      pdl_wait();
+      pdl_trigger();
+    }
     for (int v = tid; v < kLinRows * KT * 32; v += kLinWarps * 32) {
       const int i = v / (KT * 32), k = kc + (v - i * (KT * 32)) * 4;
       As[v] = (i < mrows && k < K) ? ldg4(A + (int64_t)(m0 + i) * lda + k) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -94,8 +98,8 @@ template <int KT>
 cudaError_t launch_kt(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc, int M, int N,
                       int K, cudaStream_t stream) {
   const dim3 grid((unsigned)((N + kLinCols - 1) / kLinCols), (unsigned)((M + kLinRows - 1) / kLinRows));
-  linear_small_m_kernel<KT><<<grid, kLinWarps * 32, 0, stream>>>(A, lda, W, ldw, C, ldc, M, N, K);
-  return cudaGetLastError();
+  return launch_pdl(linear_small_m_kernel<KT>, grid, dim3(kLinWarps * 32), 0, stream, A, lda, W, ldw, C, ldc, M, N,
+                    K);
 }
 
 }  // namespace

@@ -142,8 +142,9 @@ __global__ void __launch_bounds__(kRowWarps * 32, 4) mimo_row_kernel(const KPara
   const T *zx = static_cast<const T *>(p.zx);
   const int so = 2 * p.d_inner + 2 * p.d_bc;  // dd_dt[H] dd_A[H] trap[H] angle[A]
 
-  auto load_row = [&](int b, RR &r) {
-    const T *row = zx + (int64_t)b * p.zx_sb;
+  // state and angle state: written by the previous step's kernel (two or
+  // more launches back), safe to read before pdl_wait()
+  auto load_state = [&](int b, RR &r) {
     const int64_t sbase = ((int64_t)b * H + hh) * D;
 #pragma unroll
     for (int f = 0; f < F; ++f) {
@@ -153,6 +154,16 @@ __global__ void __launch_bounds__(kRowWarps * 32, 4) mimo_row_kernel(const KPara
         ld_vec<VW>(p.bx + sbase + col, r.bx[f]);
       }
     }
+#pragma unroll
+    for (int n = 0; n < NA; ++n) {
+      const int i = tid + n * kRowWarps * 32;
+      const int w = i / A, a = i - w * A;
+      if (w < kRowWarps) r.ang[n] = p.ang[((int64_t)b * H + h0 + w) * A + a];
+    }
+  };
+  // the in_proj row: produced by the preceding kernel, read after pdl_wait()
+  auto load_zx = [&](int b, RR &r) {
+    const T *row = zx + (int64_t)b * p.zx_sb;
 #pragma unroll
     for (int k = 0; k < KP; ++k) {
       const int pp = lane + 32 * k;
@@ -177,16 +188,17 @@ __global__ void __launch_bounds__(kRowWarps * 32, 4) mimo_row_kernel(const KPara
     for (int n = 0; n < NA; ++n) {
       const int i = tid + n * kRowWarps * 32;
       const int w = i / A, a = i - w * A;
-      if (w < kRowWarps) {
-        r.ang[n] = p.ang[((int64_t)b * H + h0 + w) * A + a];
-        r.araw[n] = ldg_f(row + so + 3 * H + a);
-      }
+      if (w < kRowWarps) r.araw[n] = ldg_f(row + so + 3 * H + a);
     }
   };
 
   RR cur;
+  if (b0 < b1) load_state(b0, cur);
+  pdl_wait();
+  pdl_trigger();
   for (int b = b0; b < b1; ++b) {
-    load_row(b, cur);
+    if (b != b0) load_state(b, cur);
+    load_zx(b, cur);
     const T *row = zx + (int64_t)b * p.zx_sb;
     float *wk = smem + ((b - b0) & 1) * wstride;
     float *nBC = wk, *wsc = wk + 2 * R * BD, *wrot = wsc + 4 * kRowWarps;
@@ -413,8 +425,7 @@ cudaError_t launch_row_kp(const KParams &kp, cudaStream_t stream) {
   int rows = (int)((items + slots - 1) / slots);
   if (rows < 1) rows = 1;
   const int64_t grid = (int64_t)ngrp * ((kp.B + rows - 1) / rows);
-  kern<<<(unsigned)grid, kRowWarps * 32, smem, stream>>>(kp, rows);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3((unsigned)grid), dim3(kRowWarps * 32), smem, stream, kp, rows);
 }
 
 template <int BD, int R, typename T>
@@ -437,16 +448,14 @@ cudaError_t launch_full_t(const KParams &kp, cudaStream_t stream) {
   const int ngrp = (kp.H + kp.heads_per_cta - 1) / kp.heads_per_cta;
   const unsigned grid = (unsigned)((int64_t)kp.B * ngrp);
   const size_t smem = (size_t)2 * R * BD * sizeof(float);
-  mimo_decode_kernel<BD, R, true><<<grid, kp.heads_per_cta * 32, smem, stream>>>(kp);
-  return cudaGetLastError();
+  return launch_pdl(mimo_decode_kernel<BD, R, true>, dim3(grid), dim3(kp.heads_per_cta * 32), smem, stream, kp);
 }
 
 template <int BD, int R>
 cudaError_t launch_ssm_t(const KParams &kp, cudaStream_t stream) {
   const int ngrp = (kp.H + kp.heads_per_cta - 1) / kp.heads_per_cta;
   const unsigned grid = (unsigned)((int64_t)kp.B * ngrp);
-  mimo_decode_kernel<BD, R, false><<<grid, kp.heads_per_cta * 32, 0, stream>>>(kp);
-  return cudaGetLastError();
+  return launch_pdl(mimo_decode_kernel<BD, R, false>, dim3(grid), dim3(kp.heads_per_cta * 32), 0, stream, kp);
 }
 
 template <int BD>

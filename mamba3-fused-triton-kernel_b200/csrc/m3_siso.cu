@@ -243,7 +243,33 @@ __global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams
   }
   __syncthreads();
 
-  auto issue = [&](int k) {
+  const int es_z = sizeof(T), pes_p = p.par_dt == M3_BF16 ? 2 : 4;
+  auto header_bytes = [&]() -> uint32_t {
+    return 2u * D * es_z + 2u * P * es_z + (uint32_t)(3 * p.H + p.A) * es_z + (uint32_t)p.A * 4 +
+           2u * D * pes_p;
+  };
+  auto issue_header = [&](int k) {
+    const int t = tile_of(k);
+    const int b = t / p.H, hh = t - b * p.H;
+    const uint32_t bar = smem_addr(&bars[k % sp.nstage]);
+    unsigned char *st = ring + (size_t)(k % sp.nstage) * sp.stage_bytes;
+    const T *row = static_cast<const T *>(p.zx) + (int64_t)b * p.zx_sb;
+    const uint32_t n_raw = 2u * D * es_z, n_xz = (uint32_t)P * es_z, n_scal = (uint32_t)(3 * p.H + p.A) * es_z;
+    const uint32_t n_ang = (uint32_t)p.A * 4, n_bias = (uint32_t)D * pes_p;
+    bulk_g2s(smem_addr(st + sp.o_raw), row + 2 * p.d_inner, n_raw, bar);
+    bulk_g2s(smem_addr(st + sp.o_x), row + p.d_inner + (int64_t)hh * P, n_xz, bar);
+    bulk_g2s(smem_addr(st + sp.o_z), row + (int64_t)hh * P, n_xz, bar);
+    bulk_g2s(smem_addr(st + sp.o_scal), row + 2 * p.d_inner + 2 * p.d_bc, n_scal, bar);
+    bulk_g2s(smem_addr(st + sp.o_ang), p.ang + (int64_t)t * p.A, n_ang, bar);
+    bulk_g2s(smem_addr(st + sp.o_bb), static_cast<const unsigned char *>(p.bB) + (size_t)hh * n_bias, n_bias, bar);
+    bulk_g2s(smem_addr(st + sp.o_bc), static_cast<const unsigned char *>(p.bC) + (size_t)hh * n_bias, n_bias, bar);
+  };
+  // Chunk k of this CTA into stage k % nstage: the state chunk and, for the
+  // first chunk of a tile on the staged path, the tile header.  The header
+  // comes from the in_proj output (the preceding kernel's product), so the
+  // first stages' headers are issued after pdl_wait() (with_header false
+  // arms the barrier for them but leaves their copies to issue_header).
+  auto issue = [&](int k, bool with_header) {
     const int t = tile_of(k);
     if (t >= ntiles) return;
     const int c = k % sp.nchunk;
@@ -256,32 +282,17 @@ __global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams
     unsigned char *st = ring + (size_t)s * sp.stage_bytes;
     uint32_t tx = 2 * bytes;
     if constexpr (STAGED) {
-      if (c == 0) {
-        const int b = t / p.H, hh = t - b * p.H, H = p.H;
-        const T *row = static_cast<const T *>(p.zx) + (int64_t)b * p.zx_sb;
-        const uint32_t es = sizeof(T), pes = p.par_dt == M3_BF16 ? 2 : 4;
-        const uint32_t n_raw = 2u * D * es, n_xz = (uint32_t)P * es, n_scal = (uint32_t)(3 * H + p.A) * es;
-        const uint32_t n_ang = (uint32_t)p.A * 4, n_bias = (uint32_t)D * pes;
-        tx += n_raw + 2 * n_xz + n_scal + n_ang + 2 * n_bias;
-        mbar_arrive_expect_tx(bar, tx);
-        bulk_g2s(smem_addr(st + sp.o_raw), row + 2 * p.d_inner, n_raw, bar);
-        bulk_g2s(smem_addr(st + sp.o_x), row + p.d_inner + (int64_t)hh * P, n_xz, bar);
-        bulk_g2s(smem_addr(st + sp.o_z), row + (int64_t)hh * P, n_xz, bar);
-        bulk_g2s(smem_addr(st + sp.o_scal), row + 2 * p.d_inner + 2 * p.d_bc, n_scal, bar);
-        bulk_g2s(smem_addr(st + sp.o_ang), p.ang + (int64_t)t * p.A, n_ang, bar);
-        bulk_g2s(smem_addr(st + sp.o_bb), static_cast<const unsigned char *>(p.bB) + (size_t)hh * n_bias, n_bias, bar);
-        bulk_g2s(smem_addr(st + sp.o_bc), static_cast<const unsigned char *>(p.bC) + (size_t)hh * n_bias, n_bias, bar);
-      } else {
-        mbar_arrive_expect_tx(bar, tx);
-      }
-    } else {
-      mbar_arrive_expect_tx(bar, tx);
+      if (c == 0) tx += header_bytes();
     }
+    mbar_arrive_expect_tx(bar, tx);
     bulk_g2s(smem_addr(st + sp.o_h), p.h + goff, bytes, bar);
     bulk_g2s(smem_addr(st + sp.o_bx), p.bx + goff, bytes, bar);
+    if constexpr (STAGED) {
+      if (c == 0 && with_header) issue_header(k);
+    }
   };
   if (tid == 0)
-    for (int k = 0; k < sp.nstage; ++k) issue(k);
+    for (int k = 0; k < sp.nstage; ++k) issue(k, false);
 
   if constexpr (FULL) {  // per-CTA constants: norm weights, dt_bias, D
     for (int i = tid; i < D; i += blockDim.x) {
@@ -292,8 +303,15 @@ __global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams
       q.dtb[i] = ld_any(p.dt_bias, i, p.par_dt);
       q.dsk[i] = ld_any(p.Dp, i, p.par_dt);
     }
-    __syncthreads();
   }
+  pdl_wait();
+  pdl_trigger();
+  if constexpr (STAGED) {
+    if (tid == 0)
+      for (int k = 0; k < sp.nstage; ++k)
+        if (tile_of(k) < ntiles && k % sp.nchunk == 0) issue_header(k);
+  }
+  __syncthreads();
 
   int k = 0;
   for (;; ++k) {
@@ -365,7 +383,7 @@ __global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams
       }
     }
     __syncthreads();  // stage s and the tile parameters are free again
-    if (tid == 0) issue(k + sp.nstage);
+    if (tid == 0) issue(k + sp.nstage, true);
   }
   // Normal exit: every issued chunk was consumed.  After a lost copy, wait
   // (bounded) for whatever this CTA still has in flight before leaving.
@@ -459,8 +477,7 @@ cudaError_t launch_t(const KParams &kp, cudaStream_t stream) {
   const int ntiles = kp.B * kp.H;
   int grid = num_sms() * last_per_sm;
   if (grid > ntiles) grid = ntiles;
-  kern<<<grid, kSisoThreads, smem, stream>>>(kp, sp);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(kSisoThreads), (size_t)smem, stream, kp, sp);
 }
 
 template <int BD>

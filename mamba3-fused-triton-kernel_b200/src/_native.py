@@ -92,6 +92,10 @@ def load(path: str = LIB_PATH):
         lib.m3_linear_f32.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                       c_int32, c_int32, c_int32, c_void_p]
         lib.m3_linear_f32.restype = c_int
+        lib.m3_residual_rmsnorm.argtypes = [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+                                            c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
+                                            c_float, c_void_p]
+        lib.m3_residual_rmsnorm.restype = c_int
         lib.m3_device_error.argtypes = [c_int]
         lib.m3_device_error.restype = c_int
         lib.m3_selftest_wait_timeout.argtypes = [c_void_p]

@@ -67,6 +67,28 @@ def load_params(model, params: dict) -> None:
                            for k, v in sd.items()})
 
 
+def build_stack(meta, device=None, dtype=None):
+    """The residual-stack fixture's blocks (tests/golden/make_golden.py
+    STACK_CASES): per layer synthetic parameters from seed + 1 + l and norm
+    weights 1 + 0.2 N(0, 1) from the case seed."""
+    import torch
+    from oracle import mamba3_oracle as orc
+    from src.models.mamba3 import MambaBlock
+    dims = orc.layer_dims(**layer_kwargs(meta["layer"]))
+    rng = np.random.default_rng(meta["seed"])
+    blocks, oracle_layers = [], []
+    kw = {k: v for k, v in layer_kwargs(meta["layer"]).items() if k != "d_model"}
+    for l in range(meta["layers"]):
+        params = orc.synthetic_params(dims, meta["seed"] + 1 + l, bf16=meta["bf16"])
+        w = (1.0 + 0.2 * rng.standard_normal(dims["d_model"])).astype(np.float32)
+        blk = MambaBlock(dims["d_model"], kw, device=device, dtype=dtype)
+        load_params(blk.mixer, params)
+        blk.norm.weight.data.copy_(torch.from_numpy(w))
+        blocks.append(blk)
+        oracle_layers.append((params, w))
+    return dims, blocks, oracle_layers
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

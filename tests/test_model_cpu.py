@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden_names, layer_kwargs, load_golden, load_params
+from conftest import build_stack, golden_names, layer_kwargs, load_golden, load_params
 from oracle import mamba3_oracle as orc
 from src.kernels import utils as ku
 from src.models.inference import Mamba3Decoder
@@ -100,3 +100,20 @@ def test_pytorch_backend_needs_no_device():
     dec.warmup_cuda_graph(st)  # no-op without a CUDA backend
     out, st = dec.step(torch.randn(3, 64), st)
     assert out.shape == (3, 64)
+
+
+@pytest.mark.parametrize("name", golden_names("stack"))
+def test_stack_decoder_pytorch_matches_reference(name):
+    """The stack decoder's PyTorch path reproduces the reference's own
+    residual composition (tests/golden/stack3_*)."""
+    from src.models.stack import Mamba3StackDecoder
+    g = load_golden(name)
+    m = g["meta"]
+    dtype = torch.bfloat16 if m["bf16"] else torch.float32
+    dims, blocks, _ = build_stack(m, dtype=dtype)
+    dec = Mamba3StackDecoder(blocks, use_triton=False)
+    st = dec.init_state(m["batch"])
+    u = orc.synthetic_inputs(dims, m["batch"], m["steps"], m["seed"] + 100, bf16=m["bf16"])
+    with torch.no_grad():
+        outs = [dec.step(torch.from_numpy(u[t]).to(dtype), st)[0].float().numpy() for t in range(m["steps"])]
+    np.testing.assert_allclose(np.stack(outs), g["out"], rtol=1e-2, atol=1e-2)
