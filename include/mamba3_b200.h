@@ -41,7 +41,8 @@ enum {
   M3_ERR_DTYPE = 4,  /* unsupported dtype code                             */
   M3_ERR_ALIGN = 5,  /* state not contiguous / not 16-byte aligned         */
   M3_ERR_LAUNCH = 6, /* the CUDA launch itself failed                      */
-  M3_ERR_DEVICE = 7  /* no usable CUDA device                              */
+  M3_ERR_DEVICE = 7, /* no usable CUDA device                              */
+  M3_ERR_UNSUPPORTED = 8 /* valid layer the single-launch step does not take */
 };
 
 /* Element type codes. */
@@ -143,6 +144,52 @@ int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
  * M (the batch) up to a few hundred; fp32 accumulation. */
 int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
                   int32_t M, int32_t N, int32_t K, m3_stream_t stream);
+
+/* Arguments of the single-launch decode step (m3_mimo_step).
+ *   dtype        M3_F32 or M3_BF16: u, both projection weights, the per-head
+ *                parameters (as in m3_full_args), out and the workspace's
+ *                intermediates; accumulation is fp32
+ *   u            (B, d_model) row stride u_stride_b
+ *   in_proj_w    (d_in_proj, d_model) row stride in_proj_stride
+ *   out_proj_w   (d_model, d_inner) row stride out_proj_stride
+ *   ssm_state, bx_prev, angle_state   as in m3_full_args, in place
+ *   out          (B, d_model) row stride out_stride_b
+ *   workspace    device scratch of at least m3_mimo_step_workspace_bytes,
+ *                256-byte aligned, ZEROED ONCE before its first use and then
+ *                left to the library (it holds the in_proj output, the gated
+ *                output and grid-barrier counters that each launch returns to
+ *                zero).  One workspace per concurrently running launch.
+ * d_model, row strides and the weights' row strides multiples of 4; u and
+ * the weights 16-byte (f32) / 8-byte (bf16) aligned. */
+typedef struct m3_step_args {
+  int32_t d_model;
+  int32_t dtype;
+  const void *u;           int64_t u_stride_b;
+  const void *in_proj_w;   int64_t in_proj_stride;
+  const void *out_proj_w;  int64_t out_proj_stride;
+  const void *dt_bias, *D, *B_norm_w, *C_norm_w, *B_bias, *C_bias, *mimo_x, *mimo_o;
+  float *ssm_state;
+  float *bx_prev;
+  float *angle_state;
+  void *out;               int64_t out_stride_b;
+  void *workspace;         int64_t workspace_bytes;
+} m3_step_args;
+
+/* Workspace bytes m3_mimo_step needs for this layer and batch, or the
+ * negated status (-M3_ERR_*) when the call would be rejected;
+ * -M3_ERR_UNSUPPORTED for a valid layer outside the single-launch kernel's
+ * range (nheads not a multiple of 8, headdim > 128, d_state > 128, d_model
+ * or d_inner not a multiple of 4), which the three-launch path serves. */
+int64_t m3_mimo_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32_t dtype);
+
+/* The whole decode step of one MIMO layer in ONE launch: in_proj, the
+ * full-step fused update and out_proj (the sequence of
+ * Mamba3Decoder._step_triton_full_fused, src/models/inference.py:476-559,
+ * whose projections are nn.Linear without bias, src/models/mamba3.py:
+ * 115,158).  A cooperative launch (all CTAs resident) with two grid-wide
+ * barriers; no counterpart kernel in the reference, whose step is three
+ * launches. */
+int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream);
 
 /* Residual add + RMSNorm between the blocks of a stack (x <- x +
  * mixer(RMSNorm(x)), src/models/mamba3.py:412-421 with RMSNorm :26-36):

@@ -6,12 +6,13 @@
 #include <cstdint>
 
 #include "m3_kernels.cuh"
+#include "m3_step.cuh"
 
 namespace {
 
 using m3::KParams;
 
-constexpr int kVersion = 10100;  // 1.1.0
+constexpr int kVersion = 10200;  // 1.2.0
 constexpr int kMaxHeaddim = 4096;
 
 bool dtype_ok(int32_t dt) { return dt == M3_F32 || dt == M3_BF16; }
@@ -114,6 +115,130 @@ int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool
   return launch_status(mimo ? m3::launch_mimo(kp, true, s) : m3::launch_siso(kp, true, s));
 }
 
+bool aligned_to(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Workspace layout of the single-launch step: barrier counters, the in_proj
+// output (row stride rounded up to 4 elements), the gated output.
+struct StepLayout {
+  int64_t ldzx, zx_off, y_off, bytes;
+};
+
+StepLayout step_layout(const m3_dims *d, int64_t d_in_proj, int es) {
+  StepLayout L;
+  L.ldzx = round_up(d_in_proj, 4);
+  L.zx_off = m3::kStepBarBytes;
+  L.y_off = L.zx_off + round_up((int64_t)d->batch * L.ldzx * es, 256);
+  L.bytes = L.y_off + round_up((int64_t)d->batch * d->d_inner * es, 256);
+  return L;
+}
+
+// Shape checks of the single-launch step; M3_ERR_UNSUPPORTED for a valid
+// layer the kernel does not take.
+int check_step_dims(const m3_dims *d, int32_t d_model, int32_t dtype) {
+  int st = check_dims(d, true);
+  if (st != M3_OK) return st;
+  if (!dtype_ok(dtype)) return M3_ERR_DTYPE;
+  if (d->ngroups != 1 || d->d_inner != d->nheads * d->headdim || d_model <= 0) return M3_ERR_SHAPE;
+  if (d->num_rope_angles <= 0 || 2 * d->num_rope_angles > d->d_state) return M3_ERR_SHAPE;
+  if (d->nheads % 8 != 0 || d->headdim > 128 || d->d_state > 128 || d_model % 4 != 0 || d->d_inner % 4 != 0)
+    return M3_ERR_UNSUPPORTED;
+  return M3_OK;
+}
+
+// Append an L2 prefetch range (trimmed to 16-byte boundaries; at most
+// kMaxPrefetchChunks 4 KB chunks in all, one per thread of the grid).
+void add_prefetch(m3::StepParams &sp, const void *p, int64_t bytes) {
+  constexpr int64_t kChunk = 4096, kMaxPrefetchChunks = 148 * 256;
+  if (!p || bytes <= 0 || sp.n_prefetch >= m3::kStepMaxPrefetch) return;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t lo = (a + 15) & ~uintptr_t(15);
+  const uintptr_t hi = (a + (uintptr_t)bytes) & ~uintptr_t(15);
+  if (hi <= lo) return;
+  const int first = sp.pf_first[sp.n_prefetch];
+  int64_t len = (int64_t)(hi - lo);
+  if (first + (len + kChunk - 1) / kChunk > kMaxPrefetchChunks) len = (kMaxPrefetchChunks - first) * kChunk;
+  if (len <= 0) return;
+  sp.pf_ptr[sp.n_prefetch] = reinterpret_cast<const void *>(lo);
+  sp.pf_bytes[sp.n_prefetch] = len;
+  sp.pf_first[sp.n_prefetch + 1] = first + (int)((len + kChunk - 1) / kChunk);
+  ++sp.n_prefetch;
+}
+
+int64_t step_workspace_bytes(const m3_dims *d, int32_t d_model, int32_t dtype) {
+  const int st = check_step_dims(d, d_model, dtype);
+  if (st != M3_OK) return -(int64_t)st;
+  const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * d->mimo_rank + 3LL * d->nheads + d->num_rope_angles;
+  return step_layout(d, d_in_proj, dtype == M3_BF16 ? 2 : 4).bytes;
+}
+
+int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
+  if (!d || !a) return M3_ERR_NULL;
+  int st = check_step_dims(d, a->d_model, a->dtype);
+  if (st != M3_OK) return st;
+  if (!a->u || !a->in_proj_w || !a->out_proj_w || !a->dt_bias || !a->D || !a->B_norm_w || !a->C_norm_w ||
+      !a->B_bias || !a->C_bias || !a->mimo_x || !a->mimo_o || !a->ssm_state || !a->bx_prev || !a->angle_state ||
+      !a->out || !a->workspace)
+    return M3_ERR_NULL;
+  const int es = a->dtype == M3_BF16 ? 2 : 4;
+  const int R = d->mimo_rank;
+  const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * R + 3LL * d->nheads + d->num_rope_angles;
+  if (a->u_stride_b < a->d_model || a->in_proj_stride < a->d_model || a->out_proj_stride < d->d_inner ||
+      a->out_stride_b < a->d_model)
+    return M3_ERR_SHAPE;
+  const StepLayout L = step_layout(d, d_in_proj, es);
+  if (a->workspace_bytes < L.bytes) return M3_ERR_SHAPE;
+  const unsigned va = (unsigned)(4 * es);  // a 4-element vector
+  if (a->u_stride_b % 4 || a->in_proj_stride % 4 || a->out_proj_stride % 4) return M3_ERR_ALIGN;
+  if (!aligned_to(a->u, va) || !aligned_to(a->in_proj_w, va) || !aligned_to(a->out_proj_w, va) ||
+      !aligned_to(a->B_bias, va) || !aligned_to(a->C_bias, va) || !aligned_to(a->workspace, 256) ||
+      !aligned16(a->ssm_state) || !aligned16(a->bx_prev) || !aligned_to(a->angle_state, 4))
+    return M3_ERR_ALIGN;
+  if (d->batch == 0) return M3_OK;
+  st = check_device();
+  if (st != M3_OK) return st;
+  int dev = 0, coop = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) {
+    cudaGetLastError();
+    return M3_ERR_DEVICE;
+  }
+
+  char *ws = static_cast<char *>(a->workspace);
+  m3::StepParams sp = {};
+  KParams &kp = sp.kp;
+  kp.B = d->batch; kp.H = d->nheads; kp.P = d->headdim; kp.D = d->d_state; kp.R = R;
+  kp.A = d->num_rope_angles; kp.A_floor = d->A_floor;
+  kp.d_inner = d->d_inner; kp.d_bc = d->d_state * R;
+  kp.heads_per_cta = m3::mimo_heads_per_cta(kp.H);
+  kp.zx = ws + L.zx_off; kp.zx_sb = L.ldzx; kp.zx_dt = a->dtype; kp.par_dt = a->dtype;
+  kp.dt_bias = a->dt_bias; kp.Dp = a->D; kp.wB = a->B_norm_w; kp.wC = a->C_norm_w;
+  kp.bB = a->B_bias; kp.bC = a->C_bias; kp.mx = a->mimo_x; kp.mo = a->mimo_o;
+  kp.h = a->ssm_state; kp.bx = a->bx_prev; kp.ang = a->angle_state;
+  kp.y = ws + L.y_off; kp.y_sb = d->d_inner; kp.y_sh = d->headdim; kp.y_sp = 1; kp.y_dt = a->dtype;
+  sp.g_in = {a->u, a->u_stride_b, a->in_proj_w, a->in_proj_stride, ws + L.zx_off, L.ldzx,
+             d->batch, (int)d_in_proj, a->d_model};
+  sp.g_out = {ws + L.y_off, d->d_inner, a->out_proj_w, a->out_proj_stride, a->out, a->out_stride_b,
+              d->batch, a->d_model, d->d_inner};
+  sp.bar = reinterpret_cast<unsigned *>(ws);
+
+  const int64_t S = (int64_t)d->batch * d->nheads * d->d_state * 4;
+  add_prefetch(sp, a->out_proj_w, ((int64_t)(a->d_model - 1) * a->out_proj_stride + d->d_inner) * es);
+  add_prefetch(sp, a->ssm_state, S);
+  add_prefetch(sp, a->bx_prev, S);
+  add_prefetch(sp, a->angle_state, (int64_t)d->batch * d->nheads * d->num_rope_angles * 4);
+  add_prefetch(sp, a->mimo_x, (int64_t)d->nheads * R * d->headdim * es);
+  add_prefetch(sp, a->mimo_o, (int64_t)d->nheads * R * d->headdim * es);
+  add_prefetch(sp, a->B_bias, (int64_t)d->nheads * R * d->d_state * es);
+  add_prefetch(sp, a->C_bias, (int64_t)d->nheads * R * d->d_state * es);
+  add_prefetch(sp, a->B_norm_w, (int64_t)d->d_state * es);
+  add_prefetch(sp, a->C_norm_w, (int64_t)d->d_state * es);
+  add_prefetch(sp, a->dt_bias, (int64_t)d->nheads * es);
+  add_prefetch(sp, a->D, (int64_t)d->nheads * es);
+  add_prefetch(sp, a->in_proj_w, ((d_in_proj - 1) * a->in_proj_stride + a->d_model) * es);
+  return launch_status(m3::launch_mimo_step(sp, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // namespace
 
 extern "C" {
@@ -170,11 +295,21 @@ int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o
                                                    reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int64_t m3_mimo_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32_t dtype) {
+  if (!dims) return -(int64_t)M3_ERR_NULL;
+  return step_workspace_bytes(dims, d_model, dtype);
+}
+
+int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream) {
+  return step_entry(dims, args, stream);
+}
+
 int m3_device_error(int reset) {
   const int a = m3::siso_device_error(reset != 0);
   const int b = m3::mimo_device_error(reset != 0);
-  if (a < 0 || b < 0) return -1;
-  return a | b;
+  const int c = m3::step_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a | b | c;
 }
 
 int m3_selftest_wait_timeout(m3_stream_t stream) {
@@ -195,6 +330,7 @@ const char *m3_status_string(int status) {
     case M3_ERR_ALIGN: return "state must be contiguous with a 16-byte aligned base";
     case M3_ERR_LAUNCH: return "CUDA kernel launch failed";
     case M3_ERR_DEVICE: return "no usable CUDA device";
+    case M3_ERR_UNSUPPORTED: return "layer outside the single-launch step kernel's range";
     default: return "unknown status";
   }
 }

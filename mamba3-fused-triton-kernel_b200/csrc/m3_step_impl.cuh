@@ -1,0 +1,438 @@
+// Single-launch MIMO decode step: in_proj GEMM -> fused decode -> out_proj
+// GEMM in one persistent kernel.
+//
+// Included by m3_step_f32.cu and m3_step_bf16.cu (one instantiation set per
+// dtype, compiled in parallel); m3_step.cu holds the host-side dispatch.
+//
+// The three-launch step (src/models/inference.py:476-559: in_proj, the
+// fused Triton kernel, out_proj) moves a few megabytes per step at the
+// batch sizes of decoding, so its time is the latency of three dependent
+// kernels, each of which starts with a cold DRAM round trip.  Here one
+// cooperative grid (every CTA resident) runs the three phases separated by
+// two grid-wide barriers:
+//
+//   0  every CTA asks L2 to prefetch its share of everything the later
+//      phases read from DRAM (out_proj weight, carried state, per-head
+//      parameters, the rest of in_proj's weight), so those reads overlap
+//      phase 1 and later phases only wait on L2;
+//   1  zx = u @ W_in^T into the workspace (fp32 FMA tiles, below);
+//   2  the MIMO row algorithm (m3_mimo_row.cuh) on zx, writing the gated
+//      output y into the workspace and the carried state in place;
+//   3  out = y @ W_out^T.
+//
+// Projection tiles.  A CTA computes 16 rows x TC columns of C = A W^T.  Its
+// 8 warps form 8/KS column groups of 4 columns times KS slices of the K
+// range; a lane holds the K-slices (4 consecutive k per 128) of its warp's
+// 4 W rows in registers, the tile's 16 A rows of the current K chunk sit in
+// shared memory, and each lane accumulates all 64 (row, column) partial
+// sums of its k values.  One 64-value transpose-butterfly then leaves lane l
+// with 2 finished sums, and the KS slices are added in slice order through
+// shared memory.  The per-output summation order is fixed by (KS, TK), so
+// results are deterministic.  (KS, TK) is chosen per projection on the host
+// from the tile count and the grid size.
+//
+// Grid barriers count arrivals on a counter in the workspace that is never
+// reset (see grid_barrier).  Each barrier wait sits inside the next phase,
+// after the loads that do not depend on the previous phase (carried state,
+// parameters, weights) have been issued.  Every spin is bounded: a wait
+// that gives up records M3_DEVERR_TIMEOUT and the CTA carries on (its
+// accesses stay in bounds; the launch's results are then undefined).
+#pragma once
+
+#include "m3_async.cuh"
+#include "m3_kernels.cuh"
+#include "m3_mimo_row.cuh"
+#include "m3_step.cuh"
+
+namespace m3 {
+
+namespace {
+
+using row::kRowWarps;
+using row::row_block_floats;
+
+constexpr int kStepThreads = kRowWarps * 32;
+constexpr int kTileRows = kStepTileRows;
+constexpr int kPrefetchChunk = 4096;
+
+__host__ __device__ constexpr int gemm_smem_floats(int KS, int TK) {
+  return kTileRows * 128 * TK * KS + (KS - 1) * (8 / KS) * 64;
+}
+
+// ---------------------------------------------------------------------------
+// loads
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 bf16x4_to_f4(uint2 t) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+// Four consecutive elements through the read-only path (data constant for
+// the whole launch) or L2 only (data written earlier in this launch).
+template <bool COHERENT>
+__device__ __forceinline__ float4 ld4(const float *p) {
+  if constexpr (COHERENT) return __ldcg(reinterpret_cast<const float4 *>(p));
+  else return __ldg(reinterpret_cast<const float4 *>(p));
+}
+template <bool COHERENT>
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16 *p) {
+  if constexpr (COHERENT) return bf16x4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(p)));
+  else return bf16x4_to_f4(__ldg(reinterpret_cast<const uint2 *>(p)));
+}
+
+__device__ __forceinline__ void st_out(float *p, float v) { *p = v; }
+__device__ __forceinline__ void st_out(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+// ---------------------------------------------------------------------------
+// projection tiles
+// ---------------------------------------------------------------------------
+
+// Sum each of the N values over the warp (N a multiple of 32); afterwards
+// lane l holds the totals of values N/32 * l .. N/32 * l + N/32 - 1 in
+// v[0 .. N/32 - 1] (halving exchanges at offsets 16, 8, 4, 2, 1).
+template <int N>
+__device__ __forceinline__ void warp_transpose_sum(float (&v)[N]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int lvl = 0; lvl < 5; ++lvl) {
+    const int off = 16 >> lvl;
+    const int half = (N / 2) >> lvl;
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float send = upper ? v[q] : v[q + half];
+      const float keep = upper ? v[q + half] : v[q];
+      v[q] = keep + __shfl_xor_sync(kFullMask, send, off);
+    }
+  }
+}
+
+// All tiles of C[M, N] = A[M, K] W[N, K]^T assigned to this CTA (tile t to
+// CTA t mod gridDim.x).  K, lda, ldw multiples of 4; A/W 16-byte (f32) or
+// 8-byte (bf16) aligned.  `pre()` runs once, by every thread, after the
+// first tile's weights have been requested and before A is read (A may be
+// produced by other CTAs up to that point).
+template <typename T, int KS, int TK, bool ACOH, typename Pre>
+__device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
+  extern __shared__ __align__(16) float smem[];  // the kernel's dynamic shared memory
+  constexpr int NCG = 8 / KS;    // column groups of 4
+  constexpr int TC = 4 * NCG;    // tile columns
+  constexpr int KW = 128 * TK;   // k per warp and chunk
+  constexpr int KC = KW * KS;    // k per chunk
+  constexpr int KC4 = KC / 4;
+  float4 *As = reinterpret_cast<float4 *>(smem);  // [16][KC / 4]
+  float *red = smem + kTileRows * KC;              // [KS - 1][NCG][64]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cg = warp / KS, ks = warp - cg * KS;
+  const T *A = static_cast<const T *>(g.A);
+  const T *W = static_cast<const T *>(g.W);
+  T *C = static_cast<T *>(g.C);
+  const int mt = (g.M + kTileRows - 1) / kTileRows;
+  const int ntiles = mt * ((g.N + TC - 1) / TC);
+  if ((int)blockIdx.x >= ntiles) pre();
+
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int m0 = (tile % mt) * kTileRows;
+    const int n0 = (tile / mt) * TC + 4 * cg;
+    float acc[64];  // acc[j * 16 + i]: row m0 + i, column n0 + j
+#pragma unroll
+    for (int q = 0; q < 64; ++q) acc[q] = 0.f;
+
+    for (int kc = 0; kc < g.K; kc += KC) {
+      float4 w[4][TK];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int t = 0; t < TK; ++t) {
+          const int k = kc + ks * KW + 128 * t + 4 * lane;
+          w[j][t] = (n0 + j < g.N && k < g.K) ? ld4<false>(W + (int64_t)(n0 + j) * g.ldw + k)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      if (tile == (int)blockIdx.x && kc == 0) pre();
+      // every A load of the chunk is in flight before the first is stored
+      constexpr int NLD = kTileRows * KC4 / kStepThreads;
+      float4 av[NLD];
+#pragma unroll
+      for (int q = 0; q < NLD; ++q) {
+        const int v = tid + q * kStepThreads;
+        const int i = v / KC4, k = kc + 4 * (v - i * KC4);
+        av[q] = (m0 + i < g.M && k < g.K) ? ld4<ACOH>(A + (int64_t)(m0 + i) * g.lda + k)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < NLD; ++q) As[tid + q * kStepThreads] = av[q];
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < kTileRows; ++i) {
+#pragma unroll
+        for (int t = 0; t < TK; ++t) {
+          const float4 a = As[i * KC4 + ks * (KW / 4) + lane + 32 * t];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float &c = acc[j * 16 + i];
+            c = fmaf(a.x, w[j][t].x, c);
+            c = fmaf(a.y, w[j][t].y, c);
+            c = fmaf(a.z, w[j][t].z, c);
+            c = fmaf(a.w, w[j][t].w, c);
+          }
+        }
+      }
+      __syncthreads();
+    }
+    warp_transpose_sum<64>(acc);  // lane l: outputs 2l, 2l + 1 = column l / 8, rows 2 (l % 8) + {0, 1}
+    if constexpr (KS > 1) {
+      if (ks > 0) {
+        red[((ks - 1) * NCG + cg) * 64 + 2 * lane] = acc[0];
+        red[((ks - 1) * NCG + cg) * 64 + 2 * lane + 1] = acc[1];
+      }
+      __syncthreads();
+      if (ks == 0) {
+#pragma unroll
+        for (int s = 1; s < KS; ++s) {
+          acc[0] += red[((s - 1) * NCG + cg) * 64 + 2 * lane];
+          acc[1] += red[((s - 1) * NCG + cg) * 64 + 2 * lane + 1];
+        }
+      }
+    }
+    if (ks == 0) {
+      const int n = n0 + (lane >> 3);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = m0 + 2 * (lane & 7) + e;
+        if (m < g.M && n < g.N) st_out(C + (int64_t)m * g.ldc + n, acc[e]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// L2 prefetch and grid barriers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The ranges are cut into 4 KB chunks (chunk prefix sums from the host);
+// chunk c is issued by thread c / gridDim.x of CTA c % gridDim.x, so every
+// SM's copy engine gets a few.  Starts and sizes are multiples of 16 bytes.
+__device__ __forceinline__ void prefetch_ranges(const StepParams &sp) {
+  const int c = threadIdx.x * gridDim.x + blockIdx.x;
+  if (c >= sp.pf_first[sp.n_prefetch]) return;
+  int r = 0;
+  while (c >= sp.pf_first[r + 1]) ++r;
+  const int64_t off = (int64_t)(c - sp.pf_first[r]) * kPrefetchChunk;
+  const int64_t left = sp.pf_bytes[r] - off;
+  prefetch_l2(static_cast<const char *>(sp.pf_ptr[r]) + off, left < kPrefetchChunk ? (uint32_t)left : kPrefetchChunk);
+}
+
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Grid barriers.  The workspace holds a base word and one arrival counter
+// (on its own 128-byte line); neither is ever reset.  A CTA arrives by
+// adding 1 to the counter (release), and barrier j of a launch completes
+// when the counter reaches base + j * grid (u32 arithmetic, compared through
+// the signed difference), so a wait can end late but never early; the
+// relaxed polls are followed by an acquire fence, so every write made before
+// any CTA's arrival is visible afterwards.  After the last barrier CTA 0
+// advances the base by 2 * grid for the next launch on the workspace (every
+// CTA reads it before arriving).  A wait gives up after a bounded spin and
+// records M3_DEVERR_TIMEOUT; the counter then no longer matches the base,
+// later launches time out as well (never pass early), and the workspace has
+// to be zeroed again.
+__device__ bool grid_barrier(unsigned *ws, unsigned target, int *s_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned *ctr = ws + kStepBarStride;
+    red_release_add(ctr, 1u);
+    int ok = 0;
+    for (long long i = 0; i < kSpinLimit; ++i) {
+      if ((int)(ld_relaxed(ctr) - target) >= 0) {
+        ok = 1;
+        break;
+      }
+    }
+    fence_acq_rel_gpu();
+    if (!ok) atomicOr(&g_device_error, M3_DEVERR_TIMEOUT);
+    *s_flag = ok;
+  }
+  __syncthreads();
+  return *s_flag != 0;
+}
+
+template <typename T, bool ACOH, typename Pre>
+__device__ __forceinline__ void gemm_phase(int cfg, const StepGemm &g, Pre pre) {
+  switch (cfg) {
+    case 0: gemm_tiles<T, 1, 1, ACOH>(g, pre); break;
+    case 1: gemm_tiles<T, 1, 2, ACOH>(g, pre); break;
+    case 2: gemm_tiles<T, 2, 1, ACOH>(g, pre); break;
+    default: gemm_tiles<T, 4, 1, ACOH>(g, pre); break;
+  }
+}
+
+struct NoPre {
+  __device__ void operator()() const {}
+};
+
+// Grid barrier `j` as a pre() hook: waits once, records the outcome.
+struct BarrierPre {
+  unsigned *bar;
+  unsigned target;
+  int *s_flag;
+  bool *ok;
+  __device__ void operator()() const { *ok = grid_barrier(bar, target, s_flag) && *ok; }
+};
+
+// ---------------------------------------------------------------------------
+// the step kernel
+// ---------------------------------------------------------------------------
+
+template <int BD, int R, typename T, int KP>
+__global__ void __launch_bounds__(kStepThreads, 2) mimo_step_kernel(const StepParams sp) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ int s_flag;
+  const KParams &p = sp.kp;
+  unsigned base = 0;
+  if (threadIdx.x == 0) base = ld_relaxed(sp.bar);
+
+  prefetch_ranges(sp);
+
+  gemm_phase<T, false>(sp.cfg_in, sp.g_in, NoPre{});
+
+  // barrier 1 inside the first item, once its parameters and carried state
+  // are in flight (a CTA without items waits after the loop)
+  bool ok = true, waited = false;
+  const BarrierPre bar1{sp.bar, base + gridDim.x, &s_flag, &ok};
+  const int ngrp = p.H / kRowWarps;
+  for (int item = blockIdx.x; item < sp.n_items; item += gridDim.x) {
+    const int grp = item % ngrp;
+    const int b0 = (item / ngrp) * sp.rows_per_item;
+    const int b1 = min(p.B, b0 + sp.rows_per_item);
+    row::mimo_row_block<BD, R, T, KP, true, true>(p, grp, b0, b1, smem, [&] {
+      if (!waited) bar1();
+      waited = true;
+    });
+    __syncthreads();  // the next item reuses the shared work blocks
+  }
+  if (!waited) bar1();
+
+  // barrier 2 inside the first out_proj tile, once its weights are in flight
+  gemm_phase<T, true>(sp.cfg_out, sp.g_out, BarrierPre{sp.bar, base + 2 * gridDim.x, &s_flag, &ok});
+  if (blockIdx.x == 0 && threadIdx.x == 0) sp.bar[0] = base + 2 * gridDim.x;
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+int num_sms_current() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+size_t step_smem_bytes(int R, int BD, int A) {
+  int f = 2 * row_block_floats(R, BD, A);
+  for (int c = 0; c < kStepGemmCfgs; ++c) {
+    const int g = gemm_smem_floats(kCfgKS[c], kCfgTK[c]);
+    f = g > f ? g : f;
+  }
+  return (size_t)f * sizeof(float);
+}
+
+template <int BD, int R, typename T, int KP>
+cudaError_t launch_step_t(StepParams &sp, cudaStream_t stream) {
+  auto kern = mimo_step_kernel<BD, R, T, KP>;
+  const size_t smem = step_smem_bytes(R, BD, sp.kp.A);
+  static int attr_dev[64] = {0};  // 1 + device once the attribute is set
+  static int per_sm_dev[64] = {0};
+  static size_t smem_dev[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (attr_dev[dev] == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_dev[dev] = 1;
+  }
+  if (smem_dev[dev] != smem || per_sm_dev[dev] == 0) {
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStepThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    per_sm_dev[dev] = per_sm > 2 ? 2 : per_sm;
+    smem_dev[dev] = smem;
+  }
+  const int grid = num_sms_current() * per_sm_dev[dev];
+
+  // phase-2 work items: (head group, run of rows), about one per CTA
+  const int ngrp = sp.kp.H / kRowWarps;
+  const int64_t rows_total = (int64_t)sp.kp.B * ngrp;
+  int rows = (int)((rows_total + grid - 1) / grid);
+  if (rows < 1) rows = 1;
+  sp.rows_per_item = rows;
+  sp.n_items = ngrp * ((sp.kp.B + rows - 1) / rows);
+  sp.cfg_in = step_gemm_cfg(sp.g_in.M, sp.g_in.N, sp.g_in.K, grid);
+  sp.cfg_out = step_gemm_cfg(sp.g_out.M, sp.g_out.N, sp.g_out.K, grid);
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, sp);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <int BD, int R, typename T>
+cudaError_t launch_step_p(StepParams &sp, cudaStream_t stream) {
+  if (sp.kp.P <= 32) return launch_step_t<BD, R, T, 1>(sp, stream);
+  if (sp.kp.P <= 64) return launch_step_t<BD, R, T, 2>(sp, stream);
+  return launch_step_t<BD, R, T, 4>(sp, stream);
+}
+
+template <int BD, typename T>
+cudaError_t launch_step_r(StepParams &sp, cudaStream_t stream) {
+  switch (sp.kp.R) {
+    case 1: return launch_step_p<BD, 1, T>(sp, stream);
+    case 2: return launch_step_p<BD, 2, T>(sp, stream);
+    case 4: return launch_step_p<BD, 4, T>(sp, stream);
+    case 8: return launch_step_p<BD, 8, T>(sp, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// d_state <= 32 runs the 32-wide instantiation (the row code masks columns
+// >= d_state).
+template <typename T>
+cudaError_t launch_step_d(StepParams &sp, cudaStream_t stream) {
+  if (sp.kp.D <= 32) return launch_step_r<32, T>(sp, stream);
+  if (sp.kp.D <= 64) return launch_step_r<64, T>(sp, stream);
+  return launch_step_r<128, T>(sp, stream);
+}
+
+}  // namespace
+}  // namespace m3

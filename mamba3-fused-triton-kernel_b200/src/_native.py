@@ -25,7 +25,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__
                         "lib", "libmamba3_b200.so")
 
 M3_F32, M3_BF16 = 0, 1
-M3_OK, M3_ERR_NULL, M3_ERR_SHAPE, M3_ERR_RANK, M3_ERR_DTYPE, M3_ERR_ALIGN, M3_ERR_LAUNCH, M3_ERR_DEVICE = range(8)
+(M3_OK, M3_ERR_NULL, M3_ERR_SHAPE, M3_ERR_RANK, M3_ERR_DTYPE, M3_ERR_ALIGN, M3_ERR_LAUNCH, M3_ERR_DEVICE,
+ M3_ERR_UNSUPPORTED) = range(9)
 
 SUPPORTED_RANKS = (1, 2, 4, 8)
 MAX_D_STATE = 256
@@ -62,6 +63,18 @@ class FullArgs(ctypes.Structure):
                 ("y", c_void_p), ("y_stride_b", c_int64), ("y_dtype", c_int32)]
 
 
+class StepArgs(ctypes.Structure):
+    _fields_ = [("d_model", c_int32), ("dtype", c_int32),
+                ("u", c_void_p), ("u_stride_b", c_int64),
+                ("in_proj_w", c_void_p), ("in_proj_stride", c_int64),
+                ("out_proj_w", c_void_p), ("out_proj_stride", c_int64),
+                ("dt_bias", c_void_p), ("D", c_void_p), ("B_norm_w", c_void_p), ("C_norm_w", c_void_p),
+                ("B_bias", c_void_p), ("C_bias", c_void_p), ("mimo_x", c_void_p), ("mimo_o", c_void_p),
+                ("ssm_state", c_void_p), ("bx_prev", c_void_p), ("angle_state", c_void_p),
+                ("out", c_void_p), ("out_stride_b", c_int64),
+                ("workspace", c_void_p), ("workspace_bytes", c_int64)]
+
+
 ENTRY_POINTS = {
     "m3_siso_decode": SsmArgs, "m3_mimo_decode": SsmArgs,
     "m3_siso_decode_fused": SsmArgs, "m3_mimo_decode_fused": SsmArgs,
@@ -96,6 +109,10 @@ def load(path: str = LIB_PATH):
                                             c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
                                             c_float, c_void_p]
         lib.m3_residual_rmsnorm.restype = c_int
+        lib.m3_mimo_step_workspace_bytes.argtypes = [POINTER(Dims), c_int32, c_int32]
+        lib.m3_mimo_step_workspace_bytes.restype = c_int64
+        lib.m3_mimo_step.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
+        lib.m3_mimo_step.restype = c_int
         lib.m3_device_error.argtypes = [c_int]
         lib.m3_device_error.restype = c_int
         lib.m3_selftest_wait_timeout.argtypes = [c_void_p]

@@ -7,7 +7,10 @@
   use_triton_full_fused  in_proj -> ONE fused CUDA kernel -> out_proj
                          (the kernel updates ssm_state, bx_prev and
                          angle_state in place; small fp32 batches run both
-                         projections on the library's small-batch GEMM)
+                         projections on the library's small-batch GEMM).
+                         MIMO layers the single-launch kernel takes run the
+                         whole step -- both projections included -- as ONE
+                         launch (``use_single_launch``, default on).
   use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
                          kernel -> out_proj
   use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
@@ -31,6 +34,8 @@ this package.  Differences from the reference, all deliberate:
   ``.float()`` and ``.to(u.dtype)`` casts.
 * ``decode_sequence`` under graph replay keeps a copy of every step's output
   (the reference stacks the same static buffer seq_len times).
+* ``use_single_launch`` (an extra keyword, default True) selects the
+  single-launch step kernel for the full-fused backend where it applies.
 """
 
 from __future__ import annotations
@@ -45,6 +50,7 @@ from src.kernels.mimo_decode import mamba3_mimo_decode_triton
 from src.kernels.mimo_decode_fused import mamba3_mimo_decode_fused_triton
 from src.kernels.siso_decode import mamba3_siso_decode_triton
 from src.kernels.siso_decode_fused import mamba3_siso_decode_fused_triton
+from src.kernels.step import prepare_decode_step
 from src.kernels.utils import apply_rope
 from src.models.mamba3 import Mamba3
 
@@ -63,7 +69,8 @@ class Mamba3Decoder:
 
     def __init__(self, model: Mamba3, use_triton: bool = True, use_cuda_graph: bool = False,
                  use_compile: bool = False, use_triton_fused: bool = False,
-                 use_compile_cuda_graph: bool = False, use_triton_full_fused: bool = False):
+                 use_compile_cuda_graph: bool = False, use_triton_full_fused: bool = False,
+                 use_single_launch: bool = True):
         self.model = model
         # Flag resolution as in the reference (src/models/inference.py:52-57),
         # minus the silent CPU fallback.
@@ -89,6 +96,8 @@ class Mamba3Decoder:
         self._graph_output = None
         self._graph_state = None
         self._fused_cache = None
+        self.use_single_launch = bool(use_single_launch)
+        self._step_cache = None
 
     # ------------------------------------------------------------------
     # public API
@@ -196,11 +205,29 @@ class Mamba3Decoder:
         self._fused_cache = (key, launch)
         return launch
 
+    def _single_launch(self, state: dict):
+        """Prepared single-launch step for this state and the current
+        weights, or None where the kernel does not take the layer; rebuilt
+        when a weight or parameter changes or another state is passed."""
+        m = self.model
+        ts = [m.in_proj.weight, m.out_proj.weight] + [p for p in self._param_list() if p is not None]
+        key = (tuple((t.data_ptr(), t._version, t.dtype) for t in ts),
+               tuple((t.data_ptr(), tuple(t.shape)) for t in
+                     (state["ssm_state"], state["bx_prev"], state["angle_state"])))
+        if self._step_cache is None or self._step_cache[0] != key:
+            self._step_cache = (key, prepare_decode_step(m, state))
+        return self._step_cache[1]
+
     def _step_triton_full_fused(self, u: torch.Tensor, state: dict) -> tuple:
         """in_proj -> fused CUDA step -> out_proj (reference:
         src/models/inference.py:476-559).  The kernel writes its gated output
-        in the weight dtype, which is what out_proj consumes."""
+        in the weight dtype, which is what out_proj consumes.  With
+        ``use_single_launch`` the three run as one kernel where it applies."""
         m = self.model
+        if self.use_single_launch:
+            launch = self._single_launch(state)
+            if launch is not None and launch.accepts(u):
+                return launch.run(u), state
         zx = linear(u, m.in_proj.weight)
         if zx.dtype not in (torch.float32, torch.bfloat16) or zx.stride(1) != 1:
             zx = zx.float().contiguous()

@@ -25,19 +25,19 @@ HEADER = os.path.join(ROOT, "include", "mamba3_b200.h")
 
 def _declared_functions():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char \*)\s*(m3_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char \*)\s*(m3_\w+)\s*\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 12, names
+    assert len(names) == 14, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
     exported = set(re.findall(r"\bT (m3_\w+)", out.stdout))
     assert set(names) <= exported
-    assert lib.m3_version() == 10100
+    assert lib.m3_version() == 10200
     assert nat.status_string(nat.M3_ERR_RANK).startswith("unsupported mimo_rank")
 
 
@@ -47,11 +47,13 @@ _LAYOUT_C = r"""
 #include "mamba3_b200.h"
 #define P(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
 int main(void) {
-  printf("m3_dims %zu\nm3_ssm_args %zu\nm3_full_args %zu\n",
-         sizeof(m3_dims), sizeof(m3_ssm_args), sizeof(m3_full_args));
+  printf("m3_dims %zu\nm3_ssm_args %zu\nm3_full_args %zu\nm3_step_args %zu\n",
+         sizeof(m3_dims), sizeof(m3_ssm_args), sizeof(m3_full_args), sizeof(m3_step_args));
   P(m3_dims, A_floor) P(m3_ssm_args, z) P(m3_ssm_args, y_dtype) P(m3_ssm_args, B_sd)
   P(m3_ssm_args, trap_sh) P(m3_ssm_args, mo_sp) P(m3_ssm_args, bx_prev)
   P(m3_full_args, param_dtype) P(m3_full_args, mimo_o) P(m3_full_args, y_dtype)
+  P(m3_step_args, u) P(m3_step_args, out_proj_stride) P(m3_step_args, mimo_o) P(m3_step_args, angle_state)
+  P(m3_step_args, out_stride_b) P(m3_step_args, workspace_bytes)
   return 0;
 }
 """
@@ -67,7 +69,9 @@ def test_ctypes_layout_matches_c_header():
     assert int(got["m3_dims"]) == ctypes.sizeof(nat.Dims)
     assert int(got["m3_ssm_args"]) == ctypes.sizeof(nat.SsmArgs)
     assert int(got["m3_full_args"]) == ctypes.sizeof(nat.FullArgs)
-    pairs = {"m3_dims": nat.Dims, "m3_ssm_args": nat.SsmArgs, "m3_full_args": nat.FullArgs}
+    assert int(got["m3_step_args"]) == ctypes.sizeof(nat.StepArgs)
+    pairs = {"m3_dims": nat.Dims, "m3_ssm_args": nat.SsmArgs, "m3_full_args": nat.FullArgs,
+             "m3_step_args": nat.StepArgs}
     for key, val in got.items():
         if "." in key:
             struct, field = key.split(".")
@@ -179,3 +183,73 @@ def test_status_mapping_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         nat.check(nat.M3_ERR_LAUNCH, "x")
     nat.check(nat.M3_OK, "x")
+
+
+def _valid_step():
+    """A single-launch step call with fake, well-aligned device addresses
+    (d_model 256, MIMO rank 4, 16 heads of 32, d_state 64)."""
+    lib = nat.load()
+    dims = nat.Dims(batch=4, nheads=16, headdim=32, d_state=64, mimo_rank=4, num_rope_angles=16,
+                    ngroups=1, d_inner=512, A_floor=1e-4)
+    a = nat.StepArgs()
+    a.d_model, a.dtype = 256, nat.M3_F32
+    fake = 0x7000_0000_0000
+    for i, f in enumerate(["u", "in_proj_w", "out_proj_w", "dt_bias", "D", "B_norm_w", "C_norm_w", "B_bias",
+                           "C_bias", "mimo_x", "mimo_o", "ssm_state", "bx_prev", "angle_state", "out",
+                           "workspace"]):
+        setattr(a, f, fake + (1 << 24) * i)
+    a.u_stride_b = a.in_proj_stride = a.out_stride_b = 256
+    a.out_proj_stride = 512
+    a.workspace_bytes = lib.m3_mimo_step_workspace_bytes(dims, 256, nat.M3_F32)
+    return lib, dims, a
+
+
+def test_step_workspace_size_and_range():
+    lib, dims, a = _valid_step()
+    d_in_proj = 2 * 512 + 2 * 64 * 4 + 3 * 16 + 16
+    expect = 256 + -(-4 * d_in_proj * 4 // 256) * 256 + -(-4 * 512 * 4 // 256) * 256
+    assert a.workspace_bytes == expect
+    assert lib.m3_mimo_step_workspace_bytes(dims, 256, nat.M3_BF16) < expect
+    assert lib.m3_mimo_step_workspace_bytes(None, 256, 0) == -nat.M3_ERR_NULL
+    assert lib.m3_mimo_step_workspace_bytes(dims, 256, 9) == -nat.M3_ERR_DTYPE
+    for field, bad, status in [("nheads", 12, nat.M3_ERR_SHAPE),  # d_inner != H * P
+                               ("mimo_rank", 3, nat.M3_ERR_RANK), ("ngroups", 2, nat.M3_ERR_SHAPE)]:
+        _, d2, _ = _valid_step()
+        setattr(d2, field, bad)
+        assert lib.m3_mimo_step_workspace_bytes(d2, 256, 0) == -status, field
+    # valid layers outside the kernel's range
+    for kw in [dict(nheads=4, d_inner=128), dict(headdim=256, nheads=8, d_inner=2048),
+               dict(d_state=256, num_rope_angles=16)]:
+        _, d2, _ = _valid_step()
+        for k, v in kw.items():
+            setattr(d2, k, v)
+        assert lib.m3_mimo_step_workspace_bytes(d2, 256, 0) == -nat.M3_ERR_UNSUPPORTED, kw
+    assert lib.m3_mimo_step_workspace_bytes(dims, 254, 0) == -nat.M3_ERR_UNSUPPORTED
+
+
+def test_step_validation():
+    lib, dims, a = _valid_step()
+    dims.batch = 0  # a valid call with no rows returns before touching a device
+    assert lib.m3_mimo_step(dims, a, None) == nat.M3_OK
+    assert lib.m3_mimo_step(None, a, None) == nat.M3_ERR_NULL
+    for f in ["u", "in_proj_w", "mimo_o", "angle_state", "out", "workspace"]:
+        lib, dims, a = _valid_step()
+        setattr(a, f, None)
+        assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_NULL, f
+    lib, dims, a = _valid_step()
+    a.workspace_bytes -= 1
+    assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_SHAPE
+    for f, v in [("u_stride_b", 255), ("out_proj_stride", 511), ("out_stride_b", 100)]:
+        lib, dims, a = _valid_step()
+        setattr(a, f, v)
+        assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_SHAPE, f
+    for f, off in [("u", 4), ("in_proj_w", 8), ("B_bias", 4), ("workspace", 16), ("ssm_state", 8)]:
+        lib, dims, a = _valid_step()
+        setattr(a, f, getattr(a, f) + off)
+        assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_ALIGN, f
+    lib, dims, a = _valid_step()
+    a.in_proj_stride = 258  # >= d_model but not a multiple of 4
+    assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_ALIGN
+    lib, dims, a = _valid_step()
+    dims.nheads, dims.d_inner = 4, 128
+    assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_UNSUPPORTED

@@ -179,21 +179,35 @@ def test_drift_1024_steps_against_oracle(mode, R):
 
 @pytest.mark.parametrize("mimo", [False, True])
 def test_bf16_weights_match_pytorch_bf16(mimo):
+    """bf16 weights, 16 graph-replayed steps.  The fused path (for MIMO the
+    single-launch kernel with its own projections) and PyTorch bf16 eager
+    round differently, so both are measured against fp32 arithmetic on the
+    same bf16 weights and inputs: the fused path's error must stay within
+    twice PyTorch bf16's own, and the two within bf16 distance of each other."""
+    import copy
     model = _model(d_model=512, d_state=128, headdim=64, is_mimo=mimo, mimo_rank=8, dtype=torch.bfloat16)
     ref = Mamba3Decoder(model, use_triton=False)
+    ref32 = Mamba3Decoder(copy.deepcopy(model).float(), use_triton=False)
     dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
     s_ref, s = ref.init_state(8, device="cuda"), dec.init_state(8, device="cuda")
+    s32 = ref32.init_state(8, device="cuda")
     dec.warmup_cuda_graph(s, n_warmup=2)
     torch.manual_seed(4)
     with torch.no_grad():
         for _ in range(16):
             u = torch.randn(8, 512, device="cuda").bfloat16()
             o_ref, s_ref = ref.step(u, s_ref)
+            o32, s32 = ref32.step(u.float(), s32)
             o, s = dec.step(u, s)
     assert o.dtype == torch.bfloat16
-    torch.testing.assert_close(o.float(), o_ref.float(), rtol=3e-2, atol=3e-3)
+    err_ours, err_torch = _max_diff(o, o32), _max_diff(o_ref, o32)
+    assert err_ours <= 2 * err_torch + 1e-3, (err_ours, err_torch)
+    torch.testing.assert_close(o.float(), o_ref.float(), rtol=3e-2, atol=2e-2)
     torch.testing.assert_close(s["angle_state"], s_ref["angle_state"], rtol=1e-3, atol=1e-4)
-    torch.testing.assert_close(s["ssm_state"], s_ref["ssm_state"], rtol=2e-2, atol=2e-3)
+    for k in ("ssm_state", "bx_prev"):
+        e_ours, e_torch = _max_diff(s[k], s32[k]), _max_diff(s_ref[k], s32[k])
+        assert e_ours <= 2 * e_torch + 1e-3, (k, e_ours, e_torch)
+    torch.testing.assert_close(s["ssm_state"], s_ref["ssm_state"], rtol=2e-2, atol=1e-2)
 
 
 def test_resume_from_saved_state():

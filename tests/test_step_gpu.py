@@ -1,0 +1,143 @@
+"""GPU tests of the single-launch decode step (m3_mimo_step).
+
+The kernel computes in_proj, the full-step update and out_proj in one
+cooperative launch.  It is checked against the oracle (fp32, 1e-4) and
+against the three-launch path of the same decoder (``use_single_launch=
+False``) over several steps, across ranks, state sizes, head dims, batch
+sizes that give one or many work items per CTA, bf16, and graph capture;
+plus: layers outside its range fall back, the workspace's barrier counters
+are back at zero after every launch, and the bounded waits never fire.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_params
+from oracle import mamba3_oracle as orc
+from src import _native as nat
+from src.kernels.step import decode_step, prepare_decode_step
+from src.models.inference import Mamba3Decoder
+from src.models.mamba3 import Mamba3
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # d_model, d_state, headdim, rank, batch
+    (64, 16, 16, 1, 3),
+    (64, 16, 16, 8, 5),
+    (128, 32, 16, 2, 1),
+    (256, 64, 32, 4, 128),
+    (256, 64, 32, 4, 1000),
+    (512, 128, 64, 8, 7),
+    (512, 128, 128, 4, 33),
+    (1024, 128, 64, 4, 64),
+]
+
+
+def _layer(d_model, d_state, headdim, R, seed, dtype=torch.float32):
+    kw = dict(d_model=d_model, d_state=d_state, headdim=headdim, is_mimo=True, mimo_rank=R)
+    dims = orc.layer_dims(**kw)
+    params = orc.synthetic_params(dims, seed, bf16=dtype == torch.bfloat16, randomize_small=True)
+    model = Mamba3(**kw, device="cuda", dtype=dtype)
+    load_params(model, params)
+    return kw, dims, params, model
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "d%d_n%d_p%d_r%d_b%d" % s)
+def test_single_launch_matches_oracle(shape):
+    d_model, D, P, R, B = shape
+    kw, dims, params, model = _layer(d_model, D, P, R, seed=sum(shape))
+    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    st = dec.init_state(B, device="cuda")
+    assert prepare_decode_step(model, st) is not None
+    st_np = orc.init_state(dims, B)
+    u = orc.synthetic_inputs(dims, B, 4, seed=7)
+    with torch.no_grad():
+        for t in range(4):
+            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            oe, st_np = orc.decode_step(u[t], params, dims, st_np)
+            np.testing.assert_allclose(o.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
+    for k in st_np:
+        np.testing.assert_allclose(st[k].cpu().numpy(), st_np[k], rtol=1e-4, atol=1e-4, err_msg=k)
+    assert nat.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", SHAPES[1:7:2], ids=lambda s: "d%d_n%d_p%d_r%d_b%d" % s)
+def test_single_launch_matches_three_launches(shape, dtype):
+    d_model, D, P, R, B = shape
+    _, _, _, model = _layer(d_model, D, P, R, seed=3, dtype=dtype)
+    one = Mamba3Decoder(model, use_triton_full_fused=True)
+    three = Mamba3Decoder(model, use_triton_full_fused=True, use_single_launch=False)
+    s1, s3 = one.init_state(B, device="cuda"), three.init_state(B, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    tol = dict(rtol=1e-4, atol=1e-4) if dtype == torch.float32 else dict(rtol=3e-2, atol=3e-2)
+    with torch.no_grad():
+        for _ in range(6):
+            u = torch.randn(B, d_model, device="cuda", generator=g).to(dtype)
+            o1, s1 = one.step(u, s1)
+            o3, s3 = three.step(u, s3)
+            assert o1.dtype == o3.dtype == dtype
+            torch.testing.assert_close(o1.float(), o3.float(), **tol)
+    assert one._step_cache[1] is not None and three._step_cache is None
+    for k in s1:
+        torch.testing.assert_close(s1[k], s3[k], **tol)
+
+
+def test_graph_capture_of_the_single_launch():
+    _, dims, params, model = _layer(256, 64, 32, 4, seed=21)
+    B = 128
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    st = dec.init_state(B, device="cuda")
+    dec.warmup_cuda_graph(st, n_warmup=2)
+    assert dec._step_cache[1] is not None
+    st_np = orc.init_state(dims, B)
+    u = orc.synthetic_inputs(dims, B, 2 + 12, seed=22)
+    for t in range(2):  # the warm-up steps ran on a zero input
+        _, st_np = orc.decode_step(np.zeros_like(u[0]), params, dims, st_np)
+    with torch.no_grad():
+        for t in range(12):
+            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            oe, st_np = orc.decode_step(u[t], params, dims, st_np)
+            np.testing.assert_allclose(o.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
+
+
+def test_barrier_words_advance_by_two_grids():
+    """The grid barriers' words are never reset: after every launch the base
+    word equals the arrival counter, and each launch adds the same amount."""
+    _, dims, _, model = _layer(256, 64, 32, 4, seed=2)
+    st = Mamba3Decoder(model, use_triton=False).init_state(300, device="cuda")
+    launch = prepare_decode_step(model, st)
+    u = torch.randn(300, 256, device="cuda")
+    words = []
+    for _ in range(3):
+        launch.run(u)
+        torch.cuda.synchronize()
+        w = launch.workspace[:256].view(torch.int32).cpu()
+        assert int(w[0]) == int(w[32]), "base word and arrival counter disagree"
+        words.append(int(w[0]))
+    step = words[1] - words[0]
+    assert step > 0 and step % 2 == 0 and words[2] - words[1] == step
+    assert nat.device_error() == 0
+
+
+def test_layers_outside_the_range_fall_back():
+    # 4 heads (not a multiple of 8): three-launch path, same results as eager
+    model = Mamba3(d_model=32, d_state=16, headdim=16, is_mimo=True, mimo_rank=2, device="cuda")
+    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    ref = Mamba3Decoder(model, use_triton=False)
+    s, sr = dec.init_state(2, device="cuda"), ref.init_state(2, device="cuda")
+    u = torch.randn(2, 32, device="cuda")
+    with torch.no_grad():
+        o, s = dec.step(u, s)
+        orf, sr = ref.step(u, sr)
+    assert dec._step_cache[1] is None
+    torch.testing.assert_close(o, orf, rtol=1e-4, atol=1e-4)
+    with pytest.raises(ValueError):
+        decode_step(model, u, s)
+    # SISO layers are not taken either
+    siso = Mamba3(d_model=64, d_state=16, headdim=16, device="cuda")
+    st = Mamba3Decoder(siso, use_triton=False).init_state(1, device="cuda")
+    assert prepare_decode_step(siso, st) is None
