@@ -42,7 +42,8 @@ enum {
   M3_ERR_ALIGN = 5,  /* state not contiguous / not 16-byte aligned         */
   M3_ERR_LAUNCH = 6, /* the CUDA launch itself failed                      */
   M3_ERR_DEVICE = 7, /* no usable CUDA device                              */
-  M3_ERR_UNSUPPORTED = 8 /* valid layer the single-launch step does not take */
+  M3_ERR_UNSUPPORTED = 8, /* valid layer the single-launch step does not take */
+  M3_ERR_SCRATCH = 9      /* needs more than the library's static scratch     */
 };
 
 /* Element type codes. */
@@ -190,6 +191,27 @@ int64_t m3_mimo_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32
  * barriers; no counterpart kernel in the reference, whose step is three
  * launches. */
 int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream);
+
+/* Bytes of the library's own device scratch array behind m3_mimo_step_static
+ * (held on every GPU that loads the library until the process exits). */
+#define M3_STEP_STATIC_SCRATCH_BYTES (4 * 1024 * 1024)
+
+/* m3_mimo_step for callers that cannot allocate device memory: a plugin
+ * handed device buffers by a host framework without access to its
+ * allocator, a serving thread that must not call cudaMalloc (it can
+ * synchronise the device and take milliseconds), a process whose device
+ * footprint is fixed after start-up.  Same arguments and results as
+ * m3_mimo_step, except that args->workspace must be NULL and
+ * args->workspace_bytes 0: the workspace is a device array inside the
+ * library, M3_STEP_STATIC_SCRATCH_BYTES long.  A layer and batch needing
+ * more (m3_mimo_step_workspace_bytes) return M3_ERR_SCRATCH and enqueue
+ * nothing.  Allocates nothing.  The first call on a device looks up the
+ * array's device address (once, with that device current); make that first
+ * call before any stream capture.  Each call clears the array's barrier
+ * words on `stream` before its launch; every call on a device shares the
+ * array, so calls that overlap on the GPU race and must be serialised by
+ * the caller.  No counterpart in the reference. */
+int m3_mimo_step_static(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream);
 
 /* Residual add + RMSNorm between the blocks of a stack (x <- x +
  * mixer(RMSNorm(x)), src/models/mamba3.py:412-421 with RMSNorm :26-36):

@@ -331,6 +331,7 @@ const char *m3_status_string(int status) {
     case M3_ERR_LAUNCH: return "CUDA kernel launch failed";
     case M3_ERR_DEVICE: return "no usable CUDA device";
     case M3_ERR_UNSUPPORTED: return "layer outside the single-launch step kernel's range";
+    case M3_ERR_SCRATCH: return "workspace larger than the library's static scratch (M3_STEP_STATIC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }

@@ -26,7 +26,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__
 
 M3_F32, M3_BF16 = 0, 1
 (M3_OK, M3_ERR_NULL, M3_ERR_SHAPE, M3_ERR_RANK, M3_ERR_DTYPE, M3_ERR_ALIGN, M3_ERR_LAUNCH, M3_ERR_DEVICE,
- M3_ERR_UNSUPPORTED) = range(9)
+ M3_ERR_UNSUPPORTED, M3_ERR_SCRATCH) = range(10)
+STEP_STATIC_SCRATCH_BYTES = 4 * 1024 * 1024  # M3_STEP_STATIC_SCRATCH_BYTES
 
 SUPPORTED_RANKS = (1, 2, 4, 8)
 MAX_D_STATE = 256
@@ -113,6 +114,8 @@ def load(path: str = LIB_PATH):
         lib.m3_mimo_step_workspace_bytes.restype = c_int64
         lib.m3_mimo_step.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
         lib.m3_mimo_step.restype = c_int
+        lib.m3_mimo_step_static.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
+        lib.m3_mimo_step_static.restype = c_int
         lib.m3_device_error.argtypes = [c_int]
         lib.m3_device_error.restype = c_int
         lib.m3_selftest_wait_timeout.argtypes = [c_void_p]

@@ -31,7 +31,7 @@ def _declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 14, names
+    assert len(names) == 15, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
@@ -253,3 +253,27 @@ def test_step_validation():
     lib, dims, a = _valid_step()
     dims.nheads, dims.d_inner = 4, 128
     assert lib.m3_mimo_step(dims, a, None) == nat.M3_ERR_UNSUPPORTED
+
+
+def test_static_step_validation_before_any_device_work():
+    """The allocation-free step rejects a caller workspace, bad layers and
+    batches whose workspace exceeds the library's scratch before it looks
+    for a device (status codes only; nothing is enqueued)."""
+    text = open(HEADER).read()
+    m = re.search(r"#define M3_STEP_STATIC_SCRATCH_BYTES \((\d+) \* (\d+) \* (\d+)\)", text)
+    assert m and int(m.group(1)) * int(m.group(2)) * int(m.group(3)) == nat.STEP_STATIC_SCRATCH_BYTES
+    lib, dims, a = _valid_step()
+    assert lib.m3_mimo_step_static(None, a, None) == nat.M3_ERR_NULL
+    assert lib.m3_mimo_step_static(dims, None, None) == nat.M3_ERR_NULL
+    assert lib.m3_mimo_step_static(dims, a, None) == nat.M3_ERR_SHAPE  # a caller workspace is not taken
+    a.workspace, a.workspace_bytes = None, 0
+    dims.mimo_rank = 3
+    assert lib.m3_mimo_step_static(dims, a, None) == nat.M3_ERR_RANK
+    dims.mimo_rank = 4
+    dims.nheads, dims.d_inner = 4, 128
+    assert lib.m3_mimo_step_static(dims, a, None) == nat.M3_ERR_UNSUPPORTED
+    dims.nheads, dims.d_inner = 16, 512
+    dims.batch = 4096  # 4096 rows x 1648 zx columns x 4 bytes > 4 MiB
+    assert lib.m3_mimo_step_workspace_bytes(dims, 256, nat.M3_F32) > nat.STEP_STATIC_SCRATCH_BYTES
+    assert lib.m3_mimo_step_static(dims, a, None) == nat.M3_ERR_SCRATCH
+    assert "static scratch" in nat.status_string(nat.M3_ERR_SCRATCH)
