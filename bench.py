@@ -81,6 +81,18 @@ def fused_bytes_per_launch(m, batch: int, zx_bytes: int, y_bytes: int) -> int:
     return batch * m.d_in_proj * zx_bytes + 16 * S + 8 * batch * H * A + batch * m.d_inner * y_bytes + params
 
 
+def step_bytes_per_launch(m, batch: int, es: int) -> int:
+    """Algorithmic HBM bytes of one single-launch decode step: both projection
+    weights, the input and output rows, ssm_state and bx_prev (read + write),
+    angle_state (read + write) and the per-head parameters.  The in_proj
+    output and the gated output stay in L2 between the kernel's phases."""
+    H, P, D, R, A = m.nheads, m.headdim, m.d_state, m.mimo_rank, m.num_rope_angles
+    S = batch * H * D
+    params = es * (2 * H + 2 * D + 2 * H * R * D + 2 * H * R * P)
+    weights = es * (m.d_in_proj * m.d_model + m.d_model * m.d_inner)
+    return weights + 2 * batch * m.d_model * es + 16 * S + 8 * batch * H * A + params
+
+
 def hbm_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -90,14 +102,15 @@ def hbm_peak():
         return HBM_FALLBACK_GBS, "fallback"
 
 
-def profile_traffic(workload: str):
-    """DRAM bytes per launch of the fused kernel recorded by the ncu capture
-    summary of this workload under profiles/ (line ``dram_bytes_per_launch:
-    N``), or None."""
+def profile_traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of the dominant kernel (``kernel``: "step" for
+    the single-launch step, "fused" for the fused decode kernel) recorded by
+    an ncu capture summary of this workload under profiles/ (a line
+    ``dram_bytes_per_launch[<kernel>]: N``), or None."""
     import glob
     for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"*{workload}*.md"))):
         with open(path) as f:
-            mt = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read())
+            mt = re.search(r"dram_bytes_per_launch\[" + kernel + r"\]:\s*([0-9]+)", f.read())
         if mt:
             return int(mt.group(1))
     return None
@@ -180,13 +193,18 @@ def cpu_oracle_rate(kw, batch, dtype_name, steps=None, budget_s=10.0, warmup=1):
     return batch * n / el, n, os.cpu_count() or 1
 
 
-def config_dict(workload, kw, batch, world, dtype_name):
+def config_dict(workload, kw, batch, world, dtype_name, reference=False):
     published = PUBLISHED.get(workload)
+    if reference:
+        par, l2, step = ("rank 0 only (host cores)", "n/a (CPU)",
+                         "oracle decode step (numpy restatement of the reference PyTorch decode)")
+    else:
+        par = f"batch-sharded x{world}, no collective on the decode path"
+        l2 = "flushed (256 MiB write) before every timed step; per-step CUDA events"
+        step = ("CUDA-graph replay of Mamba3Decoder.step: one single-launch kernel (in_proj, fused update, "
+                "out_proj) for MIMO layers it takes, else in_proj GEMM + fused decode kernel + out_proj GEMM")
     return {"workload": workload, "batch_per_gpu": batch, "global_batch": batch * world,
-            **kw, "weights": dtype_name, "state": "f32",
-            "parallelism": f"batch-sharded x{world}, no collective on the decode path",
-            "l2": "flushed (256 MiB write) before every timed step; per-step CUDA events",
-            "step": "CUDA-graph replay of in_proj GEMM + fused decode kernel + out_proj GEMM",
+            **kw, "weights": dtype_name, "state": "f32", "parallelism": par, "l2": l2, "step": step,
             "baseline": ("A100 full-fused+graph P50 0.295 ms at B=128 (reference README.md:229)"
                          if published else None)}
 
@@ -202,7 +220,7 @@ def run_reference(args, kw, batch, dtype_name, rank):
         "metric": "decode tokens/s", "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_dict(args.workload, kw, batch, 1, dtype_name),
+        "data": "synthetic", "config": config_dict(args.workload, kw, batch, 1, dtype_name, reference=True),
         "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{n} oracle decode steps of {batch} sequences (numpy, host cores)"},
         "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -316,12 +334,14 @@ def main():
     p50 = max_over_ranks(float(np.percentile(step_ms, 50)))
     p99 = max_over_ranks(float(np.percentile(step_ms, 99)))
     value = world * batch * K / (total_ms / 1000.0)
-    # our kernels per step: the fused decode kernel, plus both projections when
-    # they run on the library's small-batch GEMM (otherwise cuBLAS)
+    # our kernels per step: the single-launch step kernel, or the fused decode
+    # kernel plus both projections when they run on the library's small-batch
+    # GEMM (otherwise cuBLAS)
+    single = dec._step_cache is not None and dec._step_cache[1] is not None
     from src.kernels.linear import uses_small_m_kernel
     own_gemms = int(uses_small_m_kernel(u_dev[0], model.in_proj.weight)) + int(
         uses_small_m_kernel(torch.empty(batch, model.d_inner, device=dev, dtype=wdtype), model.out_proj.weight))
-    gpu_launches = K * (1 + own_gemms)
+    gpu_launches = K if single else K * (1 + own_gemms)
 
     # ---- fused kernel alone (roofline) and the two GEMMs, same flush ----
     # Each component is captured in its own CUDA graph and replayed between
@@ -342,17 +362,36 @@ def main():
             fn()
         return g
 
+    es = 2 if wdtype == torch.bfloat16 else 4
     with torch.no_grad():
         g_fused = graphed(lambda: launch.run(zx, y))
         g_in = graphed(lambda: linear(u_dev[0], model.in_proj.weight))
         g_out = graphed(lambda: linear(y, model.out_proj.weight))
-        k_ms = timed_loop(lambda i: g_fused.replay(), K)
+        f_ms = timed_loop(lambda i: g_fused.replay(), K)
         gi_ms = timed_loop(lambda i: g_in.replay(), min(K, 500))
         go_ms = timed_loop(lambda i: g_out.replay(), min(K, 500))
+        # the three-launch step (in_proj, fused kernel, out_proj) on its own state
+        dec3 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=False)
+        st3 = dec3.init_state(batch, device=dev)
+        dec3.warmup_cuda_graph(st3, n_warmup=3)
+        t3_ms = timed_loop(lambda i: dec3.step(u_dev[i % n_inputs], st3), min(K, 500))
+        dec3._cuda_graph = None
+        if single:
+            step_launch = dec._step_cache[1]
+            out_static = torch.empty(batch, model.d_model, device=dev, dtype=wdtype)
+            g_step = graphed(lambda: step_launch.run(u_dev[0], out_static))
+            s_ms = timed_loop(lambda i: g_step.replay(), K)
+            del g_step
     del g_fused, g_in, g_out
-    k_mean = max_over_ranks(float(k_ms.mean()))
-    nbytes = fused_bytes_per_launch(model, batch, 2 if wdtype == torch.bfloat16 else 4,
-                                    2 if wdtype == torch.bfloat16 else 4)
+    f_mean = max_over_ranks(float(f_ms.mean()))
+    if single:
+        kernel_name = "single-launch decode step (m3_mimo_step)"
+        k_mean = max_over_ranks(float(s_ms.mean()))
+        nbytes = step_bytes_per_launch(model, batch, es)
+    else:
+        kernel_name = "fused decode (m3_mimo_full_fused / m3_siso_full_fused)"
+        k_mean = f_mean
+        nbytes = fused_bytes_per_launch(model, batch, es, es)
     peak, peak_kind = hbm_peak()
     achieved = nbytes / (k_mean * 1e-3) / 1e9
 
@@ -393,13 +432,15 @@ def main():
             "vs_baseline": round(value / (world * published), 3) if published else None,
             "dtype": dtype_name, "data": "synthetic",
             "config": config_dict(args.workload, kw, batch, world, dtype_name),
-            "roofline": {"bound": "hbm", "kernel": "fused decode (m3_mimo_full_fused / m3_siso_full_fused)",
+            "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
                          "mean_launch_ms": round(k_mean, 5),
-                         "traffic": profile_traffic(args.workload)},
-            "kernels_ms": {"in_proj_gemm": round(float(gi_ms.mean()), 5),
-                           "fused_decode": round(k_mean, 5),
+                         "traffic": profile_traffic(args.workload, "step" if single else "fused")},
+            "kernels_ms": {"decode_step": round(k_mean, 5) if single else None,
+                           "three_launch_step": round(max_over_ranks(float(t3_ms.mean())), 5),
+                           "in_proj_gemm": round(float(gi_ms.mean()), 5),
+                           "fused_decode": round(f_mean, 5),
                            "out_proj_gemm": round(float(go_ms.mean()), 5)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": batch * model.d_model * u_host.element_size(),

@@ -10,7 +10,8 @@
                          projections on the library's small-batch GEMM).
                          MIMO layers the single-launch kernel takes run the
                          whole step -- both projections included -- as ONE
-                         launch (``use_single_launch``, default on).
+                         launch (``use_single_launch``, default on) at
+                         batch sizes up to SINGLE_LAUNCH_MAX_BATCH.
   use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
                          kernel -> out_proj
   use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
@@ -51,6 +52,11 @@ from src.kernels.mimo_decode_fused import mamba3_mimo_decode_fused_triton
 from src.kernels.siso_decode import mamba3_siso_decode_triton
 from src.kernels.siso_decode_fused import mamba3_siso_decode_fused_triton
 from src.kernels.step import prepare_decode_step
+
+# Batches up to this size run the single-launch step; beyond it the
+# projections are large enough for cuBLAS's tiles to win over the
+# single-launch kernel's latency-oriented ones.
+SINGLE_LAUNCH_MAX_BATCH = 256
 from src.kernels.utils import apply_rope
 from src.models.mamba3 import Mamba3
 
@@ -215,7 +221,8 @@ class Mamba3Decoder:
                tuple((t.data_ptr(), tuple(t.shape)) for t in
                      (state["ssm_state"], state["bx_prev"], state["angle_state"])))
         if self._step_cache is None or self._step_cache[0] != key:
-            self._step_cache = (key, prepare_decode_step(m, state))
+            small = state["ssm_state"].shape[0] <= SINGLE_LAUNCH_MAX_BATCH
+            self._step_cache = (key, prepare_decode_step(m, state) if small else None)
         return self._step_cache[1]
 
     def _step_triton_full_fused(self, u: torch.Tensor, state: dict) -> tuple:

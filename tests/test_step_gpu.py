@@ -49,14 +49,14 @@ def _layer(d_model, d_state, headdim, R, seed, dtype=torch.float32):
 def test_single_launch_matches_oracle(shape):
     d_model, D, P, R, B = shape
     kw, dims, params, model = _layer(d_model, D, P, R, seed=sum(shape))
-    dec = Mamba3Decoder(model, use_triton_full_fused=True)
-    st = dec.init_state(B, device="cuda")
-    assert prepare_decode_step(model, st) is not None
+    st = Mamba3Decoder(model, use_triton=False).init_state(B, device="cuda")
+    launch = prepare_decode_step(model, st)  # the kernel itself, at any batch size
+    assert launch is not None
     st_np = orc.init_state(dims, B)
     u = orc.synthetic_inputs(dims, B, 4, seed=7)
     with torch.no_grad():
         for t in range(4):
-            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            o = launch.run(torch.from_numpy(u[t]).cuda())
             oe, st_np = orc.decode_step(u[t], params, dims, st_np)
             np.testing.assert_allclose(o.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
     for k in st_np:
@@ -121,6 +121,17 @@ def test_barrier_words_advance_by_two_grids():
     step = words[1] - words[0]
     assert step > 0 and step % 2 == 0 and words[2] - words[1] == step
     assert nat.device_error() == 0
+
+
+def test_decoder_policy_caps_the_batch():
+    from src.models.inference import SINGLE_LAUNCH_MAX_BATCH
+    _, _, _, model = _layer(64, 16, 16, 2, seed=4)
+    for B, expect in ((SINGLE_LAUNCH_MAX_BATCH, True), (SINGLE_LAUNCH_MAX_BATCH + 1, False)):
+        dec = Mamba3Decoder(model, use_triton_full_fused=True)
+        st = dec.init_state(B, device="cuda")
+        with torch.no_grad():
+            dec.step(torch.randn(B, 64, device="cuda"), st)
+        assert (dec._step_cache[1] is not None) == expect, B
 
 
 def test_layers_outside_the_range_fall_back():
