@@ -6,25 +6,12 @@
 
 namespace m3 {
 
-// Projection tile configurations: KS K-slices across the CTA's 8 warps
-// (tile columns 64 / KS), U 16-wide k units per warp and chunk (a chunk
-// spans 16 * U * KS of K).
-constexpr int kStepGemmCfgs = 5;
+// Projection tile configurations: KS K-slices across the CTA's warps, TK
+// 128-wide k steps per warp and chunk.
+constexpr int kStepGemmCfgs = 4;
 constexpr int kStepTileRows = 16;  // output rows of a projection tile
-constexpr int kCfgKS[kStepGemmCfgs] = {1, 1, 2, 4, 4};
-constexpr int kCfgU[kStepGemmCfgs] = {8, 16, 8, 4, 8};
-
-// Shared-memory row stride of a chunk's A rows (32-bit words for fp32,
-// 16-bit for bf16), padded so that one warp's fragment reads spread over all
-// banks, and the floats the staged chunk occupies (fp32: TF32 head and
-// remainder planes).
-__host__ __device__ constexpr int step_a_stride(bool f32, int kc) { return f32 ? kc + 4 : kc + 8; }
-__host__ __device__ constexpr int step_a_floats(bool f32, int kc) {
-  return f32 ? 2 * kStepTileRows * step_a_stride(true, kc) : kStepTileRows * step_a_stride(false, kc) / 2;
-}
-__host__ __device__ constexpr int step_gemm_smem_floats(bool f32, int ks, int u) {
-  return step_a_floats(f32, 16 * u * ks) + (ks - 1) * (8 / ks) * 32 * 4;
-}
+constexpr int kCfgKS[kStepGemmCfgs] = {1, 1, 2, 4};
+constexpr int kCfgTK[kStepGemmCfgs] = {1, 2, 1, 1};
 // Grid-barrier words at the start of the workspace: a base word and an
 // arrival counter kStepBarStride u32 (128 bytes) after it.
 constexpr int kStepBarStride = 32;

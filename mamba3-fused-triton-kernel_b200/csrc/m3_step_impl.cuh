@@ -55,92 +55,76 @@ constexpr int kStepThreads = kRowWarps * 32;
 constexpr int kTileRows = kStepTileRows;
 constexpr int kPrefetchChunk = 4096;
 
+__host__ __device__ constexpr int gemm_smem_floats(int KS, int TK) {
+  return kTileRows * 128 * TK * KS + (KS - 1) * (8 / KS) * 64;
+}
+
+// ---------------------------------------------------------------------------
+// loads
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 bf16x4_to_f4(uint2 t) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+// Four consecutive elements through the read-only path (data constant for
+// the whole launch) or L2 only (data written earlier in this launch).
+template <bool COHERENT>
+__device__ __forceinline__ float4 ld4(const float *p) {
+  if constexpr (COHERENT) return __ldcg(reinterpret_cast<const float4 *>(p));
+  else return __ldg(reinterpret_cast<const float4 *>(p));
+}
+template <bool COHERENT>
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16 *p) {
+  if constexpr (COHERENT) return bf16x4_to_f4(__ldcg(reinterpret_cast<const uint2 *>(p)));
+  else return bf16x4_to_f4(__ldg(reinterpret_cast<const uint2 *>(p)));
+}
+
 __device__ __forceinline__ void st_out(float *p, float v) { *p = v; }
 __device__ __forceinline__ void st_out(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
 // ---------------------------------------------------------------------------
-// projection tiles (tensor cores)
+// projection tiles
 // ---------------------------------------------------------------------------
-//
-// C[M, N] = A[M, K] W[N, K]^T on mma.sync tiles: fp32 operands as three
-// TF32 products (A_lo W_hi + A_hi W_lo + A_hi W_hi, each operand split into
-// a TF32 head and the TF32 rounding of its remainder, so the result carries
-// fp32-level error), bf16 operands as one bf16 product; fp32 accumulation.
-// A CTA computes 16 rows x TC columns; warp w covers the 8 columns
-// n0 + 8 (w / KS) over K slice w % KS of every chunk, and the KS slices are
-// added in slice order through shared memory (deterministic).  Per 16-wide
-// k unit, lane (g = lane / 4, t = lane % 4) supplies k = 4t .. 4t + 3 of A
-// rows g and g + 8 and of W row n0 + g; the MMA's k slots receive a fixed
-// permutation of those k (the same for A and W), which leaves every product
-// and the sum unchanged and lets each lane read its k values with one
-// vector load.  The chunk's 16 A rows are staged in shared memory (fp32:
-// split into head / remainder planes once, for all warps); each warp's W
-// values go straight to registers.  Independent accumulators (k-unit parity
-// x product) keep the MMA dependency chains short; they are added in a
-// fixed order at the end.
 
-__device__ __forceinline__ uint32_t tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+// Sum each of the N values over the warp (N a multiple of 32); afterwards
+// lane l holds the totals of values N/32 * l .. N/32 * l + N/32 - 1 in
+// v[0 .. N/32 - 1] (halving exchanges at offsets 16, 8, 4, 2, 1).
+template <int N>
+__device__ __forceinline__ void warp_transpose_sum(float (&v)[N]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int lvl = 0; lvl < 5; ++lvl) {
+    const int off = 16 >> lvl;
+    const int half = (N / 2) >> lvl;
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float send = upper ? v[q] : v[q + half];
+      const float keep = upper ? v[q + half] : v[q];
+      v[q] = keep + __shfl_xor_sync(kFullMask, send, off);
+    }
+  }
 }
 
-// D += A B for one m16n8k8 TF32 / m16n8k16 bf16 fragment set.
-__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Four consecutive elements: fp32 as float4, bf16 as 4 x 16 bits (uint2),
-// through the read-only path (data constant for the whole launch) or L2
-// only (data written earlier in this launch).
-template <typename T> struct Quad;
-template <> struct Quad<float> { using V = float4; };
-template <> struct Quad<__nv_bfloat16> { using V = uint2; };
-
-template <bool COHERENT, typename T>
-__device__ __forceinline__ typename Quad<T>::V ldq(const T *p) {
-  using V = typename Quad<T>::V;
-  if constexpr (COHERENT) return __ldcg(reinterpret_cast<const V *>(p));
-  else return __ldg(reinterpret_cast<const V *>(p));
-}
-template <typename T> __device__ __forceinline__ typename Quad<T>::V zero_quad();
-template <> __device__ __forceinline__ float4 zero_quad<float>() { return make_float4(0.f, 0.f, 0.f, 0.f); }
-template <> __device__ __forceinline__ uint2 zero_quad<__nv_bfloat16>() { return make_uint2(0u, 0u); }
-
-// All tiles of C assigned to this CTA (tile t to CTA t mod gridDim.x).
-// K, lda, ldw multiples of 4; A/W 16-byte (f32) or 8-byte (bf16) aligned.
-// `pre()` runs once, by every thread, after the first tile's weights have
-// been requested and before A is read (A may be produced by other CTAs up
-// to that point).
-template <typename T, int KS, int U, bool ACOH, typename Pre>
+// All tiles of C[M, N] = A[M, K] W[N, K]^T assigned to this CTA (tile t to
+// CTA t mod gridDim.x).  K, lda, ldw multiples of 4; A/W 16-byte (f32) or
+// 8-byte (bf16) aligned.  `pre()` runs once, by every thread, after the
+// first tile's weights have been requested and before A is read (A may be
+// produced by other CTAs up to that point).
+template <typename T, int KS, int TK, bool ACOH, typename Pre>
 __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
   extern __shared__ __align__(16) float smem[];  // the kernel's dynamic shared memory
-  constexpr bool F32 = sizeof(T) == 4;
-  using Q = typename Quad<T>::V;
-  constexpr int NCG = 8 / KS;                      // column groups of 8
-  constexpr int TC = 8 * NCG;                      // tile columns
-  constexpr int KW = 16 * U;                       // k per warp and chunk
-  constexpr int KC = KW * KS;                      // k per chunk
+  constexpr int NCG = 8 / KS;    // column groups of 4
+  constexpr int TC = 4 * NCG;    // tile columns
+  constexpr int KW = 128 * TK;   // k per warp and chunk
+  constexpr int KC = KW * KS;    // k per chunk
   constexpr int KC4 = KC / 4;
-  constexpr int AST = step_a_stride(F32, KC);      // A row stride in shared memory (32- or 16-bit words)
-  uint32_t *Ahi = reinterpret_cast<uint32_t *>(smem);  // f32: TF32 heads [16][AST]
-  uint32_t *Alo = Ahi + kTileRows * AST;                // f32: TF32 remainders [16][AST]
-  uint16_t *Ab = reinterpret_cast<uint16_t *>(smem);   // bf16: [16][AST]
-  float *red = smem + step_a_floats(F32, KC);          // [KS - 1][NCG][32][4]
+  float4 *As = reinterpret_cast<float4 *>(smem);  // [16][KC / 4]
+  float *red = smem + kTileRows * KC;              // [KS - 1][NCG][64]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = lane >> 2, tq = lane & 3;
   const int cg = warp / KS, ks = warp - cg * KS;
   const T *A = static_cast<const T *>(g.A);
   const T *W = static_cast<const T *>(g.W);
@@ -151,108 +135,73 @@ __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
 
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int m0 = (tile % mt) * kTileRows;
-    const int n0 = (tile / mt) * TC + 8 * cg;  // this warp's 8 columns
-    const int nw = n0 + gq;                    // the W row this lane reads
-    constexpr int NACC = F32 ? 6 : 4;
-    float da[NACC][4];
+    const int n0 = (tile / mt) * TC + 4 * cg;
+    float acc[64];  // acc[j * 16 + i]: row m0 + i, column n0 + j
 #pragma unroll
-    for (int a = 0; a < NACC; ++a)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) da[a][e] = 0.f;
+    for (int q = 0; q < 64; ++q) acc[q] = 0.f;
 
     for (int kc = 0; kc < g.K; kc += KC) {
-      Q w[U];
+      float4 w[4][TK];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = kc + ks * KW + 16 * u + 4 * tq;
-        w[u] = (nw < g.N && k < g.K) ? ldq<false>(W + (int64_t)nw * g.ldw + k) : zero_quad<T>();
-      }
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int t = 0; t < TK; ++t) {
+          const int k = kc + ks * KW + 128 * t + 4 * lane;
+          w[j][t] = (n0 + j < g.N && k < g.K) ? ld4<false>(W + (int64_t)(n0 + j) * g.ldw + k)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       if (tile == (int)blockIdx.x && kc == 0) pre();
       // every A load of the chunk is in flight before the first is stored
       constexpr int NLD = kTileRows * KC4 / kStepThreads;
-      Q av[NLD];
+      float4 av[NLD];
 #pragma unroll
       for (int q = 0; q < NLD; ++q) {
         const int v = tid + q * kStepThreads;
         const int i = v / KC4, k = kc + 4 * (v - i * KC4);
-        av[q] = (m0 + i < g.M && k < g.K) ? ldq<ACOH>(A + (int64_t)(m0 + i) * g.lda + k) : zero_quad<T>();
+        av[q] = (m0 + i < g.M && k < g.K) ? ld4<ACOH>(A + (int64_t)(m0 + i) * g.lda + k)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int q = 0; q < NLD; ++q) {
-        const int v = tid + q * kStepThreads;
-        const int i = v / KC4, k4 = v - i * KC4;
-        if constexpr (F32) {
-          const float4 x = av[q];
-          uint4 hi, lo;
-          hi.x = tf32_rna(x.x); lo.x = tf32_rna(x.x - __uint_as_float(hi.x));
-          hi.y = tf32_rna(x.y); lo.y = tf32_rna(x.y - __uint_as_float(hi.y));
-          hi.z = tf32_rna(x.z); lo.z = tf32_rna(x.z - __uint_as_float(hi.z));
-          hi.w = tf32_rna(x.w); lo.w = tf32_rna(x.w - __uint_as_float(hi.w));
-          *reinterpret_cast<uint4 *>(Ahi + i * AST + 4 * k4) = hi;
-          *reinterpret_cast<uint4 *>(Alo + i * AST + 4 * k4) = lo;
-        } else {
-          *reinterpret_cast<uint2 *>(Ab + i * AST + 4 * k4) = av[q];
-        }
-      }
+      for (int q = 0; q < NLD; ++q) As[tid + q * kStepThreads] = av[q];
       __syncthreads();
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int kl = ks * KW + 16 * u + 4 * tq;
-        if constexpr (F32) {
-          const uint4 h0 = *reinterpret_cast<const uint4 *>(Ahi + gq * AST + kl);
-          const uint4 h1 = *reinterpret_cast<const uint4 *>(Ahi + (gq + 8) * AST + kl);
-          const uint4 l0 = *reinterpret_cast<const uint4 *>(Alo + gq * AST + kl);
-          const uint4 l1 = *reinterpret_cast<const uint4 *>(Alo + (gq + 8) * AST + kl);
-          const float4 x = w[u];
-          const uint32_t wh0 = tf32_rna(x.x), wh1 = tf32_rna(x.y), wh2 = tf32_rna(x.z), wh3 = tf32_rna(x.w);
-          const uint32_t wl0 = tf32_rna(x.x - __uint_as_float(wh0)), wl1 = tf32_rna(x.y - __uint_as_float(wh1));
-          const uint32_t wl2 = tf32_rna(x.z - __uint_as_float(wh2)), wl3 = tf32_rna(x.w - __uint_as_float(wh3));
-          // k step 0: slots t / t + 4 <- k 4t / 4t + 1; step 1: <- 4t + 2 / 4t + 3
-          float(&d0)[4] = da[3 * (u & 1) + 0];
-          float(&d1)[4] = da[3 * (u & 1) + 1];
-          float(&d2)[4] = da[3 * (u & 1) + 2];
-          mma_tf32(d0, l0.x, l1.x, l0.y, l1.y, wh0, wh1);
-          mma_tf32(d1, h0.x, h1.x, h0.y, h1.y, wl0, wl1);
-          mma_tf32(d2, h0.x, h1.x, h0.y, h1.y, wh0, wh1);
-          mma_tf32(d0, l0.z, l1.z, l0.w, l1.w, wh2, wh3);
-          mma_tf32(d1, h0.z, h1.z, h0.w, h1.w, wl2, wl3);
-          mma_tf32(d2, h0.z, h1.z, h0.w, h1.w, wh2, wh3);
-        } else {
-          // k pairs (2t, 2t + 1) <- (4t, 4t + 1), (2t + 8, 2t + 9) <- (4t + 2, 4t + 3)
-          const uint2 r0 = *reinterpret_cast<const uint2 *>(Ab + gq * AST + kl);
-          const uint2 r1 = *reinterpret_cast<const uint2 *>(Ab + (gq + 8) * AST + kl);
-          const uint2 x = w[u];
-          mma_bf16(da[u & 3], r0.x, r1.x, r0.y, r1.y, x.x, x.y);
+      for (int i = 0; i < kTileRows; ++i) {
+#pragma unroll
+        for (int t = 0; t < TK; ++t) {
+          const float4 a = As[i * KC4 + ks * (KW / 4) + lane + 32 * t];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float &c = acc[j * 16 + i];
+            c = fmaf(a.x, w[j][t].x, c);
+            c = fmaf(a.y, w[j][t].y, c);
+            c = fmaf(a.z, w[j][t].z, c);
+            c = fmaf(a.w, w[j][t].w, c);
+          }
         }
       }
       __syncthreads();
     }
-    // small products first: (lo.hi + hi.lo) of both parities, then hi.hi
-    float d[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if constexpr (F32) d[e] = ((da[0][e] + da[3][e]) + (da[1][e] + da[4][e])) + (da[2][e] + da[5][e]);
-      else d[e] = (da[0][e] + da[1][e]) + (da[2][e] + da[3][e]);
-    }
-    // d: rows m0 + gq (d[0], d[1]) and m0 + gq + 8 (d[2], d[3]), columns n0 + 2tq, n0 + 2tq + 1
+    warp_transpose_sum<64>(acc);  // lane l: outputs 2l, 2l + 1 = column l / 8, rows 2 (l % 8) + {0, 1}
     if constexpr (KS > 1) {
       if (ks > 0) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[(((ks - 1) * NCG + cg) * 32 + lane) * 4 + e] = d[e];
+        red[((ks - 1) * NCG + cg) * 64 + 2 * lane] = acc[0];
+        red[((ks - 1) * NCG + cg) * 64 + 2 * lane + 1] = acc[1];
       }
       __syncthreads();
       if (ks == 0) {
 #pragma unroll
-        for (int s = 1; s < KS; ++s)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) d[e] += red[(((s - 1) * NCG + cg) * 32 + lane) * 4 + e];
+        for (int s = 1; s < KS; ++s) {
+          acc[0] += red[((s - 1) * NCG + cg) * 64 + 2 * lane];
+          acc[1] += red[((s - 1) * NCG + cg) * 64 + 2 * lane + 1];
+        }
       }
     }
     if (ks == 0) {
+      const int n = n0 + (lane >> 3);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int m = m0 + gq + (e >> 1) * 8, n = n0 + 2 * tq + (e & 1);
-        if (m < g.M && n < g.N) st_out(C + (int64_t)m * g.ldc + n, d[e]);
+      for (int e = 0; e < 2; ++e) {
+        const int m = m0 + 2 * (lane & 7) + e;
+        if (m < g.M && n < g.N) st_out(C + (int64_t)m * g.ldc + n, acc[e]);
       }
     }
   }
@@ -323,13 +272,11 @@ __device__ bool grid_barrier(unsigned *ws, unsigned target, int *s_flag) {
 
 template <typename T, bool ACOH, typename Pre>
 __device__ __forceinline__ void gemm_phase(int cfg, const StepGemm &g, Pre pre) {
-  static_assert(kStepGemmCfgs == 5, "one case per configuration");
   switch (cfg) {
-    case 0: gemm_tiles<T, kCfgKS[0], kCfgU[0], ACOH>(g, pre); break;
-    case 1: gemm_tiles<T, kCfgKS[1], kCfgU[1], ACOH>(g, pre); break;
-    case 2: gemm_tiles<T, kCfgKS[2], kCfgU[2], ACOH>(g, pre); break;
-    case 3: gemm_tiles<T, kCfgKS[3], kCfgU[3], ACOH>(g, pre); break;
-    default: gemm_tiles<T, kCfgKS[4], kCfgU[4], ACOH>(g, pre); break;
+    case 0: gemm_tiles<T, 1, 1, ACOH>(g, pre); break;
+    case 1: gemm_tiles<T, 1, 2, ACOH>(g, pre); break;
+    case 2: gemm_tiles<T, 2, 1, ACOH>(g, pre); break;
+    default: gemm_tiles<T, 4, 1, ACOH>(g, pre); break;
   }
 }
 
@@ -400,10 +347,10 @@ int num_sms_current() {
   return cached[dev];
 }
 
-size_t step_smem_bytes(int R, int BD, int A, bool f32) {
+size_t step_smem_bytes(int R, int BD, int A) {
   int f = 2 * row_block_floats(R, BD, A);
   for (int c = 0; c < kStepGemmCfgs; ++c) {
-    const int g = step_gemm_smem_floats(f32, kCfgKS[c], kCfgU[c]);
+    const int g = gemm_smem_floats(kCfgKS[c], kCfgTK[c]);
     f = g > f ? g : f;
   }
   return (size_t)f * sizeof(float);
@@ -412,7 +359,7 @@ size_t step_smem_bytes(int R, int BD, int A, bool f32) {
 template <int BD, int R, typename T, int KP>
 cudaError_t launch_step_t(StepParams &sp, cudaStream_t stream) {
   auto kern = mimo_step_kernel<BD, R, T, KP>;
-  const size_t smem = step_smem_bytes(R, BD, sp.kp.A, sizeof(T) == 4);
+  const size_t smem = step_smem_bytes(R, BD, sp.kp.A);
   static int attr_dev[64] = {0};  // 1 + device once the attribute is set
   static int per_sm_dev[64] = {0};
   static size_t smem_dev[64] = {0};
