@@ -6,24 +6,22 @@
 namespace m3 {
 
 int step_gemm_cfg(int M, int N, int K, int grid) {
-  int best = 0;
-  long long best_cost = -1;
+  int best = -1;
+  long long best_cost = 0;
   for (int c = 0; c < kStepGemmCfgs; ++c) {
-    const int KS = kCfgKS[c], TK = kCfgTK[c];
-    const int KW = 128 * TK, KC = KW * KS;
+    const int KS = kCfgKS[c], KW = kCfgKW[c], KC = KW * KS;
     if ((long long)KW * (KS - 1) >= K) continue;  // a K slice would be empty
-    const long long tiles = (long long)((M + kStepTileRows - 1) / kStepTileRows) * ((N + 4 * (8 / KS) - 1) / (4 * (8 / KS)));
+    const long long tiles = (long long)((M + kStepTileRows - 1) / kStepTileRows) * ((N + 64 / KS - 1) / (64 / KS));
     const long long rounds = (tiles + grid - 1) / grid;
     const long long chunks = (K + KC - 1) / KC;
-    // per tile: a fixed latency (~3 steps of 128 k), the 128-k steps of a
-    // warp, one barrier pair per chunk
-    const long long cost = rounds * (3 + chunks * TK + chunks);
-    if (best_cost < 0 || cost < best_cost) {
+    // per chunk: load latency (~8 units of 32 k) plus a warp's 32-k units
+    const long long cost = rounds * chunks * (8 + KW / 32);
+    if (best < 0 || cost < best_cost) {
       best_cost = cost;
       best = c;
     }
   }
-  return best;
+  return best < 0 ? 0 : best;
 }
 
 cudaError_t launch_mimo_step(StepParams &sp, cudaStream_t stream) {

@@ -6,12 +6,17 @@
 
 namespace m3 {
 
-// Projection tile configurations: KS K-slices across the CTA's warps, TK
-// 128-wide k steps per warp and chunk.
+// Projection tile configurations: KS K-slices across the CTA's 8 warps
+// (tile columns 64 / KS), KW k per warp and chunk (a chunk spans KW * KS).
 constexpr int kStepGemmCfgs = 4;
 constexpr int kStepTileRows = 16;  // output rows of a projection tile
 constexpr int kCfgKS[kStepGemmCfgs] = {1, 1, 2, 4};
-constexpr int kCfgTK[kStepGemmCfgs] = {1, 2, 1, 1};
+constexpr int kCfgKW[kStepGemmCfgs] = {128, 256, 128, 128};
+// Shared floats of a projection tile: the chunk's 16 A rows and the K-slice
+// partial sums.
+__host__ __device__ constexpr int step_gemm_smem_floats(int ks, int kw) {
+  return kStepTileRows * kw * ks + (ks - 1) * (8 / ks) * 32 * 4;
+}
 // Grid-barrier words at the start of the workspace: a base word and an
 // arrival counter kStepBarStride u32 (128 bytes) after it.
 constexpr int kStepBarStride = 32;

@@ -55,9 +55,6 @@ constexpr int kStepThreads = kRowWarps * 32;
 constexpr int kTileRows = kStepTileRows;
 constexpr int kPrefetchChunk = 4096;
 
-__host__ __device__ constexpr int gemm_smem_floats(int KS, int TK) {
-  return kTileRows * 128 * TK * KS + (KS - 1) * (8 / KS) * 64;
-}
 
 // ---------------------------------------------------------------------------
 // loads
@@ -88,16 +85,15 @@ __device__ __forceinline__ void st_out(__nv_bfloat16 *p, float v) { *p = __float
 // projection tiles
 // ---------------------------------------------------------------------------
 
-// Sum each of the N values over the warp (N a multiple of 32); afterwards
-// lane l holds the totals of values N/32 * l .. N/32 * l + N/32 - 1 in
-// v[0 .. N/32 - 1] (halving exchanges at offsets 16, 8, 4, 2, 1).
-template <int N>
-__device__ __forceinline__ void warp_transpose_sum(float (&v)[N]) {
+// Sum each of the 32 values over the 8 lanes of each aligned lane octet
+// (offsets 4, 2, 1, halving exchanges); afterwards the lane at position q
+// of its octet holds the totals of values 4q .. 4q + 3 in v[0 .. 3].
+__device__ __forceinline__ void octet_transpose_sum(float (&v)[32]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int lvl = 0; lvl < 5; ++lvl) {
-    const int off = 16 >> lvl;
-    const int half = (N / 2) >> lvl;
+  for (int lvl = 0; lvl < 3; ++lvl) {
+    const int off = 4 >> lvl;
+    const int half = 16 >> lvl;
     const bool upper = (lane & off) != 0;
 #pragma unroll
     for (int q = 0; q < half; ++q) {
@@ -109,22 +105,32 @@ __device__ __forceinline__ void warp_transpose_sum(float (&v)[N]) {
 }
 
 // All tiles of C[M, N] = A[M, K] W[N, K]^T assigned to this CTA (tile t to
-// CTA t mod gridDim.x).  K, lda, ldw multiples of 4; A/W 16-byte (f32) or
-// 8-byte (bf16) aligned.  `pre()` runs once, by every thread, after the
-// first tile's weights have been requested and before A is read (A may be
-// produced by other CTAs up to that point).
-template <typename T, int KS, int TK, bool ACOH, typename Pre>
+// CTA t mod gridDim.x).  A CTA computes 16 rows x (64 / KS) columns: warp w
+// covers the 8 columns n0 + 8 (w / KS) over K slice w % KS of every chunk
+// (KW k per warp and chunk).  Lane (p = lane / 8, q = lane % 8) holds the
+// weights of columns 2p, 2p + 1 for k = 4q + 32t in registers, reads the
+// chunk's A rows from shared memory (lanes with the same q read the same
+// address: a broadcast) and accumulates 16 rows x 2 columns; one 3-level
+// transpose-sum over each lane octet finishes the 32 sums, and the KS
+// slices are added in slice order through shared memory.  The summation
+// order is fixed by (KS, KW), so results are deterministic.  K, lda, ldw
+// multiples of 4; A/W 16-byte (f32) or 8-byte (bf16) aligned.  `pre()` runs
+// once, by every thread, after the first tile's weights have been
+// requested and before A is read (A may be produced by other CTAs up to
+// that point).
+template <typename T, int KS, int KW, bool ACOH, typename Pre>
 __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
   extern __shared__ __align__(16) float smem[];  // the kernel's dynamic shared memory
-  constexpr int NCG = 8 / KS;    // column groups of 4
-  constexpr int TC = 4 * NCG;    // tile columns
-  constexpr int KW = 128 * TK;   // k per warp and chunk
+  constexpr int NCG = 8 / KS;    // column groups of 8
+  constexpr int TC = 8 * NCG;    // tile columns
   constexpr int KC = KW * KS;    // k per chunk
   constexpr int KC4 = KC / 4;
+  constexpr int NT = KW / 32;    // float4 of each weight row per lane and chunk
   float4 *As = reinterpret_cast<float4 *>(smem);  // [16][KC / 4]
-  float *red = smem + kTileRows * KC;              // [KS - 1][NCG][64]
+  float *red = smem + kTileRows * KC;              // [KS - 1][NCG][32][4]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cp = lane >> 3, kq = lane & 7;
   const int cg = warp / KS, ks = warp - cg * KS;
   const T *A = static_cast<const T *>(g.A);
   const T *W = static_cast<const T *>(g.W);
@@ -135,19 +141,19 @@ __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
 
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int m0 = (tile % mt) * kTileRows;
-    const int n0 = (tile / mt) * TC + 4 * cg;
-    float acc[64];  // acc[j * 16 + i]: row m0 + i, column n0 + j
+    const int nc = (tile / mt) * TC + 8 * cg + 2 * cp;  // this lane's first column
+    float acc[32];  // acc[j * 16 + i]: row m0 + i, column nc + j
 #pragma unroll
-    for (int q = 0; q < 64; ++q) acc[q] = 0.f;
+    for (int q = 0; q < 32; ++q) acc[q] = 0.f;
 
     for (int kc = 0; kc < g.K; kc += KC) {
-      float4 w[4][TK];
+      float4 w[2][NT];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int t = 0; t < TK; ++t) {
-          const int k = kc + ks * KW + 128 * t + 4 * lane;
-          w[j][t] = (n0 + j < g.N && k < g.K) ? ld4<false>(W + (int64_t)(n0 + j) * g.ldw + k)
+        for (int t = 0; t < NT; ++t) {
+          const int k = kc + ks * KW + 32 * t + 4 * kq;
+          w[j][t] = (nc + j < g.N && k < g.K) ? ld4<false>(W + (int64_t)(nc + j) * g.ldw + k)
                                                : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       if (tile == (int)blockIdx.x && kc == 0) pre();
@@ -167,10 +173,10 @@ __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
 #pragma unroll
       for (int i = 0; i < kTileRows; ++i) {
 #pragma unroll
-        for (int t = 0; t < TK; ++t) {
-          const float4 a = As[i * KC4 + ks * (KW / 4) + lane + 32 * t];
+        for (int t = 0; t < NT; ++t) {
+          const float4 a = As[i * KC4 + (ks * KW + 32 * t) / 4 + kq];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             float &c = acc[j * 16 + i];
             c = fmaf(a.x, w[j][t].x, c);
             c = fmaf(a.y, w[j][t].y, c);
@@ -181,26 +187,25 @@ __device__ __noinline__ void gemm_tiles(const StepGemm g, Pre pre) {
       }
       __syncthreads();
     }
-    warp_transpose_sum<64>(acc);  // lane l: outputs 2l, 2l + 1 = column l / 8, rows 2 (l % 8) + {0, 1}
+    octet_transpose_sum(acc);  // lane (p, q): column nc + (q >> 2), rows 4 (q & 3) + {0 .. 3}
     if constexpr (KS > 1) {
       if (ks > 0) {
-        red[((ks - 1) * NCG + cg) * 64 + 2 * lane] = acc[0];
-        red[((ks - 1) * NCG + cg) * 64 + 2 * lane + 1] = acc[1];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[(((ks - 1) * NCG + cg) * 32 + lane) * 4 + e] = acc[e];
       }
       __syncthreads();
       if (ks == 0) {
 #pragma unroll
-        for (int s = 1; s < KS; ++s) {
-          acc[0] += red[((s - 1) * NCG + cg) * 64 + 2 * lane];
-          acc[1] += red[((s - 1) * NCG + cg) * 64 + 2 * lane + 1];
-        }
+        for (int s2 = 1; s2 < KS; ++s2)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] += red[(((s2 - 1) * NCG + cg) * 32 + lane) * 4 + e];
       }
     }
     if (ks == 0) {
-      const int n = n0 + (lane >> 3);
+      const int n = nc + (kq >> 2);
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = m0 + 2 * (lane & 7) + e;
+      for (int e = 0; e < 4; ++e) {
+        const int m = m0 + 4 * (kq & 3) + e;
         if (m < g.M && n < g.N) st_out(C + (int64_t)m * g.ldc + n, acc[e]);
       }
     }
@@ -272,11 +277,12 @@ __device__ bool grid_barrier(unsigned *ws, unsigned target, int *s_flag) {
 
 template <typename T, bool ACOH, typename Pre>
 __device__ __forceinline__ void gemm_phase(int cfg, const StepGemm &g, Pre pre) {
+  static_assert(kStepGemmCfgs == 4, "one case per configuration");
   switch (cfg) {
-    case 0: gemm_tiles<T, 1, 1, ACOH>(g, pre); break;
-    case 1: gemm_tiles<T, 1, 2, ACOH>(g, pre); break;
-    case 2: gemm_tiles<T, 2, 1, ACOH>(g, pre); break;
-    default: gemm_tiles<T, 4, 1, ACOH>(g, pre); break;
+    case 0: gemm_tiles<T, kCfgKS[0], kCfgKW[0], ACOH>(g, pre); break;
+    case 1: gemm_tiles<T, kCfgKS[1], kCfgKW[1], ACOH>(g, pre); break;
+    case 2: gemm_tiles<T, kCfgKS[2], kCfgKW[2], ACOH>(g, pre); break;
+    default: gemm_tiles<T, kCfgKS[3], kCfgKW[3], ACOH>(g, pre); break;
   }
 }
 
@@ -350,7 +356,7 @@ int num_sms_current() {
 size_t step_smem_bytes(int R, int BD, int A) {
   int f = 2 * row_block_floats(R, BD, A);
   for (int c = 0; c < kStepGemmCfgs; ++c) {
-    const int g = gemm_smem_floats(kCfgKS[c], kCfgTK[c]);
+    const int g = step_gemm_smem_floats(kCfgKS[c], kCfgKW[c]);
     f = g > f ? g : f;
   }
   return (size_t)f * sizeof(float);
