@@ -154,7 +154,8 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
  *   in_proj_w    (d_in_proj, d_model) row stride in_proj_stride
  *   out_proj_w   (d_model, d_inner) row stride out_proj_stride
  *   ssm_state, bx_prev, angle_state   as in m3_full_args, in place
- *   out          (B, d_model) row stride out_stride_b
+ *   out          (B, d_model) row stride out_stride_b; device memory or pinned
+ *                host memory (the kernel's stores then go straight to the host)
  *   workspace    device scratch of at least m3_mimo_step_workspace_bytes,
  *                256-byte aligned, ZEROED ONCE before its first use and then
  *                left to the library (it holds the in_proj output, the gated

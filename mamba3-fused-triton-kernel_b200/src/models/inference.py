@@ -37,6 +37,7 @@ this package.  Differences from the reference, all deliberate:
   (the reference stacks the same static buffer seq_len times).
 * ``use_single_launch`` (an extra keyword, default True) selects the
   single-launch step kernel for the full-fused backend where it applies.
+* ``step_host`` (an extension) runs a step from and to pinned host memory.
 """
 
 from __future__ import annotations
@@ -102,6 +103,8 @@ class Mamba3Decoder:
         self._graph_output = None
         self._graph_state = None
         self._fused_cache = None
+        self._host_graph = None
+        self._host_output = None
         self.use_single_launch = bool(use_single_launch)
         self._step_cache = None
 
@@ -133,9 +136,54 @@ class Mamba3Decoder:
             step_fn(self._graph_input, state)
         torch.cuda.synchronize(device)
         self._cuda_graph = torch.cuda.CUDAGraph()
+        self._host_graph = None
+        self._host_output = None
         self._graph_state = state
         with torch.cuda.graph(self._cuda_graph):
             self._graph_output, self._graph_state = step_fn(self._graph_input, self._graph_state)
+
+    def step_host(self, u_host: torch.Tensor) -> torch.Tensor:
+        """One decode step from and to pinned host memory (an extension for
+        serving loops whose token embeddings live on the host).
+
+        ``u_host`` is a pinned (batch, d_model) tensor of the weight dtype.
+        It is copied into the captured graph's input; where the
+        single-launch kernel serves the layer, a second graph of that kernel
+        writes the output rows straight into a pinned host buffer (no
+        device-to-host copy), otherwise the captured step is replayed and its
+        output copied back.  Returns the pinned output buffer once the
+        device is idle: the same tensor every call, so copy it to keep a
+        step's output.  Needs ``warmup_cuda_graph`` first; the state passed
+        there is updated in place.  The first call validates and sets up;
+        later calls only check shape and dtype, run on the current stream and
+        wait with a device-wide synchronise, so call it with the decoder's
+        device current (the usual one-GPU-per-process serving loop)."""
+        if self._host_output is None:
+            if self._cuda_graph is None:
+                raise RuntimeError("step_host needs a captured graph: call warmup_cuda_graph first")
+            dev = self._graph_input.device
+            assert torch.cuda.current_device() == dev.index, "step_host needs the decoder's device current"
+            assert u_host.device.type == "cpu" and u_host.is_pinned(), "u_host must be pinned host memory"
+            self._host_output = torch.empty(self._graph_output.shape, dtype=self._graph_output.dtype,
+                                            pin_memory=True)
+            launch = self._step_cache[1] if self._step_cache is not None else None
+            if launch is not None and launch.accepts(self._graph_input):
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    launch.run(self._graph_input, self._host_output)  # kernel stores reach host memory
+                self._host_graph = g
+        gi = self._graph_input
+        if u_host.shape != gi.shape or u_host.dtype != gi.dtype:
+            raise AssertionError(f"u_host must be {tuple(gi.shape)} {gi.dtype}")
+        gi.copy_(u_host, non_blocking=True)
+        if self._host_graph is not None:
+            self._host_graph.replay()
+        else:
+            self._cuda_graph.replay()
+            self._host_output.copy_(self._graph_output, non_blocking=True)
+        torch.cuda.synchronize()
+        return self._host_output
 
     def step(self, u: torch.Tensor, state: dict) -> tuple:
         """One decode step: u (batch, d_model) -> (out (batch, d_model), state)."""
