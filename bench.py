@@ -62,6 +62,11 @@ WORKLOADS = {
     "mimo_r1_d1024_b4096": (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=1), 4096, "f32"),
     "mimo_r8_d1024_b4096": (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=8), 4096, "f32"),
 }
+# residual stacks: workload -> number of layers (the 24-layer bf16 stack of
+# the reference's multi-GPU configuration)
+STACKS = {"stack24_d2048_b256_bf16": 24}
+WORKLOADS["stack24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4),
+                                        256, "bf16")
 DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
 # Published reference number for the default workload: MIMO d256 B=128
 # full-fused + CUDA graph P50 step latency 0.295 ms on an A100-PCIE-40GB
@@ -210,11 +215,15 @@ def config_dict(workload, kw, batch, world, dtype_name, reference=False):
 
 
 def run_reference(args, kw, batch, dtype_name, rank):
-    """--impl reference: the oracle port of the reference's CPU decode."""
+    """--impl reference: the oracle port of the reference's CPU decode (for a
+    stack: one layer's rate divided by the number of layers)."""
     if rank != 0:
         return
-    cpu_oracle_rate(kw, batch, dtype_name, steps=max(args.warmup, 1), warmup=0)  # warm-up
-    rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=args.steps, warmup=0)
+    layers = STACKS.get(args.workload, 1)
+    steps = args.steps if layers == 1 else min(args.steps, 3)
+    cpu_oracle_rate(kw, batch, dtype_name, steps=max(min(args.warmup, steps), 1), warmup=0)  # warm-up
+    rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=steps, warmup=0)
+    rate /= layers
     ms = 1000.0 * batch / rate
     line = {
         "metric": "decode tokens/s", "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
@@ -226,6 +235,186 @@ def run_reference(args, kw, batch, dtype_name, rank):
         "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
+    """A residual stack of `layers` MIMO blocks decoded token by token through
+    Mamba3StackDecoder, the whole stack step in one CUDA graph.  Same timing
+    rules as the single-layer path: L2 flushed and a CUDA event pair around
+    every timed step, max over ranks.  `roofline` is the library's fused
+    decode kernel of one layer (the projections are cuBLAS bf16 GEMMs, whose
+    rate is reported beside it)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from src.kernels.linear import linear
+    from src.models.mamba3 import MambaBlock
+    from src.models.stack import Mamba3StackDecoder
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    torch.manual_seed(0)
+    mkw = {k: v for k, v in kw.items() if k != "d_model"}
+    blocks = []
+    with torch.no_grad():
+        for _ in range(layers):
+            blk = MambaBlock(kw["d_model"], mkw, device=dev, dtype=wdtype)
+            blk.mixer.in_proj.weight.normal_(0.0, 0.02)
+            blk.mixer.out_proj.weight.normal_(0.0, 0.02)
+            blocks.append(blk)
+    model = blocks[0].mixer
+    dec = Mamba3StackDecoder(blocks, use_cuda_graph=True, use_triton_full_fused=True)
+    states = dec.init_state(batch, device=dev)
+    K, W = args.steps, args.warmup
+    gen = torch.Generator(device="cpu").manual_seed(1 + rank)
+    n_inputs = 16
+    u_host = torch.randn(n_inputs, batch, kw["d_model"], generator=gen).to(wdtype).pin_memory()
+    u_dev = u_host.to(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        dec.warmup_cuda_graph(states, n_warmup=2)
+        for i in range(W):
+            dec.step(u_dev[i % n_inputs], states)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed_loop(fn, n, pre_sync=False):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            if pre_sync:
+                stream.synchronize()
+            else:
+                torch.cuda._sleep(20000)
+            ev[i][0].record(stream)
+            fn(i)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        return np.array([a.elapsed_time(b) for a, b in ev])
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    try:
+        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
+    except ValueError:
+        gpus = list(range(world))
+    sampler = ClockSampler(gpus) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.2)
+    barrier()
+    if sampler:
+        sampler.mark()
+    with torch.no_grad():
+        step_ms = timed_loop(lambda i: dec.step(u_dev[i % n_inputs], states), K)
+    barrier()
+    if sampler:
+        sampler.mark()
+    total_ms = max_over_ranks(float(step_ms.sum()))
+    value = world * batch * K / (total_ms / 1000.0)
+
+    # one layer's fused kernel (roofline) and its two projections
+    es = 2 if wdtype == torch.bfloat16 else 4
+    layer = dec.layers[0]
+    xn = torch.randn(batch, kw["d_model"], device=dev).to(wdtype)
+    with torch.no_grad():
+        zx = linear(xn, model.in_proj.weight)
+        y = torch.zeros(batch, model.d_inner, device=dev, dtype=wdtype)
+        launch = layer._fused_launch(states[0])
+        graphs = []
+        for fn in (lambda: launch.run(zx, y), lambda: linear(xn, model.in_proj.weight),
+                   lambda: linear(y, model.out_proj.weight)):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    fn()
+            stream.wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            graphs.append(g)
+        n_k = min(K, 200)
+        f_ms, gi_ms, go_ms = (timed_loop(lambda i, g=g: g.replay(), n_k) for g in graphs)
+    del graphs
+    k_mean = max_over_ranks(float(f_ms.mean()))
+    nbytes = fused_bytes_per_launch(model, batch, es, es)
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes / (k_mean * 1e-3) / 1e9
+    gemm_flop = 2.0 * batch * model.d_model * (model.d_in_proj + model.d_inner)
+    gemm_ms = float(gi_ms.mean() + go_ms.mean())
+
+    # end to end through the public API: pinned input in, output back to the host
+    out_host = torch.empty(batch, kw["d_model"], dtype=wdtype).pin_memory()
+    u_stage = torch.empty(batch, kw["d_model"], device=dev, dtype=wdtype)
+
+    def e2e_step(i):
+        u_stage.copy_(u_host[i % n_inputs], non_blocking=True)
+        out, _ = dec.step(u_stage, states)
+        out_host.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    barrier()
+    with torch.no_grad():
+        e2e_ms = timed_loop(e2e_step, min(K, 200), pre_sync=True)
+    barrier()
+    e2e_total = max_over_ranks(float(e2e_ms.sum()))
+    e2e_value = world * batch * len(e2e_ms) / (e2e_total / 1000.0)
+    clocks = sampler.stop() if sampler else None
+
+    cpu = None
+    if rank == 0 and world == 1:
+        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
+        cpu = {"value": round(rate / layers, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} oracle decode steps of one layer x {batch} sequences, rate divided by "
+                         f"{layers} layers (numpy float32 restatement with bf16 rounding)"}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        cfg = config_dict(args.workload, kw, batch, world, dtype_name)
+        cfg.update({"layers": layers, "step": "CUDA-graph replay of Mamba3StackDecoder.step: per layer "
+                    "in_proj (cuBLAS bf16) + fused decode kernel + out_proj (cuBLAS bf16), residual add + "
+                    "RMSNorm kernel between blocks"})
+        line = {
+            "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
+            "p50_step_ms": round(max_over_ranks(float(np.percentile(step_ms, 50))), 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": dtype_name, "data": "synthetic", "config": cfg,
+            "roofline": {"bound": "hbm", "kernel": "fused decode (m3_mimo_full_fused), one layer",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
+                         "mean_launch_ms": round(k_mean, 5), "traffic": profile_traffic(args.workload, "fused")},
+            "kernels_ms": {"fused_decode_per_layer": round(k_mean, 5),
+                           "in_proj_gemm_per_layer": round(float(gi_ms.mean()), 5),
+                           "out_proj_gemm_per_layer": round(float(go_ms.mean()), 5),
+                           "projection_tflops": round(gemm_flop / (gemm_ms * 1e-3) / 1e12, 1)},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": batch * kw["d_model"] * es,
+                    "d2h_bytes_per_step": batch * kw["d_model"] * es,
+                    "ms_per_step": round(e2e_total / len(e2e_ms), 5)},
+            "gpu_launches": K * (2 * layers + 1),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    dec._graph = None
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def main():
@@ -246,6 +435,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, kw, batch, dtype_name, rank)
+        return
+    if args.workload in STACKS:
+        run_stack(args, kw, batch, dtype_name, STACKS[args.workload], world, rank, local)
         return
 
     import datetime

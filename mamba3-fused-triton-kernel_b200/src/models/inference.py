@@ -10,8 +10,8 @@
                          projections on the library's small-batch GEMM).
                          MIMO layers the single-launch kernel takes run the
                          whole step -- both projections included -- as ONE
-                         launch (``use_single_launch``, default on) at
-                         batch sizes up to SINGLE_LAUNCH_MAX_BATCH.
+                         launch (``use_single_launch``, default on) while
+                         the projections are small (single_launch_preferred).
   use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
                          kernel -> out_proj
   use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
@@ -54,10 +54,21 @@ from src.kernels.siso_decode import mamba3_siso_decode_triton
 from src.kernels.siso_decode_fused import mamba3_siso_decode_fused_triton
 from src.kernels.step import prepare_decode_step
 
-# Batches up to this size run the single-launch step; beyond it the
-# projections are large enough for cuBLAS's tiles to win over the
-# single-launch kernel's latency-oriented ones.
+# The single-launch step computes the projections on latency-oriented FP32
+# FMA tiles; once they are large, cuBLAS's tiles (tensor cores for bf16)
+# win.  It serves batches up to SINGLE_LAUNCH_MAX_BATCH whose projection
+# work, 2 * B * d_model * (d_in_proj + d_inner) flop per step, stays within
+# SINGLE_LAUNCH_MAX_FLOP for the weight dtype.
 SINGLE_LAUNCH_MAX_BATCH = 256
+SINGLE_LAUNCH_MAX_FLOP = {torch.float32: 3e8, torch.bfloat16: 1.5e8}
+
+
+def single_launch_preferred(model, batch: int) -> bool:
+    """Whether the decoder uses the single-launch step for this layer and
+    batch (when the kernel takes the layer at all)."""
+    flop = 2.0 * batch * model.d_model * (model.d_in_proj + model.d_inner)
+    limit = SINGLE_LAUNCH_MAX_FLOP.get(model.in_proj.weight.dtype, 0.0)
+    return batch <= SINGLE_LAUNCH_MAX_BATCH and flop <= limit
 from src.kernels.utils import apply_rope
 from src.models.mamba3 import Mamba3
 
@@ -269,8 +280,8 @@ class Mamba3Decoder:
                tuple((t.data_ptr(), tuple(t.shape)) for t in
                      (state["ssm_state"], state["bx_prev"], state["angle_state"])))
         if self._step_cache is None or self._step_cache[0] != key:
-            small = state["ssm_state"].shape[0] <= SINGLE_LAUNCH_MAX_BATCH
-            self._step_cache = (key, prepare_decode_step(m, state) if small else None)
+            use = single_launch_preferred(m, state["ssm_state"].shape[0])
+            self._step_cache = (key, prepare_decode_step(m, state) if use else None)
         return self._step_cache[1]
 
     def _step_triton_full_fused(self, u: torch.Tensor, state: dict) -> tuple:

@@ -123,15 +123,19 @@ def test_barrier_words_advance_by_two_grids():
     assert nat.device_error() == 0
 
 
-def test_decoder_policy_caps_the_batch():
-    from src.models.inference import SINGLE_LAUNCH_MAX_BATCH
-    _, _, _, model = _layer(64, 16, 16, 2, seed=4)
+def test_decoder_policy_bounds_the_projection_work():
+    from src.models.inference import SINGLE_LAUNCH_MAX_BATCH, single_launch_preferred
+    _, _, _, small = _layer(64, 16, 16, 2, seed=4)
     for B, expect in ((SINGLE_LAUNCH_MAX_BATCH, True), (SINGLE_LAUNCH_MAX_BATCH + 1, False)):
-        dec = Mamba3Decoder(model, use_triton_full_fused=True)
+        assert single_launch_preferred(small, B) == expect
+        dec = Mamba3Decoder(small, use_triton_full_fused=True)
         st = dec.init_state(B, device="cuda")
         with torch.no_grad():
             dec.step(torch.randn(B, 64, device="cuda"), st)
         assert (dec._step_cache[1] is not None) == expect, B
+    # a wide bf16 layer: large projections go to cuBLAS even at small batch
+    _, _, _, wide = _layer(512, 128, 64, 8, seed=5, dtype=torch.bfloat16)
+    assert single_launch_preferred(wide, 8) and not single_launch_preferred(wide, 128)
 
 
 def test_layers_outside_the_range_fall_back():
