@@ -19,14 +19,17 @@ using row::kRowWarps;
 using row::row_block_floats;
 
 // The standalone full-step kernel: one CTA per (head group, run of rows).
-template <int BD, int R, typename T, int KP>
-__global__ void __launch_bounds__(kRowWarps * 32, 4) mimo_row_kernel(const KParams p, const int rows_per_cta) {
+// PRE: per-head parameters held in registers across the CTA's rows (wider
+// state rows, 2 CTAs per SM with twice the registers); otherwise re-read per
+// row through the read-only cache (4 CTAs per SM).
+template <int BD, int R, typename T, int KP, bool PRE>
+__global__ void __launch_bounds__(kRowWarps * 32, PRE ? 2 : 4) mimo_row_kernel(const KParams p, const int rows_per_cta) {
   extern __shared__ __align__(16) float smem[];
   const int ngrp = p.H / kRowWarps;
   const int grp = blockIdx.x % ngrp;
   const int b0 = (blockIdx.x / ngrp) * rows_per_cta;
   const int b1 = min(p.B, b0 + rows_per_cta);
-  row::mimo_row_block<BD, R, T, KP, false, false>(p, grp, b0, b1, smem, [] {
+  row::mimo_row_block<BD, R, T, KP, false, PRE>(p, grp, b0, b1, smem, [] {
     pdl_wait();
     pdl_trigger();
   });
@@ -59,7 +62,7 @@ bool row_eligible(const KParams &kp, int es, int VW) {
 
 template <int BD, int R, typename T, int KP>
 cudaError_t launch_row_kp(const KParams &kp, cudaStream_t stream) {
-  auto kern = mimo_row_kernel<BD, R, T, KP>;
+  auto kern = mimo_row_kernel<BD, R, T, KP, (BD >= 128)>;
   const size_t smem = 2 * (size_t)row_block_floats(R, BD, kp.A) * sizeof(float);
   static bool attr = false;
   static size_t last_smem = (size_t)-1;
