@@ -308,8 +308,9 @@ int m3_device_error(int reset) {
   const int a = m3::siso_device_error(reset != 0);
   const int b = m3::mimo_device_error(reset != 0);
   const int c = m3::step_device_error(reset != 0);
-  if (a < 0 || b < 0 || c < 0) return -1;
-  return a | b | c;
+  const int d = m3::mimo_stream_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
+  return a | b | c | d;
 }
 
 int m3_selftest_wait_timeout(m3_stream_t stream) {

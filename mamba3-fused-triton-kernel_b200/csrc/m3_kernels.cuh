@@ -462,6 +462,9 @@ __global__ void __launch_bounds__(256) mimo_decode_kernel(const KParams p) {
 // Launchers (defined in m3_siso.cu / m3_mimo.cu); return the launch status.
 cudaError_t launch_siso(const KParams &kp, bool full, cudaStream_t stream);
 cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
+// The streamed MIMO full-step kernel (m3_mimo_stream.cu); *taken is false
+// when the call's shapes or alignment are outside its range.
+cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *taken);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
                                     int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,
@@ -473,6 +476,7 @@ cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, i
 // Device error words of the kernel translation units (read, optionally clear).
 int siso_device_error(bool reset);
 int mimo_device_error(bool reset);
+int mimo_stream_device_error(bool reset);
 
 // Heads handled by one CTA of the MIMO kernels.
 int mimo_heads_per_cta(int H);

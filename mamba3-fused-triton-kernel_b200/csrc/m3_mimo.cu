@@ -102,6 +102,10 @@ cudaError_t launch_row(const KParams &kp, cudaStream_t stream, bool *taken) {
 template <int BD, int R>
 cudaError_t launch_full_t(const KParams &kp, cudaStream_t stream) {
   bool taken = false;
+  if (BD >= 64) {
+    cudaError_t e = launch_mimo_stream(kp, stream, &taken);
+    if (e != cudaSuccess || taken) return e;
+  }
   cudaError_t e = kp.zx_dt == M3_BF16 ? launch_row<BD, R, __nv_bfloat16>(kp, stream, &taken)
                                       : launch_row<BD, R, float>(kp, stream, &taken);
   if (e != cudaSuccess || taken) return e;

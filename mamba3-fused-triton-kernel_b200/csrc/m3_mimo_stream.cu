@@ -1,0 +1,605 @@
+// MIMO full-step decode, streamed through shared memory.
+//
+// mimo_stream_kernel does what the row kernel (m3_mimo_row.cuh) does -- the
+// whole MIMO decode update from the raw in_proj row (src/models/mamba3.py:
+// 160-217, 306-353; src/kernels/utils.py:95-148) -- for the shapes where
+// every piece of a batch row can be fetched by 1-D bulk (TMA) copies.  One
+// CTA owns 8 heads (one warp each) and a run of consecutive batch rows:
+//
+//   * one thread keeps the next nstage-1 rows in flight: for each row it
+//     copies the 8 heads' carried state (h, Bx_prev, angles) and the in_proj
+//     pieces the CTA reads (x and z of its heads, the R B-rows and R C-rows,
+//     the angle increments) into a ring stage, completing on that stage's
+//     mbarrier, so the HBM latency of a row overlaps the arithmetic of the
+//     rows before it;
+//   * the per-(row, head) scalars (DT, exp(A DT), the trapezoid weights) are
+//     computed once per 32 rows with one (row, head) pair per thread into a
+//     double-buffered table, instead of once per warp and row;
+//   * per row, each warp RMS-normalises one of the 2R B/C rows into shared
+//     memory; the single CTA barrier of a row publishes them and frees the
+//     previous row's stage for the next copy;
+//   * each warp then updates its head: lane l owns state elements
+//     [VW l, VW l + VW) (every RoPE pair lane-local) and head-dim elements
+//     [PL l, PL l + PL), computes the rotation of its own pairs, and writes
+//     h, Bx, the angles and y with vector stores.
+//
+// The per-head parameters (mimo_x, mimo_o, the B/C biases, the norm
+// weights, D) stay in registers when they fit and are otherwise re-read
+// through the read-only cache.  Every mbarrier wait is bounded; a lost copy
+// stops the CTA, which then waits (bounded) for its other copies in flight.
+#include "m3_async.cuh"
+#include "m3_kernels.cuh"
+#include "m3_mimo_row.cuh"
+
+namespace m3 {
+
+namespace {
+
+constexpr int kWarps = 8;        // heads per CTA
+constexpr int kTableRows = 32;   // rows per chunk of the head-scalar table
+constexpr int kMaxStages = 4;
+
+// Byte layout of one launch's dynamic shared memory, computed on the host.
+struct StreamLayout {
+  int nstage, stage_bytes;
+  int o_h, o_bx, o_ang, o_x, o_z, o_bc, o_araw;  // offsets inside a stage
+  unsigned n_state, n_ang, n_xz, n_bc, n_araw;   // bytes of each copy
+  unsigned tx_state, tx;                         // state bytes, all bytes of a stage
+  int o_bars, o_table, o_nbc, o_ring, smem;      // offsets of the regions
+};
+
+// sin and cos of an accumulated RoPE angle, which grows without bound over
+// a sequence: Cody-Waite reduction (Cody & Waite, "Software Manual for the
+// Elementary Functions", 1980) by 2*pi with the constant split into a float
+// head and a float tail -- each step one fma, whose product is exact -- then
+// the hardware approximations on [-pi, pi], where their absolute error is
+// about 4e-7.  Angles beyond 2^17 take the library's full-range sincosf.
+__device__ __forceinline__ void rope_sincos(float x, float &s, float &c) {
+  constexpr float kInvTwoPi = 0x1.45f306p-3f;   // 1 / (2 pi)
+  constexpr float kTwoPiHi = 0x1.921fb6p+2f;    // 2 pi rounded to float
+  constexpr float kTwoPiLo = -0x1.777a5cp-23f;  // 2 pi - kTwoPiHi, rounded to float
+  if (fabsf(x) <= 131072.f) {
+    const float k = rintf(x * kInvTwoPi);
+    float r = fmaf(-k, kTwoPiHi, x);
+    r = fmaf(-k, kTwoPiLo, r);
+    s = __sinf(r);
+    c = __cosf(r);
+  } else {
+    sincosf(x, &s, &c);
+  }
+}
+
+// Shared-memory loads of N consecutive elements (8- or 16-byte aligned for
+// N > 1) into floats.
+template <int N, typename T> __device__ __forceinline__ void lds_f(const T *p, float (&v)[N]);
+template <> __device__ __forceinline__ void lds_f<1, float>(const float *p, float (&v)[1]) { v[0] = *p; }
+template <> __device__ __forceinline__ void lds_f<2, float>(const float *p, float (&v)[2]) {
+  const float2 t = *reinterpret_cast<const float2 *>(p);
+  v[0] = t.x; v[1] = t.y;
+}
+template <> __device__ __forceinline__ void lds_f<4, float>(const float *p, float (&v)[4]) {
+  const float4 t = *reinterpret_cast<const float4 *>(p);
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+template <> __device__ __forceinline__ void lds_f<1, __nv_bfloat16>(const __nv_bfloat16 *p, float (&v)[1]) {
+  v[0] = __bfloat162float(*p);
+}
+template <> __device__ __forceinline__ void lds_f<2, __nv_bfloat16>(const __nv_bfloat16 *p, float (&v)[2]) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+  v[0] = a.x; v[1] = a.y;
+}
+template <> __device__ __forceinline__ void lds_f<4, __nv_bfloat16>(const __nv_bfloat16 *p, float (&v)[4]) {
+  const uint2 t = *reinterpret_cast<const uint2 *>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// Global stores of N consecutive floats (aligned to N * 4 bytes).
+template <int N> __device__ __forceinline__ void stg_f(float *p, const float (&v)[N]) {
+  if constexpr (N == 4)
+    asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
+                 : "memory");
+  else if constexpr (N == 2)
+    asm volatile("st.global.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(v[0]), "f"(v[1]) : "memory");
+  else
+    *p = v[0];
+}
+
+// y stores: N consecutive outputs as float or bf16 (aligned to their size).
+template <int N> __device__ __forceinline__ void st_y(void *y, int64_t i, const float (&v)[N], int dt) {
+  if (dt == M3_BF16) {
+    __nv_bfloat16 *q = static_cast<__nv_bfloat16 *>(y) + i;
+    if constexpr (N == 1) {
+      *q = __float2bfloat16_rn(v[0]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; j += 2)
+        *reinterpret_cast<__nv_bfloat162 *>(q + j) = __floats2bfloat162_rn(v[j], v[j + 1]);
+    }
+  } else {
+    stg_f<N>(static_cast<float *>(y) + i, v);
+  }
+}
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+template <int BD, int R, typename T, int PL>
+__global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KParams p, const StreamLayout L,
+                                                                      const int rows_per_cta) {
+  using Sh = MimoShape<BD>;
+  constexpr int VW = Sh::VW, F = Sh::F, NP = VW / 2;  // NP RoPE pairs per vector
+  constexpr int NRW = (2 * R + kWarps - 1) / kWarps;   // B/C rows each warp normalises
+  constexpr bool KEEP_B = 2 * R * F * VW <= 32;        // B/C biases in registers
+  constexpr bool KEEP_M = 2 * R * PL <= 32;            // mimo_x / mimo_o in registers
+  constexpr int RB = KEEP_B ? R : 1, RM = KEEP_M ? R : 1;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.o_bars);
+  float4 *table = reinterpret_cast<float4 *>(smem + L.o_table);  // [2][kTableRows][8]
+  float *nbc = reinterpret_cast<float *>(smem + L.o_nbc);        // [2][2R][BD]
+  unsigned char *ring = smem + L.o_ring;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = p.H, P = p.P, D = p.D, A = p.A;
+  const int ngrp = H / kWarps;
+  const int grp = blockIdx.x % ngrp, h0 = grp * kWarps, hh = h0 + warp;
+  const int b0 = (blockIdx.x / ngrp) * rows_per_cta;
+  const int nrows = min(p.B, b0 + rows_per_cta) - b0;
+  const int S = L.nstage;
+  const T *zx = static_cast<const T *>(p.zx);
+  const int so = 2 * p.d_inner + 2 * p.d_bc;  // dd_dt[H] dd_A[H] trap[H] angle[A]
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(smem_addr(&bars[s]), 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  // Row k of this CTA into stage k % S.  The carried state was written by
+  // the previous step's kernel (two or more launches back) and may be
+  // requested before pdl_wait(); the in_proj pieces only after it.
+  auto issue_state = [&](int k) {
+    const int s = k % S;
+    unsigned char *st = ring + (size_t)s * L.stage_bytes;
+    const uint32_t bar = smem_addr(&bars[s]);
+    const int64_t rh = (int64_t)(b0 + k) * H + h0;
+    mbar_arrive_expect_tx(bar, L.tx);
+    bulk_g2s(smem_addr(st + L.o_h), p.h + rh * D, L.n_state, bar);
+    bulk_g2s(smem_addr(st + L.o_bx), p.bx + rh * D, L.n_state, bar);
+    bulk_g2s(smem_addr(st + L.o_ang), p.ang + rh * A, L.n_ang, bar);
+  };
+  auto issue_zx = [&](int k) {
+    const int s = k % S;
+    unsigned char *st = ring + (size_t)s * L.stage_bytes;
+    const uint32_t bar = smem_addr(&bars[s]);
+    const T *row = zx + (int64_t)(b0 + k) * p.zx_sb;
+    bulk_g2s(smem_addr(st + L.o_x), row + p.d_inner + (int64_t)h0 * P, L.n_xz, bar);
+    bulk_g2s(smem_addr(st + L.o_z), row + (int64_t)h0 * P, L.n_xz, bar);
+    bulk_g2s(smem_addr(st + L.o_bc), row + 2 * p.d_inner, L.n_bc, bar);
+    bulk_g2s(smem_addr(st + L.o_araw), row + so + 3 * H, L.n_araw, bar);
+  };
+
+  const int npre = min(S - 1, nrows);
+  if (tid == 0)
+    for (int k = 0; k < npre; ++k) issue_state(k);
+
+  // ---- per-head parameters, constant for the launch ----
+  const T *mxp = static_cast<const T *>(p.mx) + (int64_t)hh * R * P;
+  const T *mop = static_cast<const T *>(p.mo) + (int64_t)hh * R * P;
+  const T *bBp = static_cast<const T *>(p.bB) + (int64_t)hh * R * D;
+  const T *bCp = static_cast<const T *>(p.bC) + (int64_t)hh * R * D;
+  float mx[RM][PL], mo[RM][PL];
+  if constexpr (KEEP_M) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        mx[r][j] = row::ldg_f(mxp + r * P + lane * PL + j);
+        mo[r][j] = row::ldg_f(mop + r * P + lane * PL + j);
+      }
+  }
+  float bb[RB][F][VW], bc[RB][F][VW];
+  if constexpr (KEEP_B) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const int col = (lane + 32 * f) * VW;
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          bb[r][f][e] = col < D ? row::ldg_f(bBp + r * D + col + e) : 0.f;
+          bc[r][f][e] = col < D ? row::ldg_f(bCp + r * D + col + e) : 0.f;
+        }
+      }
+  }
+  float wn[NRW][F][VW];  // norm weights of the B/C rows this warp normalises
+#pragma unroll
+  for (int j = 0; j < NRW; ++j) {
+    const int rr = warp + kWarps * j;
+    const T *w = static_cast<const T *>(rr < R ? p.wB : p.wC);
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int col = (lane + 32 * f) * VW;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) wn[j][f][e] = (rr < 2 * R && col < D) ? row::ldg_f(w + col + e) : 0.f;
+    }
+  }
+  const float dskip = row::ldg_f(static_cast<const T *>(p.Dp) + hh);
+  const float dtb_t = row::ldg_f(static_cast<const T *>(p.dt_bias) + h0 + (tid & 7));  // table column
+  const float inv_d = 1.f / (float)D;
+
+  // ---- head-scalar table: thread (j = tid / 8, w = tid % 8) owns row j of
+  // a 32-row chunk and head h0 + w (src/models/mamba3.py:196-199) ----
+  float traw[3];
+  auto table_load = [&](int c) {
+    const int k = c * kTableRows + (tid >> 3);
+    if (k < nrows) {
+      const T *sr = zx + (int64_t)(b0 + k) * p.zx_sb + so + h0 + (tid & 7);
+      traw[0] = row::ldg_f(sr);
+      traw[1] = row::ldg_f(sr + H);
+      traw[2] = row::ldg_f(sr + 2 * H);
+    }
+  };
+  auto table_store = [&](int c) {
+    const int k = c * kTableRows + (tid >> 3);
+    if (k < nrows) {
+      const float dd_A = traw[1];
+      float A_val;
+      if (p.A_floor > 0.f) {
+        // softplus(.) >= 0 > -A_floor for every non-NaN input, so the clamp
+        // returns -A_floor; a NaN propagates as in torch.clamp
+        A_val = dd_A != dd_A ? dd_A : p.A_floor;
+      } else {
+        const float sp = softplus_f(dd_A);
+        A_val = -(sp > -p.A_floor ? -p.A_floor : sp);
+      }
+      const float DT = softplus_f(traw[0] + dtb_t);
+      const float tr = sigmoid_f(traw[2]);
+      // h = exp(A DT) h + DT ((1 - tr) Bx + tr/2 (Bx + Bx_prev))
+      //   = exp(A DT) h + c1 Bx + c2 Bx_prev   (src/kernels/utils.py:95-99)
+      table[(c & 1) * kTableRows * kWarps + tid] =
+          make_float4(expf(A_val * DT), DT * (1.f - tr * 0.5f), DT * (tr * 0.5f), DT);
+    }
+  };
+
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0)
+    for (int k = 0; k < npre; ++k) issue_zx(k);
+  table_load(0);
+  table_store(0);
+
+  int k = 0;
+  for (; k < nrows; ++k) {
+    const int s = k % S;
+    const unsigned char *st = ring + (size_t)s * L.stage_bytes;
+    const bool ok = mbar_wait(smem_addr(&bars[s]), (uint32_t)((k / S) & 1));
+    float *nb = nbc + (k & 1) * 2 * R * BD;
+
+    // ---- phase A: RMSNorm of the 2R B/C rows (src/models/mamba3.py:34-36) ----
+    const T *sbc = reinterpret_cast<const T *>(st + L.o_bc);
+#pragma unroll
+    for (int j = 0; j < NRW; ++j) {
+      const int rr = warp + kWarps * j;
+      if (rr < 2 * R) {
+        float v[F][VW];
+        float ss = 0.f;
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const int col = (lane + 32 * f) * VW;
+          if (col < D) {
+            lds_f<VW, T>(sbc + rr * D + col, v[f]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) v[f][e] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < VW; ++e) ss = fmaf(v[f][e], v[f][e], ss);
+        }
+        ss = group_sum<32>(ss);
+        const float rinv = rsqrtf(ss * inv_d + kRmsEps);
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const int col = (lane + 32 * f) * VW;
+          if (col < D) {
+            float o[VW];
+#pragma unroll
+            for (int e = 0; e < VW; ++e) o[e] = v[f][e] * rinv * wn[j][f][e];
+            if constexpr (VW == 4)
+              *reinterpret_cast<float4 *>(nb + rr * BD + col) = make_float4(o[0], o[1], o[2], o[3]);
+            else
+              *reinterpret_cast<float2 *>(nb + rr * BD + col) = make_float2(o[0], o[1]);
+          }
+        }
+      }
+    }
+    // next table chunk: raw scalars requested 8 rows before they are stored,
+    // stored 16 rows before the chunk starts (its buffer was last read two or
+    // more rows ago, which the barriers since then have retired)
+    if (k % kTableRows == kTableRows / 4 && (k / kTableRows + 1) * kTableRows < nrows) table_load(k / kTableRows + 1);
+    if (k % kTableRows == kTableRows / 2 && (k / kTableRows + 1) * kTableRows < nrows) table_store(k / kTableRows + 1);
+
+    // the one barrier of a row: normalised rows visible, previous stage free
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0 && k + S - 1 < nrows) {
+      issue_state(k + S - 1);
+      issue_zx(k + S - 1);
+    }
+
+    // ---- phase B: this warp's head ----
+    const int b = b0 + k;
+    const float4 hs = table[((k / kTableRows) & 1) * kTableRows * kWarps + (k % kTableRows) * kWarps + warp];
+    const float DT = hs.w;
+
+    // accumulated angles of this lane's RoPE pairs, written back
+    // (src/models/mamba3.py:326-327)
+    float rc[F][NP], rs[F][NP];
+    {
+      const float *sang = reinterpret_cast<const float *>(st + L.o_ang) + warp * A;
+      const T *sraw = reinterpret_cast<const T *>(st + L.o_araw);
+      float *gang = p.ang + ((int64_t)b * H + hh) * A;
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const int i0 = (lane + 32 * f) * NP;
+        if (i0 < A) {  // A is a multiple of 4: all NP pairs rotate
+          float a[NP], raw[NP];
+          lds_f<NP, float>(sang + i0, a);
+          lds_f<NP, T>(sraw + i0, raw);
+          // angle_state + angle_raw * DT, rounded after each operation as the
+          // reference's two tensor operations are
+#pragma unroll
+          for (int q = 0; q < NP; ++q) a[q] = __fadd_rn(a[q], __fmul_rn(raw[q], DT));
+          stg_f<NP>(gang + i0, a);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) rope_sincos(a[q], rs[f][q], rc[f][q]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            rc[f][q] = 1.f;
+            rs[f][q] = 0.f;
+          }
+        }
+      }
+    }
+
+    // x_r = sum_p x_p mimo_x[h, r, p]
+    float xr[R];
+    {
+      const T *sx = reinterpret_cast<const T *>(st + L.o_x) + warp * P;
+      float xv[PL];
+      lds_f<PL, T>(sx + lane * PL, xv);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float t = 0.f;
+#pragma unroll
+        for (int j = 0; j < PL; ++j) {
+          float m;
+          if constexpr (KEEP_M) m = mx[r][j];
+          else m = row::ldg_f(mxp + r * P + lane * PL + j);
+          t = fmaf(xv[j], m, t);
+        }
+        xr[r] = t;
+      }
+      row::warp_allreduce_ranks<R>(xr);
+    }
+
+    // Bx = RoPE(sum_r x_r (Bn_r + bias_r)), the trapezoidal update, and the
+    // readout y_r = <Cn_r + cbias_r, RoPE^-1(h)> (rotations are orthogonal)
+    float yr[R];
+    {
+      const float *sh = reinterpret_cast<const float *>(st + L.o_h) + warp * D;
+      const float *sb = reinterpret_cast<const float *>(st + L.o_bx) + warp * D;
+      const int64_t gbase = ((int64_t)b * H + hh) * D;
+      const float2 dec2 = f2(hs.x, hs.x), c12 = f2(hs.y, hs.y), c22 = f2(hs.z, hs.z);
+      float2 part[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) part[r] = f2(0.f, 0.f);
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const int col = (lane + 32 * f) * VW;
+        if (col < D) {
+          float hv[VW], bp[VW];
+          lds_f<VW, float>(sh + col, hv);
+          lds_f<VW, float>(sb + col, bp);
+          float2 acc[NP];
+#pragma unroll
+          for (int q = 0; q < NP; ++q) acc[q] = f2(0.f, 0.f);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            float n[VW], bias[VW];
+            lds_f<VW, float>(nb + r * BD + col, n);
+            if constexpr (KEEP_B) {
+#pragma unroll
+              for (int e = 0; e < VW; ++e) bias[e] = bb[r][f][e];
+            } else {
+              row::ldg_vec<VW>(bBp + r * D + col, bias);
+            }
+            const float2 xx = f2(xr[r], xr[r]);
+#pragma unroll
+            for (int q = 0; q < NP; ++q)
+              acc[q] = __ffma2_rn(xx, __fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])), acc[q]);
+          }
+          float bxv[VW], hn[VW], hr[VW];
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            const float c = rc[f][q], sn = rs[f][q];
+            bxv[2 * q] = acc[q].x * c - acc[q].y * sn;
+            bxv[2 * q + 1] = acc[q].x * sn + acc[q].y * c;
+            const float2 t = __ffma2_rn(c22, f2(bp[2 * q], bp[2 * q + 1]),
+                                        __ffma2_rn(c12, f2(bxv[2 * q], bxv[2 * q + 1]),
+                                                   __fmul2_rn(dec2, f2(hv[2 * q], hv[2 * q + 1]))));
+            hn[2 * q] = t.x;
+            hn[2 * q + 1] = t.y;
+            hr[2 * q] = t.x * c + t.y * sn;
+            hr[2 * q + 1] = t.y * c - t.x * sn;
+          }
+          stg_f<VW>(p.h + gbase + col, hn);
+          stg_f<VW>(p.bx + gbase + col, bxv);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            float n[VW], bias[VW];
+            lds_f<VW, float>(nb + (R + r) * BD + col, n);
+            if constexpr (KEEP_B) {
+#pragma unroll
+              for (int e = 0; e < VW; ++e) bias[e] = bc[r][f][e];
+            } else {
+              row::ldg_vec<VW>(bCp + r * D + col, bias);
+            }
+#pragma unroll
+            for (int q = 0; q < NP; ++q)
+              part[r] = __ffma2_rn(__fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])),
+                                   f2(hr[2 * q], hr[2 * q + 1]), part[r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) yr[r] = part[r].x + part[r].y;
+      row::warp_allreduce_ranks<R>(yr);
+#pragma unroll
+      for (int r = 0; r < R; ++r) yr[r] = fmaf(dskip, xr[r], yr[r]);
+    }
+
+    // y_p = sum_r y_r mimo_o[h, r, p], gated by silu(z)
+    {
+      const T *sz = reinterpret_cast<const T *>(st + L.o_z) + warp * P;
+      float zv[PL], yv[PL];
+      lds_f<PL, T>(sz + lane * PL, zv);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) {
+        float t = 0.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float m;
+          if constexpr (KEEP_M) m = mo[r][j];
+          else m = row::ldg_f(mop + r * P + lane * PL + j);
+          t = fmaf(yr[r], m, t);
+        }
+        yv[j] = t * __fdividef(zv[j], 1.f + __expf(-zv[j]));
+      }
+      st_y<PL>(p.y, (int64_t)b * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
+    }
+  }
+  // Normal exit: every issued row was consumed.  After a lost copy, wait
+  // (bounded) for this CTA's copies still in flight before leaving.
+  if (tid == 0 && k < nrows) {
+    for (int q = k; q < min(nrows, k + S - 1); ++q)
+      mbar_wait(smem_addr(&bars[q % S]), (uint32_t)((q / S) & 1), 1 << 16);
+  }
+}
+
+int align16(int x) { return (x + 15) & ~15; }
+
+bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Whether every copy of the streamed kernel starts on a 16-byte boundary and
+// moves a multiple of 16 bytes, and every vector access is aligned.
+bool stream_eligible(const KParams &kp) {
+  const int es = kp.zx_dt == M3_BF16 ? 2 : 4, esy = kp.y_dt == M3_BF16 ? 2 : 4;
+  if (kp.zx_dt != kp.par_dt || kp.H % kWarps != 0 || kp.d_bc != kp.R * kp.D) return false;
+  if (kp.P % 32 != 0 || kp.P > 128 || kp.D < 33 || kp.D > 256 || kp.D % 4 != 0 || kp.A % 4 != 0) return false;
+  if (!aligned(kp.zx, 16) || !aligned(kp.h, 16) || !aligned(kp.bx, 16) || !aligned(kp.ang, 16) || !aligned(kp.y, 16) ||
+      !aligned(kp.bB, 16) || !aligned(kp.bC, 16))
+    return false;
+  if ((kp.zx_sb * es) % 16 || (kp.y_sb * esy) % 16 || (2 * kp.d_inner * es) % 16) return false;
+  const int64_t so = 2 * (int64_t)kp.d_inner + 2 * (int64_t)kp.d_bc;
+  if (((so + 3 * kp.H) * es) % 16 || (kp.A * es) % 16 || (2 * kp.R * kp.D * es) % 16) return false;
+  return true;
+}
+
+StreamLayout make_layout(const KParams &kp, int BD, int nstage) {
+  const int es = kp.zx_dt == M3_BF16 ? 2 : 4;
+  StreamLayout L = {};
+  L.n_state = (unsigned)(kWarps * kp.D * 4);
+  L.n_ang = (unsigned)(kWarps * kp.A * 4);
+  L.n_xz = (unsigned)(kWarps * kp.P * es);
+  L.n_bc = (unsigned)(2 * kp.R * kp.D * es);
+  L.n_araw = (unsigned)(kp.A * es);
+  L.tx_state = 2 * L.n_state + L.n_ang;
+  L.tx = L.tx_state + 2 * L.n_xz + L.n_bc + L.n_araw;
+  int o = 0;
+  L.o_h = o; o += align16((int)L.n_state);
+  L.o_bx = o; o += align16((int)L.n_state);
+  L.o_ang = o; o += align16((int)L.n_ang);
+  L.o_x = o; o += align16((int)L.n_xz);
+  L.o_z = o; o += align16((int)L.n_xz);
+  L.o_bc = o; o += align16((int)L.n_bc);
+  L.o_araw = o; o += align16((int)L.n_araw);
+  L.stage_bytes = align16(o);
+  L.nstage = nstage;
+  int g = 0;
+  L.o_bars = g; g += align16(kMaxStages * 8);
+  L.o_table = g; g += 2 * kTableRows * kWarps * 16;
+  L.o_nbc = g; g += 2 * 2 * kp.R * BD * 4;
+  L.o_ring = g; g += nstage * L.stage_bytes;
+  L.smem = g;
+  return L;
+}
+
+template <int BD, int R, typename T, int PL>
+cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
+  auto kern = mimo_stream_kernel<BD, R, T, PL>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  // the deepest ring that still lets two CTAs share an SM, else one CTA
+  StreamLayout L = make_layout(kp, BD, kMaxStages);
+  for (int s = kMaxStages; s >= 2; --s) {
+    L = make_layout(kp, BD, s);
+    if (L.smem <= 110 * 1024) break;
+  }
+  if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, L.smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ngrp = kp.H / kWarps;
+  const int64_t slots = (int64_t)sms * per_sm;
+  const int64_t items = (int64_t)kp.B * ngrp;
+  int rows = (int)((items + slots - 1) / slots);
+  if (rows < 1) rows = 1;
+  const int64_t grid = (int64_t)ngrp * ((kp.B + rows - 1) / rows);
+  return launch_pdl(kern, dim3((unsigned)grid), dim3(kWarps * 32), (size_t)L.smem, stream, kp, L, rows);
+}
+
+template <int BD, int R, typename T>
+cudaError_t launch_stream_p(const KParams &kp, cudaStream_t stream) {
+  if (kp.P == 32) return launch_stream_t<BD, R, T, 1>(kp, stream);
+  if (kp.P == 64) return launch_stream_t<BD, R, T, 2>(kp, stream);
+  return launch_stream_t<BD, R, T, 4>(kp, stream);  // P == 96 or 128 is rejected below unless 128
+}
+
+template <int BD, typename T>
+cudaError_t launch_stream_r(const KParams &kp, cudaStream_t stream) {
+  switch (kp.R) {
+    case 1: return launch_stream_p<BD, 1, T>(kp, stream);
+    case 2: return launch_stream_p<BD, 2, T>(kp, stream);
+    case 4: return launch_stream_p<BD, 4, T>(kp, stream);
+    default: return launch_stream_p<BD, 8, T>(kp, stream);
+  }
+}
+
+template <typename T>
+cudaError_t launch_stream_d(const KParams &kp, cudaStream_t stream) {
+  if (kp.D <= 64) return launch_stream_r<64, T>(kp, stream);
+  if (kp.D <= 128) return launch_stream_r<128, T>(kp, stream);
+  return launch_stream_r<256, T>(kp, stream);
+}
+
+}  // namespace
+
+cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *taken) {
+  *taken = false;
+  if (!stream_eligible(kp) || (kp.P != 32 && kp.P != 64 && kp.P != 128)) return cudaSuccess;
+  if (kp.R != 1 && kp.R != 2 && kp.R != 4 && kp.R != 8) return cudaSuccess;
+  *taken = true;
+  return kp.zx_dt == M3_BF16 ? launch_stream_d<__nv_bfloat16>(kp, stream) : launch_stream_d<float>(kp, stream);
+}
+
+int mimo_stream_device_error(bool reset) { return device_error_of_this_unit(reset); }
+
+}  // namespace m3
