@@ -53,19 +53,20 @@ struct StreamLayout {
 // Elementary Functions", 1980) by 2*pi with the constant split into a float
 // head and a float tail -- each step one fma, whose product is exact -- then
 // the hardware approximations on [-pi, pi], where their absolute error is
-// about 4e-7.  Angles beyond 2^17 take the library's full-range sincosf.
+// about 4e-7.  Angles beyond 2^17 (and NaN) take the library's full-range
+// sincosf.  Every lane of the warp must call it.
 __device__ __forceinline__ void rope_sincos(float x, float &s, float &c) {
   constexpr float kInvTwoPi = 0x1.45f306p-3f;   // 1 / (2 pi)
   constexpr float kTwoPiHi = 0x1.921fb6p+2f;    // 2 pi rounded to float
   constexpr float kTwoPiLo = -0x1.777a5cp-23f;  // 2 pi - kTwoPiHi, rounded to float
-  if (fabsf(x) <= 131072.f) {
-    const float k = rintf(x * kInvTwoPi);
-    float r = fmaf(-k, kTwoPiHi, x);
-    r = fmaf(-k, kTwoPiLo, r);
-    s = __sinf(r);
-    c = __cosf(r);
-  } else {
-    sincosf(x, &s, &c);
+  const float k = rintf(x * kInvTwoPi);
+  float r = fmaf(-k, kTwoPiHi, x);
+  r = fmaf(-k, kTwoPiLo, r);
+  s = __sinf(r);
+  c = __cosf(r);
+  const bool big = !(fabsf(x) <= 131072.f);
+  if (__any_sync(kFullMask, big)) {
+    if (big) sincosf(x, &s, &c);
   }
 }
 
@@ -124,6 +125,14 @@ template <int N> __device__ __forceinline__ void st_y(void *y, int64_t i, const 
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
+// Read-only global loads of N consecutive elements (aligned to their size).
+template <int N, typename T> __device__ __forceinline__ void ldg_n(const T *p, float (&v)[N]) {
+  if constexpr (N == 1)
+    v[0] = row::ldg_f(p);
+  else
+    row::ldg_vec<N>(p, v);
+}
+
 template <int BD, int R, typename T, int PL>
 __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KParams p, const StreamLayout L,
                                                                       const int rows_per_cta) {
@@ -156,11 +165,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   }
   __syncthreads();
 
-  // Row k of this CTA into stage k % S.  The carried state was written by
-  // the previous step's kernel (two or more launches back) and may be
-  // requested before pdl_wait(); the in_proj pieces only after it.
-  auto issue_state = [&](int k) {
-    const int s = k % S;
+  // Row k of this CTA into stage s (= k % S).  The carried state was
+  // written by the previous step's kernel (two or more launches back) and
+  // may be requested before pdl_wait(); the in_proj pieces only after it.
+  auto issue_state = [&](int k, int s) {
     unsigned char *st = ring + (size_t)s * L.stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
     const int64_t rh = (int64_t)(b0 + k) * H + h0;
@@ -169,8 +177,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
     bulk_g2s(smem_addr(st + L.o_bx), p.bx + rh * D, L.n_state, bar);
     bulk_g2s(smem_addr(st + L.o_ang), p.ang + rh * A, L.n_ang, bar);
   };
-  auto issue_zx = [&](int k) {
-    const int s = k % S;
+  auto issue_zx = [&](int k, int s) {
     unsigned char *st = ring + (size_t)s * L.stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
     const T *row = zx + (int64_t)(b0 + k) * p.zx_sb;
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
 
   const int npre = min(S - 1, nrows);
   if (tid == 0)
-    for (int k = 0; k < npre; ++k) issue_state(k);
+    for (int k = 0; k < npre; ++k) issue_state(k, k);
 
   // ---- per-head parameters, constant for the launch ----
   const T *mxp = static_cast<const T *>(p.mx) + (int64_t)hh * R * P;
@@ -192,12 +199,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   float mx[RM][PL], mo[RM][PL];
   if constexpr (KEEP_M) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int j = 0; j < PL; ++j) {
-        mx[r][j] = row::ldg_f(mxp + r * P + lane * PL + j);
-        mo[r][j] = row::ldg_f(mop + r * P + lane * PL + j);
-      }
+    for (int r = 0; r < R; ++r) {
+      ldg_n<PL>(mxp + r * P + lane * PL, mx[r]);
+      ldg_n<PL>(mop + r * P + lane * PL, mo[r]);
+    }
   }
   float bb[RB][F][VW], bc[RB][F][VW];
   if constexpr (KEEP_B) {
@@ -206,10 +211,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
 #pragma unroll
       for (int f = 0; f < F; ++f) {
         const int col = (lane + 32 * f) * VW;
+        if (col < D) {
+          row::ldg_vec<VW>(bBp + r * D + col, bb[r][f]);
+          row::ldg_vec<VW>(bCp + r * D + col, bc[r][f]);
+        } else {
 #pragma unroll
-        for (int e = 0; e < VW; ++e) {
-          bb[r][f][e] = col < D ? row::ldg_f(bBp + r * D + col + e) : 0.f;
-          bc[r][f][e] = col < D ? row::ldg_f(bCp + r * D + col + e) : 0.f;
+          for (int e = 0; e < VW; ++e) bb[r][f][e] = bc[r][f][e] = 0.f;
         }
       }
   }
@@ -221,8 +228,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
 #pragma unroll
     for (int f = 0; f < F; ++f) {
       const int col = (lane + 32 * f) * VW;
+      if (rr < 2 * R && col < D) {
+        row::ldg_vec<VW>(w + col, wn[j][f]);
+      } else {
 #pragma unroll
-      for (int e = 0; e < VW; ++e) wn[j][f][e] = (rr < 2 * R && col < D) ? row::ldg_f(w + col + e) : 0.f;
+        for (int e = 0; e < VW; ++e) wn[j][f][e] = 0.f;
+      }
     }
   }
   const float dskip = row::ldg_f(static_cast<const T *>(p.Dp) + hh);
@@ -266,15 +277,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   pdl_wait();
   pdl_trigger();
   if (tid == 0)
-    for (int k = 0; k < npre; ++k) issue_zx(k);
-  table_load(0);
-  table_store(0);
+    for (int k = 0; k < npre; ++k) issue_zx(k, k);
+  table_load(0);  // stored after the first row's norms, so the loads overlap its wait
 
-  int k = 0;
+  // stage s = k % S of row k and the parity (k / S) & 1 of its barrier
+  // phase, advanced without division
+  int k = 0, s = 0;
+  uint32_t ph = 0;
   for (; k < nrows; ++k) {
-    const int s = k % S;
     const unsigned char *st = ring + (size_t)s * L.stage_bytes;
-    const bool ok = mbar_wait(smem_addr(&bars[s]), (uint32_t)((k / S) & 1));
+    const bool ok = mbar_wait(smem_addr(&bars[s]), ph);
     float *nb = nbc + (k & 1) * 2 * R * BD;
 
     // ---- phase A: RMSNorm of the 2R B/C rows (src/models/mamba3.py:34-36) ----
@@ -314,6 +326,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
         }
       }
     }
+    if (k == 0) table_store(0);
     // next table chunk: raw scalars requested 8 rows before they are stored,
     // stored 16 rows before the chunk starts (its buffer was last read two or
     // more rows ago, which the barriers since then have retired)
@@ -323,8 +336,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
     // the one barrier of a row: normalised rows visible, previous stage free
     if (__syncthreads_or(!ok)) break;
     if (tid == 0 && k + S - 1 < nrows) {
-      issue_state(k + S - 1);
-      issue_zx(k + S - 1);
+      const int sn = s == 0 ? S - 1 : s - 1;  // (k + S - 1) % S: the previous row's stage
+      issue_state(k + S - 1, sn);
+      issue_zx(k + S - 1, sn);
     }
 
     // ---- phase B: this warp's head ----
@@ -339,25 +353,53 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
       const float *sang = reinterpret_cast<const float *>(st + L.o_ang) + warp * A;
       const T *sraw = reinterpret_cast<const T *>(st + L.o_araw);
       float *gang = p.ang + ((int64_t)b * H + hh) * A;
+      // angle_state + angle_raw * DT, rounded after each operation as the
+      // reference's two tensor operations are
+      if (NP == 2 && A <= 32) {
+        // lanes own pairs (2l, 2l+1): one angle per lane, then each lane
+        // fetches the cos/sin of its two pairs
+        float a = 0.f, sn, cs;
+        if (lane < A) {
+          float raw[1];
+          lds_f<1, T>(sraw + lane, raw);
+          a = __fadd_rn(sang[lane], __fmul_rn(raw[0], DT));
+          gang[lane] = a;
+        }
+        rope_sincos(a, sn, cs);
+        const int src = (2 * lane) & 31;
+        const float c0 = __shfl_sync(kFullMask, cs, src), s0 = __shfl_sync(kFullMask, sn, src);
+        const float c1 = __shfl_sync(kFullMask, cs, src + 1), s1 = __shfl_sync(kFullMask, sn, src + 1);
+        const bool mine = 2 * lane < A;
+        rc[0][0] = mine ? c0 : 1.f;
+        rs[0][0] = mine ? s0 : 0.f;
+        rc[0][NP - 1] = mine ? c1 : 1.f;
+        rs[0][NP - 1] = mine ? s1 : 0.f;
 #pragma unroll
-      for (int f = 0; f < F; ++f) {
-        const int i0 = (lane + 32 * f) * NP;
-        if (i0 < A) {  // A is a multiple of 4: all NP pairs rotate
-          float a[NP], raw[NP];
-          lds_f<NP, float>(sang + i0, a);
-          lds_f<NP, T>(sraw + i0, raw);
-          // angle_state + angle_raw * DT, rounded after each operation as the
-          // reference's two tensor operations are
-#pragma unroll
-          for (int q = 0; q < NP; ++q) a[q] = __fadd_rn(a[q], __fmul_rn(raw[q], DT));
-          stg_f<NP>(gang + i0, a);
-#pragma unroll
-          for (int q = 0; q < NP; ++q) rope_sincos(a[q], rs[f][q], rc[f][q]);
-        } else {
+        for (int f = 1; f < F; ++f)
 #pragma unroll
           for (int q = 0; q < NP; ++q) {
             rc[f][q] = 1.f;
             rs[f][q] = 0.f;
+          }
+      } else {
+        // every lane computes its own pairs (A is a multiple of 4, so a
+        // vector's NP pairs rotate together)
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const int i0 = (lane + 32 * f) * NP;
+          const bool on = i0 < A;
+          const int ic = on ? i0 : 0;
+          float a[NP], raw[NP];
+          lds_f<NP, float>(sang + ic, a);
+          lds_f<NP, T>(sraw + ic, raw);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) a[q] = __fadd_rn(a[q], __fmul_rn(raw[q], DT));
+          if (on) stg_f<NP>(gang + i0, a);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            rope_sincos(a[q], rs[f][q], rc[f][q]);
+            rc[f][q] = on ? rc[f][q] : 1.f;
+            rs[f][q] = on ? rs[f][q] : 0.f;
           }
         }
       }
@@ -479,6 +521,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
       }
       st_y<PL>(p.y, (int64_t)b * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
     }
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
   }
   // Normal exit: every issued row was consumed.  After a lost copy, wait
   // (bounded) for this CTA's copies still in flight before leaving.
@@ -490,6 +536,18 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
 
 int align16(int x) { return (x + 15) & ~15; }
 
+int num_sms_cached() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
 bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Whether every copy of the streamed kernel starts on a 16-byte boundary and
@@ -499,7 +557,8 @@ bool stream_eligible(const KParams &kp) {
   if (kp.zx_dt != kp.par_dt || kp.H % kWarps != 0 || kp.d_bc != kp.R * kp.D) return false;
   if (kp.P % 32 != 0 || kp.P > 128 || kp.D < 33 || kp.D > 256 || kp.D % 4 != 0 || kp.A % 4 != 0) return false;
   if (!aligned(kp.zx, 16) || !aligned(kp.h, 16) || !aligned(kp.bx, 16) || !aligned(kp.ang, 16) || !aligned(kp.y, 16) ||
-      !aligned(kp.bB, 16) || !aligned(kp.bC, 16))
+      !aligned(kp.bB, 16) || !aligned(kp.bC, 16) || !aligned(kp.mx, 16) || !aligned(kp.mo, 16) ||
+      !aligned(kp.wB, 16) || !aligned(kp.wC, 16))
     return false;
   if ((kp.zx_sb * es) % 16 || (kp.y_sb * esy) % 16 || (2 * kp.d_inner * es) % 16) return false;
   const int64_t so = 2 * (int64_t)kp.d_inner + 2 * (int64_t)kp.d_bc;
@@ -545,9 +604,15 @@ cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  // the deepest ring that still lets two CTAs share an SM, else one CTA
-  StreamLayout L = make_layout(kp, BD, kMaxStages);
-  for (int s = kMaxStages; s >= 2; --s) {
+  // the deepest ring (no deeper than this CTA's rows need) that still lets
+  // two CTAs share an SM, else one CTA with two stages
+  const int ngrp0 = kp.H / kWarps;
+  const int64_t slots0 = (int64_t)num_sms_cached() * 2;
+  const int64_t rows0 = ((int64_t)kp.B * ngrp0 + slots0 - 1) / slots0;
+  int want = (int)(rows0 + 1 < kMaxStages ? rows0 + 1 : kMaxStages);
+  if (want < 2) want = 2;
+  StreamLayout L = make_layout(kp, BD, 2);
+  for (int s = want; s >= 2; --s) {
     L = make_layout(kp, BD, s);
     if (L.smem <= 110 * 1024) break;
   }
@@ -555,8 +620,7 @@ cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, L.smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = num_sms_cached();
   const int ngrp = kp.H / kWarps;
   const int64_t slots = (int64_t)sms * per_sm;
   const int64_t items = (int64_t)kp.B * ngrp;
