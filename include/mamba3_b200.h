@@ -146,6 +146,16 @@ int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
 int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, float *C, int64_t ldc,
                   int32_t M, int32_t N, int32_t K, m3_stream_t stream);
 
+/* bf16 linear layer of the decode step's projections on the tensor cores
+ * (tcgen05, fp32 accumulation); same operation and call sites as
+ * m3_linear_f32:  C[m, n] = sum_k A[m, k] * W[n, k].  A: (M, K) bf16 row
+ * stride lda, W: (N, K) bf16 row stride ldw, C: (M, N) row stride ldc in
+ * c_dtype (M3_BF16, rounded to nearest, or M3_F32).  16-byte aligned bases,
+ * K >= 64, K, lda, ldw multiples of 8.  M3_ERR_UNSUPPORTED when the driver
+ * offers no tensor-map encoder. */
+int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
+                   int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream);
+
 /* Arguments of the single-launch decode step (m3_mimo_step).
  *   dtype        M3_F32 or M3_BF16: u, both projection weights, the per-head
  *                parameters (as in m3_full_args), out and the workspace's

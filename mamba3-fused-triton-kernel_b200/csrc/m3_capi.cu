@@ -280,6 +280,21 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
       m3::launch_linear_small_m(A, lda, W, ldw, C, ldc, M, N, K, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
+                   int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream) {
+  if (!A || !W || !C) return M3_ERR_NULL;
+  if (!dtype_ok(c_dtype)) return M3_ERR_DTYPE;
+  if (M < 0 || N <= 0 || K < 64 || lda < K || ldw < K || ldc < N) return M3_ERR_SHAPE;
+  if (K % 8 || lda % 8 || ldw % 8) return M3_ERR_ALIGN;
+  if (!aligned16(A) || !aligned16(W) || !aligned16(C)) return M3_ERR_ALIGN;
+  if (M == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  if (!m3::gemm_bf16_supported(A, lda, W, ldw, C, ldc, M, N, K)) return M3_ERR_UNSUPPORTED;
+  return launch_status(m3::launch_gemm_bf16(A, lda, W, ldw, C, ldc, M, N, K, c_dtype == M3_BF16,
+                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o, int64_t ldo, const float *w,
                         void *x_out, int64_t ldxo, void *xn, int64_t ldn, int32_t M, int32_t N, float eps,
                         m3_stream_t stream) {
@@ -309,8 +324,9 @@ int m3_device_error(int reset) {
   const int b = m3::mimo_device_error(reset != 0);
   const int c = m3::step_device_error(reset != 0);
   const int d = m3::mimo_stream_device_error(reset != 0);
-  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
-  return a | b | c | d;
+  const int e = m3::gemm_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0) return -1;
+  return a | b | c | d | e;
 }
 
 int m3_selftest_wait_timeout(m3_stream_t stream) {

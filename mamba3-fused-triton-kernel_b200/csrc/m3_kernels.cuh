@@ -465,6 +465,11 @@ cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
 // The streamed MIMO full-step kernel (m3_mimo_stream.cu); *taken is false
 // when the call's shapes or alignment are outside its range.
 cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *taken);
+// The tcgen05 bf16 projection GEMM (m3_gemm.cu): y = x . w^T.
+bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
+                         int N, int K);
+cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
+                             int N, int K, bool y_bf16, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
                                     int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,
@@ -477,6 +482,7 @@ cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, i
 int siso_device_error(bool reset);
 int mimo_device_error(bool reset);
 int mimo_stream_device_error(bool reset);
+int gemm_device_error(bool reset);
 
 // Heads handled by one CTA of the MIMO kernels.
 int mimo_heads_per_cta(int H);

@@ -106,6 +106,9 @@ def load(path: str = LIB_PATH):
         lib.m3_linear_f32.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                       c_int32, c_int32, c_int32, c_void_p]
         lib.m3_linear_f32.restype = c_int
+        lib.m3_linear_bf16.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                       c_int32, c_int32, c_int32, c_int32, c_void_p]
+        lib.m3_linear_bf16.restype = c_int
         lib.m3_residual_rmsnorm.argtypes = [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                                             c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32,
                                             c_float, c_void_p]

@@ -2,9 +2,10 @@
 
 ``linear(x, weight)`` computes ``x @ weight.T`` (``nn.Linear`` without bias,
 src/models/mamba3.py:115,158).  Small fp32 batches -- the latency-bound
-decode regime -- run the library's ``m3_linear_f32`` kernel; larger batches
-and bf16 use cuBLAS through ``torch.nn.functional.linear``, where tensor
-cores or large tiles pay.
+decode regime -- run the library's ``m3_linear_f32`` kernel; bf16 batches up
+to ``TC_MAX_M`` rows run the library's tcgen05 GEMM (``m3_linear_bf16``,
+split-K over a thread-block cluster so that a decode batch fills the SMs);
+everything else uses cuBLAS through ``torch.nn.functional.linear``.
 """
 
 from __future__ import annotations
@@ -15,6 +16,7 @@ import torch.nn.functional as F
 from src import _native as nat
 
 SMALL_M_MAX = 256  # batch rows up to which the latency-optimised kernel is used
+TC_MAX_M = 512     # bf16 batch rows up to which the tcgen05 GEMM is used
 
 
 def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
@@ -24,8 +26,33 @@ def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
 
 
+def uses_tc_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    return (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype == torch.bfloat16
+            and weight.dtype == torch.bfloat16 and 0 < x.shape[0] <= TC_MAX_M and x.shape[1] >= 64
+            and x.shape[1] % 8 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
+            and weight.stride(1) == 1 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
+
+
+def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """``x @ weight.T`` on the tcgen05 GEMM (bf16 operands, fp32
+    accumulation, output rounded to ``out_dtype``)."""
+    M, K = x.shape
+    N = weight.shape[0]
+    out = torch.empty(M, N, device=x.device, dtype=out_dtype)
+    code = nat.M3_BF16 if out_dtype == torch.bfloat16 else nat.M3_F32
+    with nat.device_guard(x.device):
+        st = nat.load().m3_linear_bf16(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+                                       out.data_ptr(), out.stride(0), M, N, K, code,
+                                       nat.stream_handle(x.device))
+    nat.check(st, "m3_linear_bf16")
+    return out
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """``x @ weight.T`` for x (M, K), weight (N, K)."""
+    if uses_tc_bf16(x, weight):
+        return linear_bf16(x, weight)
     if not uses_small_m_kernel(x, weight):
         return F.linear(x, weight)
     M, K = x.shape

@@ -49,3 +49,47 @@ def test_dispatch_to_cublas_outside_the_small_batch_regime():
 def test_empty_batch():
     out = linear(torch.zeros(0, 256, device="cuda"), torch.randn(32, 256, device="cuda"))
     assert out.shape == (0, 32)
+
+
+# ---- bf16 projections on the tcgen05 GEMM (m3_linear_bf16) ----
+
+from src.kernels.linear import TC_MAX_M, linear_bf16, uses_tc_bf16  # noqa: E402
+
+TC_SHAPES = [  # M, N, K: the 24-layer stack's in_proj / out_proj, tails in every dimension, split-K
+    (256, 9472, 2048), (256, 2048, 4096), (1, 128, 64), (7, 300, 136), (100, 4176, 512),
+    (512, 512, 1024), (33, 1000, 1000), (300, 64, 72),
+]
+
+
+@pytest.mark.parametrize("M,N,K", TC_SHAPES)
+def test_tc_bf16_matches_float64(M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + 7 * N + 13 * K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    assert uses_tc_bf16(x, w)
+    ref = x.double() @ w.double().T
+    y32 = linear_bf16(x, w, torch.float32)
+    # bf16 products are exact in fp32; the error is the fp32 accumulation's
+    err = (y32.double() - ref).abs().max().item()
+    assert err <= 2e-6 * K ** 0.5 * max(1.0, ref.abs().max().item()), err
+    y = linear(x, w)
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    assert torch.equal(y, y32.bfloat16()), "bf16 output is not the rounded fp32 result"
+
+
+def test_tc_bf16_strided_rows():
+    xb = torch.randn(64, 264, device="cuda").bfloat16()
+    wb = (torch.randn(200, 272, device="cuda") * 0.05).bfloat16()
+    x, w = xb[:, :256], wb[:, :256]
+    assert uses_tc_bf16(x, w)
+    ref = x.double() @ w.double().T
+    torch.testing.assert_close(linear_bf16(x, w, torch.float32).double(), ref, rtol=0, atol=1e-4)
+
+
+def test_tc_bf16_dispatch():
+    w = torch.randn(64, 128, device="cuda").bfloat16()
+    assert not uses_tc_bf16(torch.randn(TC_MAX_M + 1, 128, device="cuda").bfloat16(), w)
+    assert not uses_tc_bf16(torch.randn(4, 128, device="cuda"), w.float())
+    assert not uses_tc_bf16(torch.randn(4, 60, device="cuda").bfloat16(), torch.randn(8, 60, device="cuda").bfloat16())
+    from src import _native as nat
+    assert nat.device_error() == 0
