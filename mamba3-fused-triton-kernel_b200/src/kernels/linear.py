@@ -2,10 +2,11 @@
 
 ``linear(x, weight)`` computes ``x @ weight.T`` (``nn.Linear`` without bias,
 src/models/mamba3.py:115,158).  Small fp32 batches -- the latency-bound
-decode regime -- run the library's ``m3_linear_f32`` kernel; bf16 batches up
-to ``TC_MAX_M`` rows run the library's tcgen05 GEMM (``m3_linear_bf16``,
-split-K over a thread-block cluster so that a decode batch fills the SMs);
-everything else uses cuBLAS through ``torch.nn.functional.linear``.
+decode regime -- run the library's ``m3_linear_f32`` kernel; with
+``TC_ROUTE`` set, bf16 batches up to ``TC_MAX_M`` rows run the library's
+tcgen05 GEMM (``m3_linear_bf16``, split-K over a thread-block cluster so
+that a decode batch fills the SMs); everything else uses cuBLAS through
+``torch.nn.functional.linear``.
 """
 
 from __future__ import annotations
@@ -17,6 +18,7 @@ from src import _native as nat
 
 SMALL_M_MAX = 256  # batch rows up to which the latency-optimised kernel is used
 TC_MAX_M = 512     # bf16 batch rows up to which the tcgen05 GEMM is used
+TC_ROUTE = False   # route bf16 projections to it (off: cuBLAS is faster at the measured shapes)
 
 
 def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
@@ -51,7 +53,7 @@ def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16)
 
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """``x @ weight.T`` for x (M, K), weight (N, K)."""
-    if uses_tc_bf16(x, weight):
+    if TC_ROUTE and uses_tc_bf16(x, weight):
         return linear_bf16(x, weight)
     if not uses_small_m_kernel(x, weight):
         return F.linear(x, weight)

@@ -72,7 +72,7 @@ def test_tc_bf16_matches_float64(M, N, K):
     # bf16 products are exact in fp32; the error is the fp32 accumulation's
     err = (y32.double() - ref).abs().max().item()
     assert err <= 2e-6 * K ** 0.5 * max(1.0, ref.abs().max().item()), err
-    y = linear(x, w)
+    y = linear_bf16(x, w)
     assert y.dtype == torch.bfloat16 and y.shape == (M, N)
     assert torch.equal(y, y32.bfloat16()), "bf16 output is not the rounded fp32 result"
 
