@@ -151,10 +151,18 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
  * m3_linear_f32:  C[m, n] = sum_k A[m, k] * W[n, k].  A: (M, K) bf16 row
  * stride lda, W: (N, K) bf16 row stride ldw, C: (M, N) row stride ldc in
  * c_dtype (M3_BF16, rounded to nearest, or M3_F32).  16-byte aligned bases,
- * K >= 64, K, lda, ldw multiples of 8.  M3_ERR_UNSUPPORTED when the driver
- * offers no tensor-map encoder. */
+ * K >= 64, K, lda, ldw multiples of 8.  When the call splits K, the partial
+ * tiles go through `workspace` (16-byte aligned, at least
+ * m3_linear_bf16_workspace_bytes(M, N, K) bytes, M3_ERR_SHAPE otherwise;
+ * NULL / 0 when that is 0); calls sharing a workspace must not overlap on
+ * the GPU.  M3_ERR_UNSUPPORTED when the driver offers no tensor-map encoder. */
 int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
-                   int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream);
+                   int32_t N, int32_t K, int32_t c_dtype, void *workspace, int64_t workspace_bytes,
+                   m3_stream_t stream);
+
+/* Workspace bytes m3_linear_bf16 needs for this shape on the current device
+ * (0 when it does not split K); negative for an invalid shape. */
+int64_t m3_linear_bf16_workspace_bytes(int32_t M, int32_t N, int32_t K);
 
 /* Arguments of the single-launch decode step (m3_mimo_step).
  *   dtype        M3_F32 or M3_BF16: u, both projection weights, the per-head

@@ -280,8 +280,14 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
       m3::launch_linear_small_m(A, lda, W, ldw, C, ldc, M, N, K, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int64_t m3_linear_bf16_workspace_bytes(int32_t M, int32_t N, int32_t K) {
+  if (M < 0 || N <= 0 || K < 64) return -M3_ERR_SHAPE;
+  return m3::gemm_bf16_workspace_bytes(M, N, K);
+}
+
 int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
-                   int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream) {
+                   int32_t N, int32_t K, int32_t c_dtype, void *workspace, int64_t workspace_bytes,
+                   m3_stream_t stream) {
   if (!A || !W || !C) return M3_ERR_NULL;
   if (!dtype_ok(c_dtype)) return M3_ERR_DTYPE;
   if (M < 0 || N <= 0 || K < 64 || lda < K || ldw < K || ldc < N) return M3_ERR_SHAPE;
@@ -291,8 +297,11 @@ int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void 
   const int st = check_device();
   if (st != M3_OK) return st;
   if (!m3::gemm_bf16_supported(A, lda, W, ldw, C, ldc, M, N, K)) return M3_ERR_UNSUPPORTED;
+  const int64_t need = m3::gemm_bf16_workspace_bytes(M, N, K);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return M3_ERR_SHAPE;
+  if (need > 0 && !aligned16(workspace)) return M3_ERR_ALIGN;
   return launch_status(m3::launch_gemm_bf16(A, lda, W, ldw, C, ldc, M, N, K, c_dtype == M3_BF16,
-                                            reinterpret_cast<cudaStream_t>(stream)));
+                                            static_cast<float *>(workspace), reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o, int64_t ldo, const float *w,

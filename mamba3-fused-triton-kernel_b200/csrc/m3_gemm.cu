@@ -12,15 +12,17 @@
 //   * warp 1 / lane 0 issues four tcgen05.mma (kind::f16: bf16 operands,
 //     fp32 accumulation) per k-tile into one TMEM accumulator of 128 lanes x
 //     NB columns, and hands each stage back with tcgen05.commit;
-//   * when the tiles alone do not fill the SMs, K is split over the CTAs of
-//     a thread-block cluster (up to 8): every CTA moves its accumulator to its
-//     own shared memory, and after a cluster barrier CTA j sums slice j of
-//     the batch rows over all the cluster's shared memory (distributed
-//     shared-memory loads) and writes it.
+//   * the tile width (batch rows per CTA) and a K split are planned per call
+//     so that the CTAs fill the SMs; a split runs its CTAs as one thread-block
+//     cluster (up to 4): every CTA writes its fp32 partial tile to the
+//     caller's workspace, and after a cluster barrier CTA j sums slice j of the
+//     batch rows over the cluster's partials (from L2) and writes it.
+//     Distributed shared memory was tried for that exchange and measured at
+//     about 15 GB/s per CTA -- far slower than L2.
 //
 // All four warps drain TMEM (tcgen05.ld, warp w owns lanes 32w..32w+31).
 // Every mbarrier wait is bounded and records M3_DEVERR_TIMEOUT when it gives
-// up; the cluster barriers are reached on every path.  No load uses cluster
+// up; the cluster barrier is reached on every path.  No load uses cluster
 // multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -37,9 +39,9 @@ namespace {
 constexpr int kTileN = 128;  // weight rows per CTA (MMA M)
 constexpr int kTileK = 64;   // k per stage: one 128-byte swizzle row of bf16
 constexpr int kThreads = 128;
-constexpr int kMaxSplit = 8;
-constexpr int kMaxNB = 256;
+constexpr int kMaxSplit = 4;
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kMaxStages = 8;
 
 struct GemmArgs {
   int M, N;
@@ -54,6 +56,7 @@ struct GemmArgs {
   void *y;
   int64_t ldy;
   int y_bf16;
+  float *ws;       // split-K partial tiles (nsplit > 1)
 };
 
 // UMMA shared-memory descriptor of a K-major operand in the 128-byte swizzle
@@ -93,33 +96,16 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
-// 16 consecutive accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// 16 consecutive accumulator columns of this thread's TMEM lane (read them
+// after tmem_wait).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
+__device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const GemmArgs g) {
@@ -160,18 +146,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // the batch rows are the preceding kernel's product
+  // the weights are constant: the first stages' weight tiles are requested
+  // before waiting for the preceding kernel, whose product the batch rows are
+  const int npre = min(S, nkt);
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+    for (int i = 0; i < npre; ++i) {
+      const uint32_t bar = smem_addr(&full[i]);
+      mbar_arrive_expect_tx(bar, (uint32_t)(g.stage_a + g.stage_b));
+      tma_load_2d(smem_addr(ringA + (size_t)i * g.stage_a), &tw, (kt0 + i) * kTileK, n0, bar);
+    }
+  }
   pdl_wait();
   pdl_trigger();
 
   if (tid == 0) {
     // producer: k-tile i into stage i % S, after the MMAs of k-tile i - S
     // have released it
-    int s = 0;
-    uint32_t ph = 0;
-    int issued = 0;
-    for (int i = 0; i < nkt; ++i) {
-      if (i >= S && !mbar_wait(smem_addr(&empty[s]), ph ^ 1u)) break;
+    for (int i = 0; i < npre; ++i)
+      tma_load_2d(smem_addr(ringB + (size_t)i * g.stage_b), &tx, (kt0 + i) * kTileK, m0, smem_addr(&full[i]));
+    int s = npre % S;
+    uint32_t ph = npre == S ? 1u : 0u;
+    int issued = npre;
+    for (int i = npre; i < nkt; ++i) {
+      if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1u)) break;
       const uint32_t bar = smem_addr(&full[s]);
       mbar_arrive_expect_tx(bar, (uint32_t)(g.stage_a + g.stage_b));
       const int kx = (kt0 + i) * kTileK;
@@ -211,45 +210,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncwarp();
 
-  // accumulator -> this CTA's shared memory, part[m][n] (fp32); the ring
-  // it overwrites was last written by TMA and read by the finished MMAs
   mbar_wait(smem_addr(accum), 0);
   __syncwarp();
   tc_fence_after();
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  float *part = reinterpret_cast<float *>(smem);
   const int nl = 32 * warp + lane;
-  for (int c0 = 0; c0 < g.nb; c0 += 16) {
-    float v[16];
-    tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+  const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+  // Drain the accumulator 64 columns (batch rows) at a time: up to four
+  // tcgen05.ld per wait; `put(m, value)` stores column m of this thread's row.
+  auto drain = [&](auto &&put) {
+    for (int c0 = 0; c0 < g.nb; c0 += 64) {  // nb is a multiple of 16
+      uint32_t v[4][16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) part[(c0 + j) * kTileN + nl] = nkt > 0 ? v[j] : 0.f;
-  }
-  tc_fence_before();
-  if (g.nsplit > 1)
-    cluster_sync();
-  else
-    __syncthreads();
-
-  // CTA `split` sums and writes batch rows [r0, r1) of the tile
-  const int per = (g.nb + g.nsplit - 1) / g.nsplit;
-  const int r0 = split * per, r1 = min(g.nb, r0 + per);
-  const uint32_t pbase = smem_addr(part);
-  const int n = n0 + 4 * lane;
-  for (int mm = r0 + warp; mm < r1; mm += 4) {
-    const uint32_t off = (uint32_t)(mm * kTileN + 4 * lane) * 4u;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (g.nsplit > 1) {
-      for (int q = 0; q < g.nsplit; ++q) {
-        const float4 t = ld_dsmem4(map_rank(pbase + off, (uint32_t)q));
-        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
-      }
-    } else {
-      acc = *reinterpret_cast<const float4 *>(smem + off);
+      for (int q = 0; q < 4; ++q)
+        if (c0 + 16 * q < g.nb) tmem_ld16(trow + (uint32_t)(c0 + 16 * q), v[q]);
+      tmem_wait();
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (c0 + 16 * q < g.nb)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) put(c0 + 16 * q + j, nkt > 0 ? __uint_as_float(v[q][j]) : 0.f);
     }
-    const int m = m0 + mm;
-    if (m >= g.M) continue;
-    const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+  };
+  const int n = n0 + 4 * lane;
+  auto store_row = [&](int m, const float4 a4) {
+    const float o[4] = {a4.x, a4.y, a4.z, a4.w};
     if (g.y_bf16) {
       __nv_bfloat16 *yr = static_cast<__nv_bfloat16 *>(g.y) + (int64_t)m * g.ldy;
       if (n + 3 < g.N && ((g.ldy | n) & 3) == 0) {
@@ -266,17 +250,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       float *yr = static_cast<float *>(g.y) + (int64_t)m * g.ldy;
       if (n + 3 < g.N && ((g.ldy | n) & 3) == 0) {
-        *reinterpret_cast<float4 *>(yr + n) = acc;
+        *reinterpret_cast<float4 *>(yr + n) = a4;
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (n + e < g.N) yr[n + e] = o[e];
       }
     }
+  };
+
+  if (g.nsplit > 1) {
+    // split-K: this CTA's fp32 partial tile -> workspace [m][n] (each warp
+    // store one 128-byte row segment), a cluster barrier, then CTA `split`
+    // sums batch rows [r0, r1) of the tile over the cluster's partials from L2
+    const size_t tile = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+    float *tws = g.ws + tile * g.nsplit * g.nb * kTileN;
+    float *mine = tws + (size_t)split * g.nb * kTileN;
+    drain([&](int m, float v) { __stcg(mine + (size_t)m * kTileN + nl, v); });
+    tc_fence_before();
+    cluster_sync();  // release / acquire at cluster scope: every partial is visible
+    const int per = (g.nb + g.nsplit - 1) / g.nsplit;
+    const int r0 = split * per, r1 = min(g.nb, r0 + per);
+    constexpr int RU = 4;  // rows per warp and pass: RU x nsplit loads in flight
+    for (int base = r0; base < r1; base += 4 * RU) {
+      float4 acc[RU];
+#pragma unroll
+      for (int u = 0; u < RU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < kMaxSplit; ++q) {
+        if (q < g.nsplit) {
+#pragma unroll
+          for (int u = 0; u < RU; ++u) {
+            const int mm = base + 4 * u + warp;
+            if (mm < r1) {
+              const float4 t = __ldcg(reinterpret_cast<const float4 *>(tws + ((size_t)q * g.nb + mm) * kTileN + 4 * lane));
+              acc[u].x += t.x; acc[u].y += t.y; acc[u].z += t.z; acc[u].w += t.w;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < RU; ++u) {
+        const int mm = base + 4 * u + warp;
+        if (mm < r1 && m0 + mm < g.M) store_row(m0 + mm, acc[u]);
+      }
+    }
+  } else {
+    // whole K here: accumulator -> shared memory part[m][n] (the ring it
+    // overwrites was last written by TMA and read by the finished MMAs),
+    // then coalesced row stores
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    float *part = reinterpret_cast<float *>(smem);
+    drain([&](int m, float v) { part[m * kTileN + nl] = v; });
+    tc_fence_before();
+    __syncthreads();
+    for (int mm = warp; mm < g.nb && m0 + mm < g.M; mm += 4)
+      store_row(m0 + mm, *reinterpret_cast<const float4 *>(part + mm * kTileN + 4 * lane));
   }
 
-  // no CTA leaves while a peer may still read its shared memory
-  if (g.nsplit > 1) cluster_sync();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
@@ -322,6 +353,41 @@ int sm_count() {
   return cached[dev];
 }
 
+// Tile width (batch rows per CTA) and K split of one call: the cheapest by
+// a simple model -- each k-tile moves its weight and batch tiles at about
+// 100 GB/s per SM (the operands mostly come from L2), CTAs beyond one per SM
+// run in further waves, and a split adds the partial tiles' write and read.
+struct GemmPlan {
+  int nb, ntiles, mchunks, ktotal, ktiles, nsplit;
+};
+
+GemmPlan plan_gemm(int M, int N, int K) {
+  const int sms = sm_count();
+  const int ntiles = (N + kTileN - 1) / kTileN, ktotal = (K + kTileK - 1) / kTileK;
+  const int mr = (M + 15) / 16 * 16;
+  GemmPlan best = {};
+  double best_cost = 1e30;
+  for (int nb : {256, 128, 64, 32, 16}) {
+    if (nb > mr && nb != 16 && (nb >> 1) >= mr) continue;  // skip widths twice the batch or more
+    const int b = nb < mr ? nb : mr;
+    const int mchunks = (M + b - 1) / b, tiles = ntiles * mchunks;
+    int nsplit = tiles >= sms ? 1 : sms / tiles;
+    nsplit = nsplit < 1 ? 1 : nsplit > kMaxSplit ? kMaxSplit : nsplit;
+    if (nsplit > ktotal) nsplit = ktotal;
+    const int ktiles = (ktotal + nsplit - 1) / nsplit;
+    nsplit = (ktotal + ktiles - 1) / ktiles;  // every split gets at least one k-tile
+    const int waves = (tiles * nsplit + sms - 1) / sms;
+    const double us_per_ktile = (kTileN * kTileK * 2.0 + b * kTileK * 2.0) / 1.0e5;
+    double cost = waves * ktiles * us_per_ktile + b * kTileN * 4.0 / 1.0e5;
+    if (nsplit > 1) cost += 2.0 * b * kTileN * 4.0 / 1.0e5 + 0.7;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = {b, ntiles, mchunks, ktotal, ktiles, nsplit};
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
@@ -331,25 +397,29 @@ bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw,
          ldy >= N && al(x) && al(w) && al(y) && encode_fn() != nullptr;
 }
 
+int64_t gemm_bf16_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K < kTileK) return 0;
+  const GemmPlan pl = plan_gemm(M, N, K);
+  if (pl.nsplit <= 1) return 0;
+  return (int64_t)pl.ntiles * pl.mchunks * pl.nsplit * pl.nb * kTileN * 4;
+}
+
 cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
-                             int N, int K, bool y_bf16, cudaStream_t stream) {
+                             int N, int K, bool y_bf16, float *workspace, cudaStream_t stream) {
+  const GemmPlan pl = plan_gemm(M, N, K);
   GemmArgs g = {};
   g.M = M;
   g.N = N;
-  g.nb = M >= kMaxNB ? kMaxNB : (M + 15) / 16 * 16;
-  g.ktotal = (K + kTileK - 1) / kTileK;
-  const int ntiles = (N + kTileN - 1) / kTileN, mchunks = (M + g.nb - 1) / g.nb;
-  const int sms = sm_count();
-  int nsplit = 1;
-  if (ntiles * mchunks < sms) nsplit = sms / (ntiles * mchunks);
-  nsplit = nsplit < 1 ? 1 : nsplit > kMaxSplit ? kMaxSplit : nsplit;
-  if (nsplit > g.ktotal) nsplit = g.ktotal;
-  g.ktiles = (g.ktotal + nsplit - 1) / nsplit;
-  g.nsplit = (g.ktotal + g.ktiles - 1) / g.ktiles;  // every split gets at least one k-tile
+  g.nb = pl.nb;
+  g.ktotal = pl.ktotal;
+  g.ktiles = pl.ktiles;
+  g.nsplit = pl.nsplit;
+  if (g.nsplit > 1 && workspace == nullptr) return cudaErrorInvalidValue;
+  g.ws = workspace;
   g.stage_a = kTileN * kTileK * 2;
   g.stage_b = g.nb * kTileK * 2;
   int S = kSmemBudget / (g.stage_a + g.stage_b);
-  S = S > 4 ? 4 : S;
+  S = S > kMaxStages ? kMaxStages : S;
   if (S > g.ktiles) S = g.ktiles < 2 ? 2 : g.ktiles;
   g.nstage = S;
   g.tmem_cols = 32;
@@ -370,7 +440,7 @@ cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t 
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ntiles, (unsigned)mchunks, (unsigned)g.nsplit);
+  cfg.gridDim = dim3((unsigned)pl.ntiles, (unsigned)pl.mchunks, (unsigned)g.nsplit);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;

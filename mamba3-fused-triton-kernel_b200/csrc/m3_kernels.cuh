@@ -468,8 +468,9 @@ cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *tak
 // The tcgen05 bf16 projection GEMM (m3_gemm.cu): y = x . w^T.
 bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
                          int N, int K);
+int64_t gemm_bf16_workspace_bytes(int M, int N, int K);
 cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
-                             int N, int K, bool y_bf16, cudaStream_t stream);
+                             int N, int K, bool y_bf16, float *workspace, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
                                     int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,

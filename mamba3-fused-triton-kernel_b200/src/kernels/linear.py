@@ -36,6 +36,22 @@ def uses_tc_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
 
 
+_workspaces: dict = {}  # device index -> split-K workspace, grown on demand and kept
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The device's split-K workspace, at least ``nbytes``.  Calls on one
+    device share it, which is safe because they run in stream order; it is
+    kept for the life of the process (CUDA graphs that captured a call keep
+    pointing at it), so the first calls of each shape should come before
+    capture."""
+    ws = _workspaces.get(device.index)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[device.index] = ws
+    return ws
+
+
 def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     """``x @ weight.T`` on the tcgen05 GEMM (bf16 operands, fp32
     accumulation, output rounded to ``out_dtype``)."""
@@ -43,10 +59,14 @@ def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16)
     N = weight.shape[0]
     out = torch.empty(M, N, device=x.device, dtype=out_dtype)
     code = nat.M3_BF16 if out_dtype == torch.bfloat16 else nat.M3_F32
+    lib = nat.load()
     with nat.device_guard(x.device):
-        st = nat.load().m3_linear_bf16(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
-                                       out.data_ptr(), out.stride(0), M, N, K, code,
-                                       nat.stream_handle(x.device))
+        need = lib.m3_linear_bf16_workspace_bytes(M, N, K)
+        ws = _workspace(x.device, need) if need > 0 else None
+        st = lib.m3_linear_bf16(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+                                out.data_ptr(), out.stride(0), M, N, K, code,
+                                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                                nat.stream_handle(x.device))
     nat.check(st, "m3_linear_bf16")
     return out
 
