@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("M,N", [(1, 64), (7, 2048), (256, 1000), (3, 8192)])
+@pytest.mark.parametrize("M,N", [(1, 64), (7, 2048), (256, 1000), (3, 8192), (5, 1001)])  # 1001: element-wise path
 def test_residual_rmsnorm_matches_torch(dtype, M, N):
     g = torch.Generator(device="cuda").manual_seed(M + N)
     x = torch.randn(M, N, device="cuda", generator=g).to(dtype)
