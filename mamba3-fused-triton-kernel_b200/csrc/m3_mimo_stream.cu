@@ -37,7 +37,7 @@ namespace {
 
 constexpr int kWarps = 8;        // heads per CTA
 constexpr int kTableRows = 32;   // rows per chunk of the head-scalar table
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;  // mbarriers reserved; the ring uses 4 (one row a pass) or 6 (two)
 
 // Byte layout of one launch's dynamic shared memory, computed on the host.
 struct StreamLayout {
@@ -46,6 +46,11 @@ struct StreamLayout {
   unsigned n_state, n_ang, n_xz, n_bc, n_araw;   // bytes of each copy
   unsigned tx_state, tx;                         // state bytes, all bytes of a stage
   int o_bars, o_table, o_nbc, o_ring, smem;      // offsets of the regions
+  // per-head parameters of the CTA's 8 heads staged in shared memory by
+  // bulk copies that complete with the first row (o_par < 0: read from
+  // global memory instead); offsets inside the region and copy bytes
+  int o_par, p_bB, p_bC, p_mx, p_mo, p_wB, p_wC, p_Dp, p_dtb;
+  unsigned n_bBC, n_mxo, n_w, n_h8, n_par;
 };
 
 // sin and cos of an accumulated RoPE angle, which grows without bound over
@@ -54,19 +59,27 @@ struct StreamLayout {
 // head and a float tail -- each step one fma, whose product is exact -- then
 // the hardware approximations on [-pi, pi], where their absolute error is
 // about 4e-7.  Angles beyond 2^17 (and NaN) take the library's full-range
-// sincosf.  Every lane of the warp must call it.
-__device__ __forceinline__ void rope_sincos(float x, float &s, float &c) {
+// sincosf, N angles at a time with one warp vote for that fallback.  Every
+// lane of the warp must call it.
+template <int N>
+__device__ __forceinline__ void rope_sincos_n(const float (&x)[N], float (&s)[N], float (&c)[N]) {
   constexpr float kInvTwoPi = 0x1.45f306p-3f;   // 1 / (2 pi)
   constexpr float kTwoPiHi = 0x1.921fb6p+2f;    // 2 pi rounded to float
   constexpr float kTwoPiLo = -0x1.777a5cp-23f;  // 2 pi - kTwoPiHi, rounded to float
-  const float k = rintf(x * kInvTwoPi);
-  float r = fmaf(-k, kTwoPiHi, x);
-  r = fmaf(-k, kTwoPiLo, r);
-  s = __sinf(r);
-  c = __cosf(r);
-  const bool big = !(fabsf(x) <= 131072.f);
+  bool big = false;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float k = rintf(x[i] * kInvTwoPi);
+    float r = fmaf(-k, kTwoPiHi, x[i]);
+    r = fmaf(-k, kTwoPiLo, r);
+    s[i] = __sinf(r);
+    c[i] = __cosf(r);
+    big = big || !(fabsf(x[i]) <= 131072.f);
+  }
   if (__any_sync(kFullMask, big)) {
-    if (big) sincosf(x, &s, &c);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (!(fabsf(x[i]) <= 131072.f)) sincosf(x[i], &s[i], &c[i]);
   }
 }
 
@@ -133,14 +146,25 @@ template <int N, typename T> __device__ __forceinline__ void ldg_n(const T *p, f
     row::ldg_vec<N>(p, v);
 }
 
-template <int BD, int R, typename T, int PL>
+// A parameter vector: from its staged copy (byte offset `off` in the
+// shared-memory region at `base`) or from global memory.
+template <int N, typename T>
+__device__ __forceinline__ void ld_param(bool staged, const unsigned char *base, int off, const T *g, float (&v)[N]) {
+  if (staged)
+    lds_f<N, T>(reinterpret_cast<const T *>(base + off), v);
+  else
+    ldg_n<N>(g, v);
+}
+
+template <int BD, int R, typename T, int PL, int RP>
 __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KParams p, const StreamLayout L,
                                                                       const int rows_per_cta) {
   using Sh = MimoShape<BD>;
   constexpr int VW = Sh::VW, F = Sh::F, NP = VW / 2;  // NP RoPE pairs per vector
   constexpr int NRW = (2 * R + kWarps - 1) / kWarps;   // B/C rows each warp normalises
-  constexpr bool KEEP_B = 2 * R * F * VW <= 32;        // B/C biases in registers
-  constexpr bool KEEP_M = 2 * R * PL <= 32;            // mimo_x / mimo_o in registers
+  // per-head parameters held in registers when they fit beside RP rows' work
+  constexpr bool KEEP_B = 2 * R * F * VW <= 32 / RP;   // B/C biases
+  constexpr bool KEEP_M = 2 * R * PL <= 32 / RP;       // mimo_x / mimo_o
   constexpr int RB = KEEP_B ? R : 1, RM = KEEP_M ? R : 1;
 
   extern __shared__ __align__(128) unsigned char smem[];
@@ -165,9 +189,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   }
   __syncthreads();
 
-  // Row k of this CTA into stage s (= k % S).  The carried state was
-  // written by the previous step's kernel (two or more launches back) and
-  // may be requested before pdl_wait(); the in_proj pieces only after it.
+  // Row k of this CTA into stage s (= k % S), issued by one thread.  The
+  // carried state was written by the previous step's kernel (two or more
+  // launches back) and may be requested before pdl_wait(); the in_proj
+  // pieces only after it.  (Spreading the copies over warp 0's lanes, each
+  // lane selecting its own source and size, was measured slower.)
   auto issue_state = [&](int k, int s) {
     unsigned char *st = ring + (size_t)s * L.stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
@@ -187,57 +213,88 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
     bulk_g2s(smem_addr(st + L.o_araw), row + so + 3 * H, L.n_araw, bar);
   };
 
-  const int npre = min(S - 1, nrows);
-  if (tid == 0)
+  const int npre = min(S - RP, nrows);
+  const bool par_smem = L.o_par >= 0;
+  unsigned char *par = smem + (par_smem ? L.o_par : 0);
+  if (tid == 0) {
+    if (par_smem) {
+      // the parameters join row 0's phase (their bytes are added before row
+      // 0's arrival below): constant for the launch, so requested before
+      // the preceding kernel completes
+      const uint32_t bar = smem_addr(&bars[0]);
+      const int es = (int)sizeof(T);
+      mbar_expect_tx(bar, L.n_par);
+      bulk_g2s(smem_addr(par + L.p_bB), static_cast<const T *>(p.bB) + (int64_t)h0 * R * D, L.n_bBC, bar);
+      bulk_g2s(smem_addr(par + L.p_bC), static_cast<const T *>(p.bC) + (int64_t)h0 * R * D, L.n_bBC, bar);
+      bulk_g2s(smem_addr(par + L.p_mx), static_cast<const T *>(p.mx) + (int64_t)h0 * R * P, L.n_mxo, bar);
+      bulk_g2s(smem_addr(par + L.p_mo), static_cast<const T *>(p.mo) + (int64_t)h0 * R * P, L.n_mxo, bar);
+      bulk_g2s(smem_addr(par + L.p_wB), p.wB, L.n_w, bar);
+      bulk_g2s(smem_addr(par + L.p_wC), p.wC, L.n_w, bar);
+      bulk_g2s(smem_addr(par + L.p_Dp), static_cast<const unsigned char *>(p.Dp) + (size_t)h0 * es, L.n_h8, bar);
+      bulk_g2s(smem_addr(par + L.p_dtb), static_cast<const unsigned char *>(p.dt_bias) + (size_t)h0 * es, L.n_h8,
+               bar);
+    }
     for (int k = 0; k < npre; ++k) issue_state(k, k);
+  }
 
-  // ---- per-head parameters, constant for the launch ----
+  // ---- per-head parameters, constant for the launch: read from the staged
+  // shared-memory copy once row 0 has landed, or from global memory ----
   const T *mxp = static_cast<const T *>(p.mx) + (int64_t)hh * R * P;
   const T *mop = static_cast<const T *>(p.mo) + (int64_t)hh * R * P;
   const T *bBp = static_cast<const T *>(p.bB) + (int64_t)hh * R * D;
   const T *bCp = static_cast<const T *>(p.bC) + (int64_t)hh * R * D;
+  constexpr int es = (int)sizeof(T);
   float mx[RM][PL], mo[RM][PL];
-  if constexpr (KEEP_M) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      ldg_n<PL>(mxp + r * P + lane * PL, mx[r]);
-      ldg_n<PL>(mop + r * P + lane * PL, mo[r]);
-    }
-  }
   float bb[RB][F][VW], bc[RB][F][VW];
-  if constexpr (KEEP_B) {
+  float wn[NRW][F][VW];  // norm weights of the B/C rows this warp normalises
+  float dskip, dtb_t;    // D of this warp's head; dt_bias of the table column's head
+  auto load_params = [&]() {
+    if constexpr (KEEP_M) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r) {
+        const int e0 = (warp * R + r) * P + lane * PL;
+        ld_param<PL>(par_smem, par, L.p_mx + e0 * es, mxp + r * P + lane * PL, mx[r]);
+        ld_param<PL>(par_smem, par, L.p_mo + e0 * es, mop + r * P + lane * PL, mo[r]);
+      }
+    }
+    if constexpr (KEEP_B) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          const int col = (lane + 32 * f) * VW;
+          if (col < D) {
+            const int e0 = (warp * R + r) * D + col;
+            ld_param<VW>(par_smem, par, L.p_bB + e0 * es, bBp + r * D + col, bb[r][f]);
+            ld_param<VW>(par_smem, par, L.p_bC + e0 * es, bCp + r * D + col, bc[r][f]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) bb[r][f][e] = bc[r][f][e] = 0.f;
+          }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NRW; ++j) {
+      const int rr = warp + kWarps * j;
+      const T *w = static_cast<const T *>(rr < R ? p.wB : p.wC);
 #pragma unroll
       for (int f = 0; f < F; ++f) {
         const int col = (lane + 32 * f) * VW;
-        if (col < D) {
-          row::ldg_vec<VW>(bBp + r * D + col, bb[r][f]);
-          row::ldg_vec<VW>(bCp + r * D + col, bc[r][f]);
+        if (rr < 2 * R && col < D) {
+          ld_param<VW>(par_smem, par, (rr < R ? L.p_wB : L.p_wC) + col * es, w + col, wn[j][f]);
         } else {
 #pragma unroll
-          for (int e = 0; e < VW; ++e) bb[r][f][e] = bc[r][f][e] = 0.f;
+          for (int e = 0; e < VW; ++e) wn[j][f][e] = 0.f;
         }
       }
-  }
-  float wn[NRW][F][VW];  // norm weights of the B/C rows this warp normalises
-#pragma unroll
-  for (int j = 0; j < NRW; ++j) {
-    const int rr = warp + kWarps * j;
-    const T *w = static_cast<const T *>(rr < R ? p.wB : p.wC);
-#pragma unroll
-    for (int f = 0; f < F; ++f) {
-      const int col = (lane + 32 * f) * VW;
-      if (rr < 2 * R && col < D) {
-        row::ldg_vec<VW>(w + col, wn[j][f]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < VW; ++e) wn[j][f][e] = 0.f;
-      }
     }
-  }
-  const float dskip = row::ldg_f(static_cast<const T *>(p.Dp) + hh);
-  const float dtb_t = row::ldg_f(static_cast<const T *>(p.dt_bias) + h0 + (tid & 7));  // table column
+    float t[1];
+    ld_param<1>(par_smem, par, L.p_Dp + warp * es, static_cast<const T *>(p.Dp) + hh, t);
+    dskip = t[0];
+    ld_param<1>(par_smem, par, L.p_dtb + (tid & 7) * es, static_cast<const T *>(p.dt_bias) + h0 + (tid & 7), t);
+    dtb_t = t[0];
+  };
+  if (!par_smem) load_params();
   const float inv_d = 1.f / (float)D;
 
   // ---- head-scalar table: thread (j = tid / 8, w = tid % 8) owns row j of
@@ -280,48 +337,81 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
     for (int k = 0; k < npre; ++k) issue_zx(k, k);
   table_load(0);  // stored after the first row's norms, so the loads overlap its wait
 
-  // stage s = k % S of row k and the parity (k / S) & 1 of its barrier
-  // phase, advanced without division
-  int k = 0, s = 0;
-  uint32_t ph = 0;
-  for (; k < nrows; ++k) {
-    const unsigned char *st = ring + (size_t)s * L.stage_bytes;
-    const bool ok = mbar_wait(smem_addr(&bars[s]), ph);
-    float *nb = nbc + (k & 1) * 2 * R * BD;
-
-    // ---- phase A: RMSNorm of the 2R B/C rows (src/models/mamba3.py:34-36) ----
-    const T *sbc = reinterpret_cast<const T *>(st + L.o_bc);
+  // A pass takes RP consecutive rows: their waits, their norms, ONE CTA
+  // barrier, then each warp updates its head for all RP rows in lockstep, so
+  // the rows' dependency chains (loads, reductions, shuffles) overlap.  A row
+  // past the end aliases the pass's first row (same stage and inputs) with
+  // its stores suppressed.  Stage sk / parity pk of row k advance without
+  // division.
+  int k = 0, sk = 0, pass = 0;
+  uint32_t pk = 0;
+  for (; k < nrows; k += RP, ++pass) {
+    int sj[RP];
+    uint32_t pj[RP];
+    bool live[RP];
+    int kj[RP];
+    {
+      int s_ = sk;
+      uint32_t p_ = pk;
 #pragma unroll
-    for (int j = 0; j < NRW; ++j) {
-      const int rr = warp + kWarps * j;
-      if (rr < 2 * R) {
-        float v[F][VW];
-        float ss = 0.f;
-#pragma unroll
-        for (int f = 0; f < F; ++f) {
-          const int col = (lane + 32 * f) * VW;
-          if (col < D) {
-            lds_f<VW, T>(sbc + rr * D + col, v[f]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < VW; ++e) v[f][e] = 0.f;
-          }
-#pragma unroll
-          for (int e = 0; e < VW; ++e) ss = fmaf(v[f][e], v[f][e], ss);
+      for (int j = 0; j < RP; ++j) {
+        live[j] = k + j < nrows;
+        kj[j] = live[j] ? k + j : k;
+        sj[j] = live[j] ? s_ : sj[0];
+        pj[j] = live[j] ? p_ : pj[0];
+        if (++s_ == S) {
+          s_ = 0;
+          p_ ^= 1u;
         }
-        ss = group_sum<32>(ss);
-        const float rinv = rsqrtf(ss * inv_d + kRmsEps);
+      }
+      sk = s_;
+      pk = p_;
+    }
+    bool ok = true;
 #pragma unroll
-        for (int f = 0; f < F; ++f) {
-          const int col = (lane + 32 * f) * VW;
-          if (col < D) {
-            float o[VW];
+    for (int j = 0; j < RP; ++j)
+      if (j == 0 || live[j]) ok = mbar_wait(smem_addr(&bars[sj[j]]), pj[j]) && ok;
+    if (pass == 0 && par_smem) load_params();  // staged with row 0
+
+    // ---- phase A: RMSNorm of each row's 2R B/C rows (src/models/mamba3.py:34-36) ----
 #pragma unroll
-            for (int e = 0; e < VW; ++e) o[e] = v[f][e] * rinv * wn[j][f][e];
-            if constexpr (VW == 4)
-              *reinterpret_cast<float4 *>(nb + rr * BD + col) = make_float4(o[0], o[1], o[2], o[3]);
-            else
-              *reinterpret_cast<float2 *>(nb + rr * BD + col) = make_float2(o[0], o[1]);
+    for (int j = 0; j < RP; ++j) {
+      if (j > 0 && !live[j]) continue;
+      const unsigned char *st = ring + (size_t)sj[j] * L.stage_bytes;
+      float *nb = nbc + ((pass & 1) * RP + j) * 2 * R * BD;
+      const T *sbc = reinterpret_cast<const T *>(st + L.o_bc);
+#pragma unroll
+      for (int q = 0; q < NRW; ++q) {
+        const int rr = warp + kWarps * q;
+        if (rr < 2 * R) {
+          float v[F][VW];
+          float ss = 0.f;
+#pragma unroll
+          for (int f = 0; f < F; ++f) {
+            const int col = (lane + 32 * f) * VW;
+            if (col < D) {
+              lds_f<VW, T>(sbc + rr * D + col, v[f]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < VW; ++e) v[f][e] = 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < VW; ++e) ss = fmaf(v[f][e], v[f][e], ss);
+          }
+          ss = group_sum<32>(ss);
+          const float rinv = rsqrtf(ss * inv_d + kRmsEps);
+#pragma unroll
+          for (int f = 0; f < F; ++f) {
+            const int col = (lane + 32 * f) * VW;
+            if (col < D) {
+              float o[VW];
+#pragma unroll
+              for (int e = 0; e < VW; ++e) o[e] = __fmul_rn(__fmul_rn(v[f][e], rinv), wn[q][f][e]);
+              if constexpr (VW == 4)
+                *reinterpret_cast<float4 *>(nb + rr * BD + col) = make_float4(o[0], o[1], o[2], o[3]);
+              else
+                *reinterpret_cast<float2 *>(nb + rr * BD + col) = make_float2(o[0], o[1]);
+            }
           }
         }
       }
@@ -329,207 +419,262 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
     if (k == 0) table_store(0);
     // next table chunk: raw scalars requested 8 rows before they are stored,
     // stored 16 rows before the chunk starts (its buffer was last read two or
-    // more rows ago, which the barriers since then have retired)
+    // more passes ago, which the barriers since then have retired)
     if (k % kTableRows == kTableRows / 4 && (k / kTableRows + 1) * kTableRows < nrows) table_load(k / kTableRows + 1);
     if (k % kTableRows == kTableRows / 2 && (k / kTableRows + 1) * kTableRows < nrows) table_store(k / kTableRows + 1);
 
-    // the one barrier of a row: normalised rows visible, previous stage free
+    // the one barrier of a pass: normalised rows visible, the previous
+    // pass's stages free
     if (__syncthreads_or(!ok)) break;
-    if (tid == 0 && k + S - 1 < nrows) {
-      const int sn = s == 0 ? S - 1 : s - 1;  // (k + S - 1) % S: the previous row's stage
-      issue_state(k + S - 1, sn);
-      issue_zx(k + S - 1, sn);
-    }
-
-    // ---- phase B: this warp's head ----
-    const int b = b0 + k;
-    const float4 hs = table[((k / kTableRows) & 1) * kTableRows * kWarps + (k % kTableRows) * kWarps + warp];
-    const float DT = hs.w;
-
-    // accumulated angles of this lane's RoPE pairs, written back
-    // (src/models/mamba3.py:326-327)
-    float rc[F][NP], rs[F][NP];
-    {
-      const float *sang = reinterpret_cast<const float *>(st + L.o_ang) + warp * A;
-      const T *sraw = reinterpret_cast<const T *>(st + L.o_araw);
-      float *gang = p.ang + ((int64_t)b * H + hh) * A;
-      // angle_state + angle_raw * DT, rounded after each operation as the
-      // reference's two tensor operations are
-      if (NP == 2 && A <= 32) {
-        // lanes own pairs (2l, 2l+1): one angle per lane, then each lane
-        // fetches the cos/sin of its two pairs
-        float a = 0.f, sn, cs;
-        if (lane < A) {
-          float raw[1];
-          lds_f<1, T>(sraw + lane, raw);
-          a = __fadd_rn(sang[lane], __fmul_rn(raw[0], DT));
-          gang[lane] = a;
-        }
-        rope_sincos(a, sn, cs);
-        const int src = (2 * lane) & 31;
-        const float c0 = __shfl_sync(kFullMask, cs, src), s0 = __shfl_sync(kFullMask, sn, src);
-        const float c1 = __shfl_sync(kFullMask, cs, src + 1), s1 = __shfl_sync(kFullMask, sn, src + 1);
-        const bool mine = 2 * lane < A;
-        rc[0][0] = mine ? c0 : 1.f;
-        rs[0][0] = mine ? s0 : 0.f;
-        rc[0][NP - 1] = mine ? c1 : 1.f;
-        rs[0][NP - 1] = mine ? s1 : 0.f;
+    if (tid == 0) {
 #pragma unroll
-        for (int f = 1; f < F; ++f)
-#pragma unroll
-          for (int q = 0; q < NP; ++q) {
-            rc[f][q] = 1.f;
-            rs[f][q] = 0.f;
-          }
-      } else {
-        // every lane computes its own pairs (A is a multiple of 4, so a
-        // vector's NP pairs rotate together)
-#pragma unroll
-        for (int f = 0; f < F; ++f) {
-          const int i0 = (lane + 32 * f) * NP;
-          const bool on = i0 < A;
-          const int ic = on ? i0 : 0;
-          float a[NP], raw[NP];
-          lds_f<NP, float>(sang + ic, a);
-          lds_f<NP, T>(sraw + ic, raw);
-#pragma unroll
-          for (int q = 0; q < NP; ++q) a[q] = __fadd_rn(a[q], __fmul_rn(raw[q], DT));
-          if (on) stg_f<NP>(gang + i0, a);
-#pragma unroll
-          for (int q = 0; q < NP; ++q) {
-            rope_sincos(a[q], rs[f][q], rc[f][q]);
-            rc[f][q] = on ? rc[f][q] : 1.f;
-            rs[f][q] = on ? rs[f][q] : 0.f;
-          }
+      for (int j = 0; j < RP; ++j) {
+        const int kn = k + S - RP + j;  // into the stage of row k - RP + j
+        if (kn < nrows) {
+          int sn = sj[0] - RP + j;
+          if (sn < 0) sn += S;
+          issue_state(kn, sn);
+          issue_zx(kn, sn);
         }
       }
     }
 
+    // ---- phase B: this warp's head, RP rows ----
+    const unsigned char *st[RP];
+    const float *nbj[RP];
+    float4 hs[RP];
+#pragma unroll
+    for (int j = 0; j < RP; ++j) {
+      st[j] = ring + (size_t)sj[j] * L.stage_bytes;
+      nbj[j] = nbc + ((pass & 1) * RP + j) * 2 * R * BD;
+      hs[j] = table[((kj[j] / kTableRows) & 1) * kTableRows * kWarps + (kj[j] % kTableRows) * kWarps + warp];
+    }
+
+    // accumulated angles of this lane's RoPE pairs, written back
+    // (src/models/mamba3.py:326-327); angle_state + angle_raw * DT, rounded
+    // after each operation as the reference's two tensor operations are
+    float rc[RP][F][NP], rs[RP][F][NP];
+    if (NP == 2 && A <= 32) {
+      // lanes own pairs (2l, 2l+1): one angle per lane, then each lane
+      // fetches the cos/sin of its two pairs
+      float a[RP], sn[RP], cs[RP];
+#pragma unroll
+      for (int j = 0; j < RP; ++j) {
+        a[j] = 0.f;
+        if (lane < A) {
+          const float *sang = reinterpret_cast<const float *>(st[j] + L.o_ang) + warp * A;
+          const T *sraw = reinterpret_cast<const T *>(st[j] + L.o_araw);
+          float raw[1];
+          lds_f<1, T>(sraw + lane, raw);
+          a[j] = __fadd_rn(sang[lane], __fmul_rn(raw[0], hs[j].w));
+          if (live[j]) p.ang[((int64_t)(b0 + kj[j]) * H + hh) * A + lane] = a[j];
+        }
+      }
+      rope_sincos_n<RP>(a, sn, cs);
+      const int src = (2 * lane) & 31;
+      const bool mine = 2 * lane < A;
+#pragma unroll
+      for (int j = 0; j < RP; ++j) {
+        const float c0 = __shfl_sync(kFullMask, cs[j], src), s0 = __shfl_sync(kFullMask, sn[j], src);
+        const float c1 = __shfl_sync(kFullMask, cs[j], src + 1), s1 = __shfl_sync(kFullMask, sn[j], src + 1);
+        rc[j][0][0] = mine ? c0 : 1.f;
+        rs[j][0][0] = mine ? s0 : 0.f;
+        rc[j][0][NP - 1] = mine ? c1 : 1.f;
+        rs[j][0][NP - 1] = mine ? s1 : 0.f;
+#pragma unroll
+        for (int f = 1; f < F; ++f)
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            rc[j][f][q] = 1.f;
+            rs[j][f][q] = 0.f;
+          }
+      }
+    } else {
+      // every lane computes its own pairs (A is a multiple of 4, so a
+      // vector's NP pairs rotate together)
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const int i0 = (lane + 32 * f) * NP;
+        const bool on = i0 < A;
+        const int ic = on ? i0 : 0;
+        float a[RP * NP], sn[RP * NP], cs[RP * NP];
+#pragma unroll
+        for (int j = 0; j < RP; ++j) {
+          const float *sang = reinterpret_cast<const float *>(st[j] + L.o_ang) + warp * A;
+          const T *sraw = reinterpret_cast<const T *>(st[j] + L.o_araw);
+          float av[NP], raw[NP];
+          lds_f<NP, float>(sang + ic, av);
+          lds_f<NP, T>(sraw + ic, raw);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) av[q] = __fadd_rn(av[q], __fmul_rn(raw[q], hs[j].w));
+          if (on && live[j]) stg_f<NP>(p.ang + ((int64_t)(b0 + kj[j]) * H + hh) * A + i0, av);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) a[j * NP + q] = av[q];
+        }
+        rope_sincos_n<RP * NP>(a, sn, cs);
+#pragma unroll
+        for (int j = 0; j < RP; ++j)
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            rc[j][f][q] = on ? cs[j * NP + q] : 1.f;
+            rs[j][f][q] = on ? sn[j * NP + q] : 0.f;
+          }
+      }
+    }
+
     // x_r = sum_p x_p mimo_x[h, r, p]
-    float xr[R];
-    {
-      const T *sx = reinterpret_cast<const T *>(st + L.o_x) + warp * P;
+    float xr[RP][R];
+#pragma unroll
+    for (int j = 0; j < RP; ++j) {
+      const T *sx = reinterpret_cast<const T *>(st[j] + L.o_x) + warp * P;
       float xv[PL];
       lds_f<PL, T>(sx + lane * PL, xv);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         float t = 0.f;
 #pragma unroll
-        for (int j = 0; j < PL; ++j) {
+        for (int q = 0; q < PL; ++q) {
           float m;
-          if constexpr (KEEP_M) m = mx[r][j];
-          else m = row::ldg_f(mxp + r * P + lane * PL + j);
-          t = fmaf(xv[j], m, t);
+          if constexpr (KEEP_M) {
+            m = mx[r][q];
+          } else {
+            float t1[1];
+            ld_param<1>(par_smem, par, L.p_mx + ((warp * R + r) * P + lane * PL + q) * es, mxp + r * P + lane * PL + q, t1);
+            m = t1[0];
+          }
+          t = fmaf(xv[q], m, t);
         }
-        xr[r] = t;
+        xr[j][r] = t;
       }
-      row::warp_allreduce_ranks<R>(xr);
     }
+#pragma unroll
+    for (int j = 0; j < RP; ++j) row::warp_allreduce_ranks<R>(xr[j]);
 
     // Bx = RoPE(sum_r x_r (Bn_r + bias_r)), the trapezoidal update, and the
     // readout y_r = <Cn_r + cbias_r, RoPE^-1(h)> (rotations are orthogonal)
-    float yr[R];
-    {
-      const float *sh = reinterpret_cast<const float *>(st + L.o_h) + warp * D;
-      const float *sb = reinterpret_cast<const float *>(st + L.o_bx) + warp * D;
-      const int64_t gbase = ((int64_t)b * H + hh) * D;
-      const float2 dec2 = f2(hs.x, hs.x), c12 = f2(hs.y, hs.y), c22 = f2(hs.z, hs.z);
-      float2 part[R];
+    float2 part[RP][R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) part[r] = f2(0.f, 0.f);
+    for (int j = 0; j < RP; ++j)
 #pragma unroll
-      for (int f = 0; f < F; ++f) {
-        const int col = (lane + 32 * f) * VW;
-        if (col < D) {
-          float hv[VW], bp[VW];
-          lds_f<VW, float>(sh + col, hv);
-          lds_f<VW, float>(sb + col, bp);
-          float2 acc[NP];
+      for (int r = 0; r < R; ++r) part[j][r] = f2(0.f, 0.f);
 #pragma unroll
-          for (int q = 0; q < NP; ++q) acc[q] = f2(0.f, 0.f);
+    for (int f = 0; f < F; ++f) {
+      const int col = (lane + 32 * f) * VW;
+      if (col < D) {
+        float hv[RP][VW], bp[RP][VW];
+        float2 acc[RP][NP];
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float n[VW], bias[VW];
-            lds_f<VW, float>(nb + r * BD + col, n);
-            if constexpr (KEEP_B) {
+        for (int j = 0; j < RP; ++j) {
+          lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_h) + warp * D + col, hv[j]);
+          lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_bx) + warp * D + col, bp[j]);
 #pragma unroll
-              for (int e = 0; e < VW; ++e) bias[e] = bb[r][f][e];
-            } else {
-              row::ldg_vec<VW>(bBp + r * D + col, bias);
-            }
-            const float2 xx = f2(xr[r], xr[r]);
+          for (int q = 0; q < NP; ++q) acc[j][q] = f2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float bias[VW];
+          if constexpr (KEEP_B) {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) bias[e] = bb[r][f][e];
+          } else {
+            ld_param<VW>(par_smem, par, L.p_bB + ((warp * R + r) * D + col) * es, bBp + r * D + col, bias);
+          }
+#pragma unroll
+          for (int j = 0; j < RP; ++j) {
+            float n[VW];
+            lds_f<VW, float>(nbj[j] + r * BD + col, n);
+            const float2 xx = f2(xr[j][r], xr[j][r]);
 #pragma unroll
             for (int q = 0; q < NP; ++q)
-              acc[q] = __ffma2_rn(xx, __fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])), acc[q]);
+              acc[j][q] =
+                  __ffma2_rn(xx, __fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])), acc[j][q]);
           }
-          float bxv[VW], hn[VW], hr[VW];
+        }
+        float hr[RP][VW];
+#pragma unroll
+        for (int j = 0; j < RP; ++j) {
+          const float2 dec2 = f2(hs[j].x, hs[j].x), c12 = f2(hs[j].y, hs[j].y), c22 = f2(hs[j].z, hs[j].z);
+          float bxv[VW], hn[VW];
 #pragma unroll
           for (int q = 0; q < NP; ++q) {
-            const float c = rc[f][q], sn = rs[f][q];
-            bxv[2 * q] = acc[q].x * c - acc[q].y * sn;
-            bxv[2 * q + 1] = acc[q].x * sn + acc[q].y * c;
-            const float2 t = __ffma2_rn(c22, f2(bp[2 * q], bp[2 * q + 1]),
+            const float c = rc[j][f][q], sn = rs[j][f][q];
+            // rotations with their roundings spelled out, so that every
+            // instantiation (one or two rows a pass) rounds a row alike
+            bxv[2 * q] = fmaf(acc[j][q].x, c, __fmul_rn(-acc[j][q].y, sn));
+            bxv[2 * q + 1] = fmaf(acc[j][q].x, sn, __fmul_rn(acc[j][q].y, c));
+            const float2 t = __ffma2_rn(c22, f2(bp[j][2 * q], bp[j][2 * q + 1]),
                                         __ffma2_rn(c12, f2(bxv[2 * q], bxv[2 * q + 1]),
-                                                   __fmul2_rn(dec2, f2(hv[2 * q], hv[2 * q + 1]))));
+                                                   __fmul2_rn(dec2, f2(hv[j][2 * q], hv[j][2 * q + 1]))));
             hn[2 * q] = t.x;
             hn[2 * q + 1] = t.y;
-            hr[2 * q] = t.x * c + t.y * sn;
-            hr[2 * q + 1] = t.y * c - t.x * sn;
+            hr[j][2 * q] = fmaf(t.x, c, __fmul_rn(t.y, sn));
+            hr[j][2 * q + 1] = fmaf(t.y, c, __fmul_rn(-t.x, sn));
           }
-          stg_f<VW>(p.h + gbase + col, hn);
-          stg_f<VW>(p.bx + gbase + col, bxv);
+          if (live[j]) {
+            const int64_t gbase = ((int64_t)(b0 + kj[j]) * H + hh) * D;
+            stg_f<VW>(p.h + gbase + col, hn);
+            stg_f<VW>(p.bx + gbase + col, bxv);
+          }
+        }
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float n[VW], bias[VW];
-            lds_f<VW, float>(nb + (R + r) * BD + col, n);
-            if constexpr (KEEP_B) {
+        for (int r = 0; r < R; ++r) {
+          float bias[VW];
+          if constexpr (KEEP_B) {
 #pragma unroll
-              for (int e = 0; e < VW; ++e) bias[e] = bc[r][f][e];
-            } else {
-              row::ldg_vec<VW>(bCp + r * D + col, bias);
-            }
+            for (int e = 0; e < VW; ++e) bias[e] = bc[r][f][e];
+          } else {
+            ld_param<VW>(par_smem, par, L.p_bC + ((warp * R + r) * D + col) * es, bCp + r * D + col, bias);
+          }
+#pragma unroll
+          for (int j = 0; j < RP; ++j) {
+            float n[VW];
+            lds_f<VW, float>(nbj[j] + (R + r) * BD + col, n);
 #pragma unroll
             for (int q = 0; q < NP; ++q)
-              part[r] = __ffma2_rn(__fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])),
-                                   f2(hr[2 * q], hr[2 * q + 1]), part[r]);
+              part[j][r] = __ffma2_rn(__fadd2_rn(f2(n[2 * q], n[2 * q + 1]), f2(bias[2 * q], bias[2 * q + 1])),
+                                      f2(hr[j][2 * q], hr[j][2 * q + 1]), part[j][r]);
           }
         }
       }
-#pragma unroll
-      for (int r = 0; r < R; ++r) yr[r] = part[r].x + part[r].y;
-      row::warp_allreduce_ranks<R>(yr);
-#pragma unroll
-      for (int r = 0; r < R; ++r) yr[r] = fmaf(dskip, xr[r], yr[r]);
     }
+    float yr[RP][R];
+#pragma unroll
+    for (int j = 0; j < RP; ++j)
+#pragma unroll
+      for (int r = 0; r < R; ++r) yr[j][r] = part[j][r].x + part[j][r].y;
+#pragma unroll
+    for (int j = 0; j < RP; ++j) row::warp_allreduce_ranks<R>(yr[j]);
 
-    // y_p = sum_r y_r mimo_o[h, r, p], gated by silu(z)
-    {
-      const T *sz = reinterpret_cast<const T *>(st + L.o_z) + warp * P;
+    // y_p = sum_r (y_r + D x_r) mimo_o[h, r, p], gated by silu(z)
+#pragma unroll
+    for (int j = 0; j < RP; ++j) {
+      const T *sz = reinterpret_cast<const T *>(st[j] + L.o_z) + warp * P;
       float zv[PL], yv[PL];
       lds_f<PL, T>(sz + lane * PL, zv);
 #pragma unroll
-      for (int j = 0; j < PL; ++j) {
+      for (int q = 0; q < PL; ++q) {
         float t = 0.f;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           float m;
-          if constexpr (KEEP_M) m = mo[r][j];
-          else m = row::ldg_f(mop + r * P + lane * PL + j);
-          t = fmaf(yr[r], m, t);
+          if constexpr (KEEP_M) {
+            m = mo[r][q];
+          } else {
+            float t1[1];
+            ld_param<1>(par_smem, par, L.p_mo + ((warp * R + r) * P + lane * PL + q) * es, mop + r * P + lane * PL + q, t1);
+            m = t1[0];
+          }
+          t = fmaf(fmaf(dskip, xr[j][r], yr[j][r]), m, t);
         }
-        yv[j] = t * __fdividef(zv[j], 1.f + __expf(-zv[j]));
+        yv[q] = t * __fdividef(zv[q], 1.f + __expf(-zv[q]));
       }
-      st_y<PL>(p.y, (int64_t)b * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
-    }
-    if (++s == S) {
-      s = 0;
-      ph ^= 1u;
+      if (live[j]) st_y<PL>(p.y, (int64_t)(b0 + kj[j]) * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
     }
   }
   // Normal exit: every issued row was consumed.  After a lost copy, wait
   // (bounded) for this CTA's copies still in flight before leaving.
   if (tid == 0 && k < nrows) {
-    for (int q = k; q < min(nrows, k + S - 1); ++q)
+    for (int q = k; q < min(nrows, k + S - RP); ++q)
       mbar_wait(smem_addr(&bars[q % S]), (uint32_t)((q / S) & 1), 1 << 16);
   }
 }
@@ -566,7 +711,7 @@ bool stream_eligible(const KParams &kp) {
   return true;
 }
 
-StreamLayout make_layout(const KParams &kp, int BD, int nstage) {
+StreamLayout make_layout(const KParams &kp, int BD, int nstage, int rp, bool stage_par) {
   const int es = kp.zx_dt == M3_BF16 ? 2 : 4;
   StreamLayout L = {};
   L.n_state = (unsigned)(kWarps * kp.D * 4);
@@ -589,34 +734,40 @@ StreamLayout make_layout(const KParams &kp, int BD, int nstage) {
   int g = 0;
   L.o_bars = g; g += align16(kMaxStages * 8);
   L.o_table = g; g += 2 * kTableRows * kWarps * 16;
-  L.o_nbc = g; g += 2 * 2 * kp.R * BD * 4;
+  L.o_nbc = g; g += 2 * rp * 2 * kp.R * BD * 4;
   L.o_ring = g; g += nstage * L.stage_bytes;
+  L.o_par = -1;
+  L.n_bBC = (unsigned)(kWarps * kp.R * kp.D * es);
+  L.n_mxo = (unsigned)(kWarps * kp.R * kp.P * es);
+  L.n_w = (unsigned)(kp.D * es);
+  L.n_h8 = (unsigned)(kWarps * es);
+  const bool can = (L.n_w % 16) == 0 && aligned(kp.Dp, 16) && aligned(kp.dt_bias, 16);
+  if (stage_par && can) {
+    L.o_par = g;
+    L.p_bB = 0;
+    L.p_bC = L.p_bB + (int)L.n_bBC;
+    L.p_mx = L.p_bC + (int)L.n_bBC;
+    L.p_mo = L.p_mx + (int)L.n_mxo;
+    L.p_wB = L.p_mo + (int)L.n_mxo;
+    L.p_wC = L.p_wB + (int)L.n_w;
+    L.p_Dp = L.p_wC + (int)L.n_w;
+    L.p_dtb = L.p_Dp + (int)L.n_h8;
+    L.n_par = (unsigned)(L.p_dtb + (int)L.n_h8);
+    g += (int)L.n_par;
+  }
   L.smem = g;
   return L;
 }
 
-template <int BD, int R, typename T, int PL>
-cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
-  auto kern = mimo_stream_kernel<BD, R, T, PL>;
+template <int BD, int R, typename T, int PL, int RP>
+cudaError_t launch_stream_rp(const KParams &kp, const StreamLayout &L, cudaStream_t stream) {
+  auto kern = mimo_stream_kernel<BD, R, T, PL, RP>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  // the deepest ring (no deeper than this CTA's rows need) that still lets
-  // two CTAs share an SM, else one CTA with two stages
-  const int ngrp0 = kp.H / kWarps;
-  const int64_t slots0 = (int64_t)num_sms_cached() * 2;
-  const int64_t rows0 = ((int64_t)kp.B * ngrp0 + slots0 - 1) / slots0;
-  int want = (int)(rows0 + 1 < kMaxStages ? rows0 + 1 : kMaxStages);
-  if (want < 2) want = 2;
-  StreamLayout L = make_layout(kp, BD, 2);
-  for (int s = want; s >= 2; --s) {
-    L = make_layout(kp, BD, s);
-    if (L.smem <= 110 * 1024) break;
-  }
-  if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, L.smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
@@ -628,6 +779,30 @@ cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
   if (rows < 1) rows = 1;
   const int64_t grid = (int64_t)ngrp * ((kp.B + rows - 1) / rows);
   return launch_pdl(kern, dim3((unsigned)grid), dim3(kWarps * 32), (size_t)L.smem, stream, kp, L, rows);
+}
+
+// Ring depth: up to 4 stages (no deeper than the CTA's rows need), with the
+// per-head parameters staged in shared memory when that still lets two CTAs
+// share an SM (else they are read from global memory in the prologue).  One
+// row a pass: two-row passes (RP = 2) were measured slower per row (3.0 us a
+// pass against 0.9 us a row at d2048 / batch 256).
+template <int BD, int R, typename T, int PL>
+cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
+  const int ngrp = kp.H / kWarps;
+  const int64_t slots = (int64_t)num_sms_cached() * 2;
+  const int64_t rows = ((int64_t)kp.B * ngrp + slots - 1) / slots;
+  int want = (int)(rows + 1 < 4 ? rows + 1 : 4);
+  if (want < 2) want = 2;
+  StreamLayout L = make_layout(kp, BD, want, 1, true);
+  if (L.smem > 110 * 1024) {
+    L = make_layout(kp, BD, 2, 1, false);
+    for (int s = want; s >= 2; --s) {
+      L = make_layout(kp, BD, s, 1, false);
+      if (L.smem <= 110 * 1024) break;
+    }
+  }
+  if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
+  return launch_stream_rp<BD, R, T, PL, 1>(kp, L, stream);
 }
 
 template <int BD, int R, typename T>

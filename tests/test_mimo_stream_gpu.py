@@ -5,7 +5,8 @@ a batch row can be bulk-copied (8 heads per CTA, headdim 32/64/128, d_state
 36..256, 16-byte aligned sections).  These cases are chosen to land on it:
 state widths 64/96/128/256 (one and two vectors per lane, padded lanes),
 headdims 32/64/128, every rank, rope_fraction 1.0, fp32 and bf16, batches
-that give one or many rows per CTA, more than one 32-row chunk of the
+that give one or many rows per CTA (one-row and two-row passes, an odd
+row count whose last pass has one live row), more than one 32-row chunk of the
 head-scalar table, and accumulated angles far from zero (both the reduced
 and the full-range sin/cos).  Oracle tolerance 1e-4 in fp32.
 """
@@ -28,6 +29,8 @@ LAYERS = [
     (dict(d_model=1024, d_state=256, headdim=128), 3),    # D 256: 2 vectors per lane, headdim 128
     (dict(d_model=128, d_state=96, headdim=32), 300),     # D 96 (padded lanes), headdim 32, rows per CTA > 1
     (dict(d_model=512, d_state=128, headdim=64, rope_fraction=1.0), 4),  # every pair rotates
+    (dict(d_model=256, d_state=128, headdim=64), 601),    # 3 rows per CTA, last CTA 1: two-row passes with a tail
+    (dict(d_model=512, d_state=128, headdim=64, rope_fraction=1.0), 900),  # two-row passes, every pair rotates
 ]
 
 
