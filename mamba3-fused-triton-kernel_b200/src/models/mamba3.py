@@ -11,6 +11,7 @@ CUDA backends live in ``src.models.inference`` and ``src.kernels``.
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass, field
 
 import torch
 import torch.nn as nn
@@ -225,3 +226,83 @@ class MambaBlock(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return x + self.mixer(self.norm(x))
+
+
+@dataclass
+class MambaConfig:
+    """Configuration of a stacked Mamba-3 language model; same fields and
+    defaults as the reference (src/models/mamba3.py:396-409).  The attention,
+    ``rms_norm``, ``residual_in_fp32`` and ``fused_add_norm`` fields are
+    carried for interchange and, as in the reference, not acted on."""
+
+    d_model: int = 2560
+    d_intermediate: int = 0
+    n_layer: int = 64
+    vocab_size: int = 50277
+    ssm_cfg: dict = field(default_factory=dict)
+    attn_layer_idx: list = field(default_factory=list)
+    attn_cfg: dict = field(default_factory=dict)
+    rms_norm: bool = True
+    residual_in_fp32: bool = True
+    fused_add_norm: bool = True
+    pad_vocab_size_multiple: int = 8
+    tie_embeddings: bool = True
+
+
+class MLP(nn.Module):
+    """SwiGLU feed-forward layer (reference: src/models/mamba3.py:424-435)."""
+
+    def __init__(self, d_model: int, d_intermediate: int, device=None, dtype=None):
+        super().__init__()
+        factory_kwargs = {"device": device, "dtype": dtype}
+        self.fc1 = nn.Linear(d_model, 2 * d_intermediate, bias=False, **factory_kwargs)
+        self.fc2 = nn.Linear(d_intermediate, d_model, bias=False, **factory_kwargs)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gate, val = self.fc1(x).chunk(2, dim=-1)
+        return self.fc2(F.silu(gate) * val)
+
+
+class MambaLMHeadModel(nn.Module):
+    """Language model of stacked Mamba-3 blocks (reference:
+    src/models/mamba3.py:438-481): embedding, ``n_layer`` residual blocks
+    (each optionally followed by a residual SwiGLU MLP), final RMSNorm, LM
+    head.  Parameters are created in the reference's order, so the same seed
+    gives the same weights.  One deliberate difference: the reference
+    declares ``lm_head = nn.Linear(vocab_size, d_model)``, whose weight has
+    the transposed shape and works only when tied to the embedding; here it
+    is ``nn.Linear(d_model, vocab_size)`` (the same number of random draws,
+    and the same tied weight)."""
+
+    def __init__(self, config: MambaConfig, device=None, dtype=None):
+        factory_kwargs = {"device": device, "dtype": dtype}
+        super().__init__()
+        self.config = config
+        vocab_size = config.vocab_size
+        r = vocab_size % config.pad_vocab_size_multiple
+        if r != 0:
+            vocab_size += config.pad_vocab_size_multiple - r
+        self.vocab_size = vocab_size
+        self.embedding = nn.Embedding(vocab_size, config.d_model, **factory_kwargs)
+        self.layers = nn.ModuleList([MambaBlock(config.d_model, config.ssm_cfg, **factory_kwargs)
+                                     for _ in range(config.n_layer)])
+        if config.d_intermediate > 0:
+            self.mlp_norms = nn.ModuleList([RMSNorm(config.d_model, device=device) for _ in range(config.n_layer)])
+            self.mlp_layers = nn.ModuleList([MLP(config.d_model, config.d_intermediate, **factory_kwargs)
+                                             for _ in range(config.n_layer)])
+        else:
+            self.mlp_norms = None
+            self.mlp_layers = None
+        self.norm_f = RMSNorm(config.d_model, device=device)
+        self.lm_head = nn.Linear(config.d_model, vocab_size, bias=False, **factory_kwargs)
+        if config.tie_embeddings:
+            self.lm_head.weight = self.embedding.weight
+
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        x = self.embedding(input_ids)
+        for i, block in enumerate(self.layers):
+            x = block(x)
+            if self.mlp_layers is not None:
+                x = x + self.mlp_layers[i](self.mlp_norms[i](x))
+        x = self.norm_f(x)
+        return self.lm_head(x)

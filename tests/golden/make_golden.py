@@ -198,6 +198,36 @@ def make_stack_case(mods, name, spec, out_dir):
     np.savez_compressed(os.path.join(out_dir, name + ".npz"), meta=json.dumps(meta), out=np.stack(outs))
 
 
+# language model (src/models/mamba3.py:396-481): config, batch, length, seed.
+# The reference's own initialisation under torch.manual_seed(seed) (tied
+# embeddings: the reference's lm_head only works tied) and its forward over a
+# seeded token sequence; the fixture keeps the token ids, the logits and a
+# sum per parameter (to check that a rebuilt model holds the same weights).
+LM_CASES = {
+    "lm2_mimo_r2": (dict(d_model=64, n_layer=2, vocab_size=50, d_intermediate=0,
+                         ssm_cfg=dict(d_state=16, headdim=16, is_mimo=True, mimo_rank=2)), 2, 5, 410),
+    "lm2_siso_mlp": (dict(d_model=64, n_layer=2, vocab_size=50, d_intermediate=32,
+                          ssm_cfg=dict(d_state=16, headdim=16)), 2, 5, 411),
+}
+
+
+def make_lm_case(mods, name, spec, out_dir):
+    torch = mods[0]
+    from src.models.mamba3 import MambaConfig, MambaLMHeadModel
+    cfg_kw, batch, length, seed = spec
+    torch.manual_seed(seed)
+    model = MambaLMHeadModel(MambaConfig(**cfg_kw)).eval()
+    gen = torch.Generator().manual_seed(seed + 1)
+    ids = torch.randint(0, cfg_kw["vocab_size"], (batch, length), generator=gen)
+    with torch.no_grad():
+        logits = model(ids)
+    rec = {"input_ids": ids.numpy().astype(np.int64), "logits": _to_np(logits)}
+    for pname, prm in model.state_dict().items():
+        rec["sum." + pname] = np.array(_to_np(prm).reshape(-1).astype(np.float64).sum())
+    meta = dict(kind="lm", config=cfg_kw, batch=batch, length=length, seed=seed)
+    np.savez_compressed(os.path.join(out_dir, name + ".npz"), meta=json.dumps(meta), **rec)
+
+
 # parameter initialisation under torch.manual_seed(seed) on the CPU
 INIT_CASES = {
     "init_siso_d256": (dict(d_model=256, d_state=64, headdim=32), 0),
@@ -235,7 +265,9 @@ def main():
         make_stack_case(mods, name, spec, args.out)
     for name, spec in INIT_CASES.items():
         make_init_case(mods, name, spec, args.out)
-    n = len(LAYER_CASES) + len(SSM_CASES) + len(STACK_CASES) + len(INIT_CASES)
+    for name, spec in LM_CASES.items():
+        make_lm_case(mods, name, spec, args.out)
+    n = len(LAYER_CASES) + len(SSM_CASES) + len(STACK_CASES) + len(INIT_CASES) + len(LM_CASES)
     print("wrote", n, "fixtures to", args.out)
 
 
