@@ -64,9 +64,14 @@ WORKLOADS = {
 }
 # residual stacks: workload -> number of layers (the 24-layer bf16 stack of
 # the reference's multi-GPU configuration)
-STACKS = {"stack24_d2048_b256_bf16": 24}
+STACKS = {"stack24_d2048_b256_bf16": 24, "lm24_d2048_b256_bf16": 24}
 WORKLOADS["stack24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4),
                                         256, "bf16")
+# the same stack as a language model: token ids in, logits out (embedding,
+# 24 blocks, final norm, LM head tied to the embedding; the default vocabulary)
+LM_WORKLOADS = {"lm24_d2048_b256_bf16": 50277}
+LM_STACK_PROFILE = {"lm24_d2048_b256_bf16": "stack24_d2048_b256_bf16"}  # same fused kernel and shapes
+WORKLOADS["lm24_d2048_b256_bf16"] = WORKLOADS["stack24_d2048_b256_bf16"]
 DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
 # Published reference number for the default workload: MIMO d256 B=128
 # full-fused + CUDA graph P50 step latency 0.295 ms on an A100-PCIE-40GB
@@ -249,7 +254,8 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
     import torch.distributed as dist
 
     from src.kernels.linear import linear
-    from src.models.mamba3 import MambaBlock
+    from src.models.lm import Mamba3LMDecoder
+    from src.models.mamba3 import MambaBlock, MambaConfig, MambaLMHeadModel
     from src.models.stack import Mamba3StackDecoder
 
     torch.cuda.set_device(local)
@@ -259,20 +265,34 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
     wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
     torch.manual_seed(0)
     mkw = {k: v for k, v in kw.items() if k != "d_model"}
+    vocab = LM_WORKLOADS.get(args.workload)
     blocks = []
     with torch.no_grad():
-        for _ in range(layers):
-            blk = MambaBlock(kw["d_model"], mkw, device=dev, dtype=wdtype)
+        if vocab is not None:
+            lm = MambaLMHeadModel(MambaConfig(d_model=kw["d_model"], n_layer=layers, vocab_size=vocab, ssm_cfg=mkw),
+                                  device=dev, dtype=wdtype)
+            blocks = list(lm.layers)
+        else:
+            for _ in range(layers):
+                blocks.append(MambaBlock(kw["d_model"], mkw, device=dev, dtype=wdtype))
+        for blk in blocks:
             blk.mixer.in_proj.weight.normal_(0.0, 0.02)
             blk.mixer.out_proj.weight.normal_(0.0, 0.02)
-            blocks.append(blk)
     model = blocks[0].mixer
-    dec = Mamba3StackDecoder(blocks, use_cuda_graph=True, use_triton_full_fused=True)
+    if vocab is not None:
+        dec = Mamba3LMDecoder(lm, use_cuda_graph=True, use_triton_full_fused=True)
+    else:
+        dec = Mamba3StackDecoder(blocks, use_cuda_graph=True, use_triton_full_fused=True)
     states = dec.init_state(batch, device=dev)
     K, W = args.steps, args.warmup
     gen = torch.Generator(device="cpu").manual_seed(1 + rank)
     n_inputs = 16
-    u_host = torch.randn(n_inputs, batch, kw["d_model"], generator=gen).to(wdtype).pin_memory()
+    if vocab is not None:  # token ids in, logits out
+        u_host = torch.randint(0, vocab, (n_inputs, batch), generator=gen).pin_memory()
+        out_shape = (batch, lm.vocab_size)
+    else:
+        u_host = torch.randn(n_inputs, batch, kw["d_model"], generator=gen).to(wdtype).pin_memory()
+        out_shape = (batch, kw["d_model"])
     u_dev = u_host.to(dev)
     flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream(dev)
@@ -359,8 +379,8 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
     gemm_ms = float(gi_ms.mean() + go_ms.mean())
 
     # end to end through the public API: pinned input in, output back to the host
-    out_host = torch.empty(batch, kw["d_model"], dtype=wdtype).pin_memory()
-    u_stage = torch.empty(batch, kw["d_model"], device=dev, dtype=wdtype)
+    out_host = torch.empty(*out_shape, dtype=wdtype).pin_memory()
+    u_stage = torch.empty(u_host.shape[1:], device=dev, dtype=u_host.dtype)
 
     def e2e_step(i):
         u_stage.copy_(u_host[i % n_inputs], non_blocking=True)
@@ -381,7 +401,8 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
         cpu = {"value": round(rate / layers, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} oracle decode steps of one layer x {batch} sequences, rate divided by "
-                         f"{layers} layers (numpy float32 restatement with bf16 rounding)"}
+                         f"{layers} layers (numpy float32 restatement with bf16 rounding"
+                         + ("; embedding and LM head not included" if vocab is not None else "") + ")"}
     # every rank takes part in every collective, so they all run before the
     # rank-0-only report
     p50_all = max_over_ranks(float(np.percentile(step_ms, 50)))
@@ -392,6 +413,11 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         cfg.update({"layers": layers, "step": "CUDA-graph replay of Mamba3StackDecoder.step: per layer "
                     "in_proj (cuBLAS bf16) + fused decode kernel + out_proj (cuBLAS bf16), residual add + "
                     "RMSNorm kernel between blocks"})
+        if vocab is not None:
+            cfg.update({"model": "MambaLMHeadModel", "vocab_size": vocab, "padded_vocab": lm.vocab_size,
+                        "step": "CUDA-graph replay of Mamba3LMDecoder.step: token ids -> embedding, per layer "
+                        "in_proj (cuBLAS bf16) + fused decode kernel + out_proj (cuBLAS bf16) + residual add "
+                        "and RMSNorm kernel, final norm, LM head (cuBLAS bf16) -> logits"})
         line = {
             "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
@@ -401,14 +427,15 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": "fused decode (m3_mimo_full_fused), one layer",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
-                         "mean_launch_ms": round(k_mean, 5), "traffic": profile_traffic(args.workload, "fused")},
+                         "mean_launch_ms": round(k_mean, 5),
+                         "traffic": profile_traffic(LM_STACK_PROFILE.get(args.workload, args.workload), "fused")},
             "kernels_ms": {"fused_decode_per_layer": round(k_mean, 5),
                            "in_proj_gemm_per_layer": round(float(gi_ms.mean()), 5),
                            "out_proj_gemm_per_layer": round(float(go_ms.mean()), 5),
                            "projection_tflops": round(gemm_flop / (gemm_ms * 1e-3) / 1e12, 1)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": batch * kw["d_model"] * es,
-                    "d2h_bytes_per_step": batch * kw["d_model"] * es,
+                    "h2d_bytes_per_step": u_stage.numel() * u_stage.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
                     "ms_per_step": round(e2e_total / len(e2e_ms), 5)},
             "gpu_launches": K * (2 * layers + 1),
             "clocks": clocks,
