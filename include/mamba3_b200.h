@@ -137,6 +137,15 @@ int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
  * lifts the reference's R == 4 restriction (fused_full_decode.py:600). */
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream);
 
+/* Prefill of MIMO layers: dims->batch sequences of seq_len tokens each, the
+ * full step of m3_mimo_full_fused applied token after token with the carried
+ * state kept on chip (replaces the sequential loop of Mamba3.forward,
+ * src/models/mamba3.py:242-304).  zx rows (in_proj outputs) and y rows are
+ * b * seq_len + t at zx_stride_b / y_stride_b; the state arrays hold
+ * dims->batch rows, read once and written once.  M3_ERR_UNSUPPORTED for
+ * shapes the streamed kernel does not take (then step token by token). */
+int m3_mimo_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_len, m3_stream_t stream);
+
 /* Small-batch fp32 linear layer of the decode step's projections (in_proj /
  * out_proj, nn.Linear without bias, src/models/mamba3.py:115,158, called at
  * src/models/inference.py:489,553):  C[m, n] = sum_k A[m, k] * W[n, k].

@@ -79,7 +79,10 @@ int ssm_entry(const m3_dims *d, const m3_ssm_args *a, m3_stream_t stream, bool m
   return launch_status(mimo ? m3::launch_mimo(kp, false, s) : m3::launch_siso(kp, false, s));
 }
 
-int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool mimo) {
+// Validation and kernel parameters of a full-step call; M3_OK with *empty
+// set when the batch is empty (nothing to launch).
+int full_params(const m3_dims *d, const m3_full_args *a, bool mimo, m3::KParams *out, bool *empty) {
+  *empty = false;
   int st = check_dims(d, mimo);
   if (st != M3_OK) return st;
   if (!a) return M3_ERR_NULL;
@@ -97,11 +100,15 @@ int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool
   if (!dtype_ok(a->zx_dtype) || !dtype_ok(a->param_dtype) || !dtype_ok(a->y_dtype)) return M3_ERR_DTYPE;
   if (!aligned16(a->ssm_state) || !aligned16(a->bx_prev)) return M3_ERR_ALIGN;
   if ((reinterpret_cast<uintptr_t>(a->angle_state) & 3u) != 0) return M3_ERR_ALIGN;
-  if (d->batch == 0) return M3_OK;
+  if (d->batch == 0) {
+    *empty = true;
+    return M3_OK;
+  }
   st = check_device();
   if (st != M3_OK) return st;
 
-  KParams kp = {};
+  KParams &kp = *out;
+  kp = KParams{};
   kp.B = d->batch; kp.H = d->nheads; kp.P = d->headdim; kp.D = d->d_state; kp.R = R;
   kp.A = d->num_rope_angles; kp.A_floor = d->A_floor;
   kp.d_inner = d->d_inner; kp.d_bc = d->d_state * R;
@@ -111,6 +118,14 @@ int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool
   kp.bB = a->B_bias; kp.bC = a->C_bias; kp.mx = a->mimo_x; kp.mo = a->mimo_o;
   kp.h = a->ssm_state; kp.bx = a->bx_prev; kp.ang = a->angle_state;
   kp.y = a->y; kp.y_sb = a->y_stride_b; kp.y_sh = d->headdim; kp.y_sp = 1; kp.y_dt = a->y_dtype;
+  return M3_OK;
+}
+
+int full_entry(const m3_dims *d, const m3_full_args *a, m3_stream_t stream, bool mimo) {
+  KParams kp;
+  bool empty = false;
+  const int st = full_params(d, a, mimo, &kp, &empty);
+  if (st != M3_OK || empty) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return launch_status(mimo ? m3::launch_mimo(kp, true, s) : m3::launch_siso(kp, true, s));
 }
@@ -261,6 +276,19 @@ int m3_mimo_decode_fused(const m3_dims *dims, const m3_ssm_args *args, m3_stream
 
 int m3_siso_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {
   return full_entry(dims, args, stream, false);
+}
+
+int m3_mimo_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_len, m3_stream_t stream) {
+  if (seq_len < 0) return M3_ERR_SHAPE;
+  KParams kp;
+  bool empty = false;
+  const int st = full_params(dims, args, true, &kp, &empty);
+  if (st != M3_OK || empty || seq_len == 0) return st;
+  kp.L = seq_len;
+  bool taken = false;
+  const cudaError_t e = m3::launch_mimo_prefill(kp, reinterpret_cast<cudaStream_t>(stream), &taken);
+  if (!taken) return M3_ERR_UNSUPPORTED;
+  return launch_status(e);
 }
 
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {

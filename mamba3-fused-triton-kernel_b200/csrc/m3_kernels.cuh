@@ -58,6 +58,7 @@ struct KParams {
   const float *smo; int64_t mo_sh, mo_sr, mo_sp;
   // carried state (in place) and output
   float *h, *bx, *ang;
+  int L;  // tokens per sequence of a prefill launch (decode: unused)
   void *y; int64_t y_sb, y_sh, y_sp; int y_dt;
 };
 
@@ -465,6 +466,9 @@ cudaError_t launch_mimo(const KParams &kp, bool full, cudaStream_t stream);
 // The streamed MIMO full-step kernel (m3_mimo_stream.cu); *taken is false
 // when the call's shapes or alignment are outside its range.
 cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *taken);
+// The streamed kernel in prefill form: kp.B sequences of kp.L tokens each,
+// in_proj / y rows b * L + t, state rows b (m3_mimo_stream.cu).
+cudaError_t launch_mimo_prefill(const KParams &kp, cudaStream_t stream, bool *taken);
 // The tcgen05 bf16 projection GEMM (m3_gemm.cu): y = x . w^T.
 bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
                          int N, int K);

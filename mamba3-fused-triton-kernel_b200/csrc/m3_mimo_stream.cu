@@ -156,7 +156,7 @@ __device__ __forceinline__ void ld_param(bool staged, const unsigned char *base,
     ldg_n<N>(g, v);
 }
 
-template <int BD, int R, typename T, int PL, int RP>
+template <int BD, int R, typename T, int PL, int RP, bool SEQ>
 __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KParams p, const StreamLayout L,
                                                                       const int rows_per_cta) {
   using Sh = MimoShape<BD>;
@@ -177,8 +177,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   const int H = p.H, P = p.P, D = p.D, A = p.A;
   const int ngrp = H / kWarps;
   const int grp = blockIdx.x % ngrp, h0 = grp * kWarps, hh = h0 + warp;
-  const int b0 = (blockIdx.x / ngrp) * rows_per_cta;
-  const int nrows = min(p.B, b0 + rows_per_cta) - b0;
+  // Decode: "rows" are batch rows b0 + k.  SEQ (prefill): they are the
+  // p.L tokens of sequence bs -- in_proj / y rows bs * L + k -- and the
+  // carried state of row bs stays in registers from the first token to the
+  // last (read once, written once).
+  static_assert(!SEQ || RP == 1, "a prefill CTA takes its tokens one at a time");
+  const int bs = SEQ ? (int)(blockIdx.x / ngrp) : 0;
+  const int b0 = SEQ ? 0 : (int)(blockIdx.x / ngrp) * rows_per_cta;
+  const int nrows = SEQ ? p.L : min(p.B, b0 + rows_per_cta) - b0;
+  auto zrow = [&](int k) -> int64_t { return SEQ ? (int64_t)bs * p.L + k : (int64_t)(b0 + k); };
+  auto srow = [&](int k) -> int64_t { return SEQ ? (int64_t)bs : (int64_t)(b0 + k); };
   const int S = L.nstage;
   const T *zx = static_cast<const T *>(p.zx);
   const int so = 2 * p.d_inner + 2 * p.d_bc;  // dd_dt[H] dd_A[H] trap[H] angle[A]
@@ -197,7 +205,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   auto issue_state = [&](int k, int s) {
     unsigned char *st = ring + (size_t)s * L.stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
-    const int64_t rh = (int64_t)(b0 + k) * H + h0;
+    const int64_t rh = srow(k) * H + h0;
+    if (SEQ && k > 0) {  // later tokens carry the state in registers
+      mbar_arrive_expect_tx(bar, L.tx - L.tx_state);
+      return;
+    }
     mbar_arrive_expect_tx(bar, L.tx);
     bulk_g2s(smem_addr(st + L.o_h), p.h + rh * D, L.n_state, bar);
     bulk_g2s(smem_addr(st + L.o_bx), p.bx + rh * D, L.n_state, bar);
@@ -206,7 +218,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   auto issue_zx = [&](int k, int s) {
     unsigned char *st = ring + (size_t)s * L.stage_bytes;
     const uint32_t bar = smem_addr(&bars[s]);
-    const T *row = zx + (int64_t)(b0 + k) * p.zx_sb;
+    const T *row = zx + zrow(k) * p.zx_sb;
     bulk_g2s(smem_addr(st + L.o_x), row + p.d_inner + (int64_t)h0 * P, L.n_xz, bar);
     bulk_g2s(smem_addr(st + L.o_z), row + (int64_t)h0 * P, L.n_xz, bar);
     bulk_g2s(smem_addr(st + L.o_bc), row + 2 * p.d_inner, L.n_bc, bar);
@@ -303,7 +315,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   auto table_load = [&](int c) {
     const int k = c * kTableRows + (tid >> 3);
     if (k < nrows) {
-      const T *sr = zx + (int64_t)(b0 + k) * p.zx_sb + so + h0 + (tid & 7);
+      const T *sr = zx + zrow(k) * p.zx_sb + so + h0 + (tid & 7);
       traw[0] = row::ldg_f(sr);
       traw[1] = row::ldg_f(sr + H);
       traw[2] = row::ldg_f(sr + 2 * H);
@@ -343,9 +355,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   // past the end aliases the pass's first row (same stage and inputs) with
   // its stores suppressed.  Stage sk / parity pk of row k advance without
   // division.
+  // prefill: the state carried from token to token (this lane's elements)
+  float carry_h[F][VW], carry_bx[F][VW], carry_a1 = 0.f, carry_av[F][NP];
   int k = 0, sk = 0, pass = 0;
   uint32_t pk = 0;
   for (; k < nrows; k += RP, ++pass) {
+    const bool from_stage = !SEQ || k == 0;      // state from the ring (else registers)
+    const bool write_state = !SEQ || k == nrows - 1;
     int sj[RP];
     uint32_t pj[RP];
     bool live[RP];
@@ -466,8 +482,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
           const T *sraw = reinterpret_cast<const T *>(st[j] + L.o_araw);
           float raw[1];
           lds_f<1, T>(sraw + lane, raw);
-          a[j] = __fadd_rn(sang[lane], __fmul_rn(raw[0], hs[j].w));
-          if (live[j]) p.ang[((int64_t)(b0 + kj[j]) * H + hh) * A + lane] = a[j];
+          a[j] = __fadd_rn(from_stage ? sang[lane] : carry_a1, __fmul_rn(raw[0], hs[j].w));
+          if constexpr (SEQ) carry_a1 = a[j];
+          if (live[j] && write_state) p.ang[(srow(kj[j]) * H + hh) * A + lane] = a[j];
         }
       }
       rope_sincos_n<RP>(a, sn, cs);
@@ -503,11 +520,20 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
           const float *sang = reinterpret_cast<const float *>(st[j] + L.o_ang) + warp * A;
           const T *sraw = reinterpret_cast<const T *>(st[j] + L.o_araw);
           float av[NP], raw[NP];
-          lds_f<NP, float>(sang + ic, av);
+          if (from_stage) {
+            lds_f<NP, float>(sang + ic, av);
+          } else {
+#pragma unroll
+            for (int q = 0; q < NP; ++q) av[q] = carry_av[f][q];
+          }
           lds_f<NP, T>(sraw + ic, raw);
 #pragma unroll
           for (int q = 0; q < NP; ++q) av[q] = __fadd_rn(av[q], __fmul_rn(raw[q], hs[j].w));
-          if (on && live[j]) stg_f<NP>(p.ang + ((int64_t)(b0 + kj[j]) * H + hh) * A + i0, av);
+          if constexpr (SEQ) {
+#pragma unroll
+            for (int q = 0; q < NP; ++q) carry_av[f][q] = av[q];
+          }
+          if (on && live[j] && write_state) stg_f<NP>(p.ang + (srow(kj[j]) * H + hh) * A + i0, av);
 #pragma unroll
           for (int q = 0; q < NP; ++q) a[j * NP + q] = av[q];
         }
@@ -565,8 +591,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
         float2 acc[RP][NP];
 #pragma unroll
         for (int j = 0; j < RP; ++j) {
-          lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_h) + warp * D + col, hv[j]);
-          lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_bx) + warp * D + col, bp[j]);
+          if (from_stage) {
+            lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_h) + warp * D + col, hv[j]);
+            lds_f<VW, float>(reinterpret_cast<const float *>(st[j] + L.o_bx) + warp * D + col, bp[j]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) {
+              hv[j][e] = carry_h[f][e];
+              bp[j][e] = carry_bx[f][e];
+            }
+          }
 #pragma unroll
           for (int q = 0; q < NP; ++q) acc[j][q] = f2(0.f, 0.f);
         }
@@ -610,8 +644,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
             hr[j][2 * q] = fmaf(t.x, c, __fmul_rn(t.y, sn));
             hr[j][2 * q + 1] = fmaf(t.y, c, __fmul_rn(-t.x, sn));
           }
-          if (live[j]) {
-            const int64_t gbase = ((int64_t)(b0 + kj[j]) * H + hh) * D;
+          if constexpr (SEQ) {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) {
+              carry_h[f][e] = hn[e];
+              carry_bx[f][e] = bxv[e];
+            }
+          }
+          if (live[j] && write_state) {
+            const int64_t gbase = (srow(kj[j]) * H + hh) * D;
             stg_f<VW>(p.h + gbase + col, hn);
             stg_f<VW>(p.bx + gbase + col, bxv);
           }
@@ -668,7 +709,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
         }
         yv[q] = t * __fdividef(zv[q], 1.f + __expf(-zv[q]));
       }
-      if (live[j]) st_y<PL>(p.y, (int64_t)(b0 + kj[j]) * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
+      if (live[j]) st_y<PL>(p.y, zrow(kj[j]) * p.y_sb + (int64_t)hh * P + lane * PL, yv, p.y_dt);
     }
   }
   // Normal exit: every issued row was consumed.  After a lost copy, wait
@@ -759,20 +800,24 @@ StreamLayout make_layout(const KParams &kp, int BD, int nstage, int rp, bool sta
   return L;
 }
 
-template <int BD, int R, typename T, int PL, int RP>
+template <int BD, int R, typename T, int PL, int RP, bool SEQ>
 cudaError_t launch_stream_rp(const KParams &kp, const StreamLayout &L, cudaStream_t stream) {
-  auto kern = mimo_stream_kernel<BD, R, T, PL, RP>;
+  auto kern = mimo_stream_kernel<BD, R, T, PL, RP, SEQ>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  const int ngrp = kp.H / kWarps;
+  if constexpr (SEQ) {  // one CTA per (sequence, head group), all tokens of it
+    const int64_t grid = (int64_t)ngrp * kp.B;
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(kWarps * 32), (size_t)L.smem, stream, kp, L, 0);
+  }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, L.smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   const int sms = num_sms_cached();
-  const int ngrp = kp.H / kWarps;
   const int64_t slots = (int64_t)sms * per_sm;
   const int64_t items = (int64_t)kp.B * ngrp;
   int rows = (int)((items + slots - 1) / slots);
@@ -781,16 +826,17 @@ cudaError_t launch_stream_rp(const KParams &kp, const StreamLayout &L, cudaStrea
   return launch_pdl(kern, dim3((unsigned)grid), dim3(kWarps * 32), (size_t)L.smem, stream, kp, L, rows);
 }
 
-// Ring depth: up to 4 stages (no deeper than the CTA's rows need), with the
-// per-head parameters staged in shared memory when that still lets two CTAs
-// share an SM (else they are read from global memory in the prologue).  One
-// row a pass: two-row passes (RP = 2) were measured slower per row (3.0 us a
-// pass against 0.9 us a row at d2048 / batch 256).
-template <int BD, int R, typename T, int PL>
+// Ring depth: up to 4 stages (no deeper than the CTA's rows -- batch rows,
+// or tokens in a prefill -- need), with the per-head parameters staged in
+// shared memory when that still lets two CTAs share an SM (else they are
+// read from global memory in the prologue).  One row a pass: two-row passes
+// (RP = 2) were measured slower per row (3.0 us a pass against 0.9 us a row
+// at d2048 / batch 256).
+template <int BD, int R, typename T, int PL, bool SEQ>
 cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
   const int ngrp = kp.H / kWarps;
   const int64_t slots = (int64_t)num_sms_cached() * 2;
-  const int64_t rows = ((int64_t)kp.B * ngrp + slots - 1) / slots;
+  const int64_t rows = SEQ ? (int64_t)kp.L : ((int64_t)kp.B * ngrp + slots - 1) / slots;
   int want = (int)(rows + 1 < 4 ? rows + 1 : 4);
   if (want < 2) want = 2;
   StreamLayout L = make_layout(kp, BD, want, 1, true);
@@ -802,41 +848,54 @@ cudaError_t launch_stream_t(const KParams &kp, cudaStream_t stream) {
     }
   }
   if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
-  return launch_stream_rp<BD, R, T, PL, 1>(kp, L, stream);
+  return launch_stream_rp<BD, R, T, PL, 1, SEQ>(kp, L, stream);
 }
 
-template <int BD, int R, typename T>
+template <int BD, int R, typename T, bool SEQ>
 cudaError_t launch_stream_p(const KParams &kp, cudaStream_t stream) {
-  if (kp.P == 32) return launch_stream_t<BD, R, T, 1>(kp, stream);
-  if (kp.P == 64) return launch_stream_t<BD, R, T, 2>(kp, stream);
-  return launch_stream_t<BD, R, T, 4>(kp, stream);  // P == 96 or 128 is rejected below unless 128
+  if (kp.P == 32) return launch_stream_t<BD, R, T, 1, SEQ>(kp, stream);
+  if (kp.P == 64) return launch_stream_t<BD, R, T, 2, SEQ>(kp, stream);
+  return launch_stream_t<BD, R, T, 4, SEQ>(kp, stream);  // P == 128 (others are not taken)
 }
 
-template <int BD, typename T>
+template <int BD, typename T, bool SEQ>
 cudaError_t launch_stream_r(const KParams &kp, cudaStream_t stream) {
   switch (kp.R) {
-    case 1: return launch_stream_p<BD, 1, T>(kp, stream);
-    case 2: return launch_stream_p<BD, 2, T>(kp, stream);
-    case 4: return launch_stream_p<BD, 4, T>(kp, stream);
-    default: return launch_stream_p<BD, 8, T>(kp, stream);
+    case 1: return launch_stream_p<BD, 1, T, SEQ>(kp, stream);
+    case 2: return launch_stream_p<BD, 2, T, SEQ>(kp, stream);
+    case 4: return launch_stream_p<BD, 4, T, SEQ>(kp, stream);
+    default: return launch_stream_p<BD, 8, T, SEQ>(kp, stream);
   }
 }
 
-template <typename T>
+template <typename T, bool SEQ>
 cudaError_t launch_stream_d(const KParams &kp, cudaStream_t stream) {
-  if (kp.D <= 64) return launch_stream_r<64, T>(kp, stream);
-  if (kp.D <= 128) return launch_stream_r<128, T>(kp, stream);
-  return launch_stream_r<256, T>(kp, stream);
+  if (kp.D <= 64) return launch_stream_r<64, T, SEQ>(kp, stream);
+  if (kp.D <= 128) return launch_stream_r<128, T, SEQ>(kp, stream);
+  return launch_stream_r<256, T, SEQ>(kp, stream);
+}
+
+bool stream_takes(const KParams &kp) {
+  return stream_eligible(kp) && (kp.P == 32 || kp.P == 64 || kp.P == 128) &&
+         (kp.R == 1 || kp.R == 2 || kp.R == 4 || kp.R == 8);
 }
 
 }  // namespace
 
 cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *taken) {
   *taken = false;
-  if (!stream_eligible(kp) || (kp.P != 32 && kp.P != 64 && kp.P != 128)) return cudaSuccess;
-  if (kp.R != 1 && kp.R != 2 && kp.R != 4 && kp.R != 8) return cudaSuccess;
+  if (!stream_takes(kp)) return cudaSuccess;
   *taken = true;
-  return kp.zx_dt == M3_BF16 ? launch_stream_d<__nv_bfloat16>(kp, stream) : launch_stream_d<float>(kp, stream);
+  return kp.zx_dt == M3_BF16 ? launch_stream_d<__nv_bfloat16, false>(kp, stream)
+                             : launch_stream_d<float, false>(kp, stream);
+}
+
+cudaError_t launch_mimo_prefill(const KParams &kp, cudaStream_t stream, bool *taken) {
+  *taken = false;
+  if (kp.L < 1 || !stream_takes(kp)) return cudaSuccess;
+  *taken = true;
+  return kp.zx_dt == M3_BF16 ? launch_stream_d<__nv_bfloat16, true>(kp, stream)
+                             : launch_stream_d<float, true>(kp, stream);
 }
 
 int mimo_stream_device_error(bool reset) { return device_error_of_this_unit(reset); }

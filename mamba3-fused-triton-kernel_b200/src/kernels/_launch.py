@@ -147,6 +147,25 @@ class FullFusedLaunch:
             st = self.fn(self.dims, a, nat.stream_handle(self.device))
         nat.check(st, self.fn.__name__)
 
+    def prefill(self, zx: torch.Tensor, y: torch.Tensor, seq_len: int) -> bool:
+        """MIMO prefill (``m3_mimo_prefill``): ``zx`` / ``y`` hold
+        batch x seq_len rows (row b * seq_len + t); the state is stepped
+        through all tokens in one launch.  False (nothing enqueued) when the
+        layer's shape is outside the prefill kernel's range."""
+        n = self.batch * seq_len
+        assert zx.shape == (n, self.d_in_proj) and zx.stride(1) == 1 and zx.device == self.device
+        assert y.shape == (n, self.d_inner) and y.stride(1) == 1 and y.device == self.device
+        a = self.args
+        a.zx = zx.data_ptr(); a.zx_stride_b = zx.stride(0); a.zx_dtype = nat.dtype_code(zx)
+        a.y = y.data_ptr(); a.y_stride_b = y.stride(0); a.y_dtype = nat.dtype_code(y)
+        lib = nat.load()
+        with nat.device_guard(self.device):
+            st = lib.m3_mimo_prefill(self.dims, a, seq_len, nat.stream_handle(self.device))
+        if st == nat.M3_ERR_UNSUPPORTED:
+            return False
+        nat.check(st, "m3_mimo_prefill")
+        return True
+
 
 def prepare_full_fused(mimo: bool, batch: int, device, dt_bias, D_skip, B_norm_w, C_norm_w, B_bias,
                        C_bias, mimo_x, mimo_o, h, bx_prev, angle_state, *, d_inner, d_state, ngroups,

@@ -304,6 +304,34 @@ class Mamba3Decoder:
         out = linear(y.to(u.dtype), m.out_proj.weight)
         return out, state
 
+    def prefill(self, u: torch.Tensor, state: dict) -> tuple:
+        """Feed a prompt: ``u`` (batch, length, d_model) -> (outputs (batch,
+        length, d_model), state), the state advanced by all ``length`` tokens
+        (what the reference computes with ``Mamba3.forward``'s sequential
+        loop, src/models/mamba3.py:242-304, from a given state).  With the
+        CUDA full-fused backend a MIMO layer runs one in_proj GEMM over all
+        batch x length tokens, ONE launch of the streamed kernel's prefill
+        form (the carried state stays on chip from token to token) and one
+        out_proj GEMM; other layers and backends step token by token."""
+        B, L = u.shape[0], u.shape[1]
+        m = self.model
+        if self.use_triton_full_fused and m.is_mimo and B > 0 and L > 0:
+            flat = u.reshape(B * L, u.shape[2])
+            zx = linear(flat, m.in_proj.weight)
+            if zx.dtype not in (torch.float32, torch.bfloat16) or zx.stride(1) != 1:
+                zx = zx.float().contiguous()
+            w_dtype = m.out_proj.weight.dtype
+            y_dtype = w_dtype if w_dtype in (torch.float32, torch.bfloat16) else torch.float32
+            y = torch.empty(B * L, m.d_inner, device=u.device, dtype=y_dtype)
+            if self._fused_launch(state).prefill(zx, y, L):
+                out = linear(y.to(u.dtype), m.out_proj.weight)
+                return out.view(B, L, -1), state
+        outs = []
+        for t in range(L):
+            o, state = self.step(u[:, t].contiguous(), state)
+            outs.append(o.clone())
+        return torch.stack(outs, dim=1), state
+
     def _prep_projections(self, u: torch.Tensor, state: dict):
         """PyTorch split / norm / RoPE of the partially fused backends
         (reference: src/models/inference.py:305-358), with the angle state

@@ -117,3 +117,19 @@ def test_stack_decoder_pytorch_matches_reference(name):
     with torch.no_grad():
         outs = [dec.step(torch.from_numpy(u[t]).to(dtype), st)[0].float().numpy() for t in range(m["steps"])]
     np.testing.assert_allclose(np.stack(outs), g["out"], rtol=1e-2, atol=1e-2)
+
+
+def test_prefill_on_the_pytorch_path_is_forward():
+    """Mamba3Decoder.prefill from a zero state gives Mamba3.forward's outputs
+    (the reference's sequential loop, src/models/mamba3.py:242-304)."""
+    import torch as _t
+    from src.models.inference import Mamba3Decoder as _Dec
+    from src.models.mamba3 import Mamba3 as _M
+    _t.manual_seed(3)
+    m = _M(d_model=64, d_state=16, headdim=16, is_mimo=True, mimo_rank=2)
+    u = _t.randn(2, 6, 64)
+    dec = _Dec(m, use_triton=False)
+    with _t.no_grad():
+        out, st = dec.prefill(u, dec.init_state(2))
+        ref = m(u)
+    _t.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
