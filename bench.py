@@ -71,6 +71,10 @@ WORKLOADS["stack24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=
 # 24 blocks, final norm, LM head tied to the embedding; the default vocabulary)
 LM_WORKLOADS = {"lm24_d2048_b256_bf16": 50277}
 LM_STACK_PROFILE = {"lm24_d2048_b256_bf16": "stack24_d2048_b256_bf16"}  # same fused kernel and shapes
+# prompt prefill of one MIMO layer (Mamba3Decoder.prefill): batch sequences x prompt tokens
+PREFILLS = {"prefill_d2048_b64_l512_bf16": 512}
+WORKLOADS["prefill_d2048_b64_l512_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True,
+                                                 mimo_rank=4), 64, "bf16")
 WORKLOADS["lm24_d2048_b256_bf16"] = WORKLOADS["stack24_d2048_b256_bf16"]
 DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
 # Published reference number for the default workload: MIMO d256 B=128
@@ -447,6 +451,156 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
+    """Prompt prefill of one MIMO layer: `batch` sequences of `length` tokens
+    through Mamba3Decoder.prefill (one in_proj GEMM over all tokens, one
+    launch of the streamed kernel's prefill form, one out_proj GEMM).  A
+    step is one whole prefill; L2 flushed and a CUDA event pair around every
+    timed step, max over ranks.  `roofline` is the prefill kernel alone: the
+    in_proj rows read once, y written once, the state read and written once."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from src.kernels.linear import linear
+    from src.models.inference import Mamba3Decoder
+    from src.models.mamba3 import Mamba3
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    torch.manual_seed(0)
+    model = Mamba3(**kw, device=dev, dtype=wdtype)
+    with torch.no_grad():
+        model.in_proj.weight.normal_(0.0, 0.02)
+        model.out_proj.weight.normal_(0.0, 0.02)
+    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    state = dec.init_state(batch, device=dev)
+    K, W = args.steps, args.warmup
+    gen = torch.Generator(device="cpu").manual_seed(1 + rank)
+    u_host = torch.randn(batch, length, kw["d_model"], generator=gen).to(wdtype).pin_memory()
+    u_dev = u_host.to(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(W):
+            dec.prefill(u_dev, state)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed_loop(fn, n, pre_sync=False):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            if pre_sync:
+                stream.synchronize()
+            else:
+                torch.cuda._sleep(20000)
+            ev[i][0].record(stream)
+            fn(i)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        return np.array([a.elapsed_time(b) for a, b in ev])
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    try:
+        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
+    except ValueError:
+        gpus = list(range(world))
+    sampler = ClockSampler(gpus) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.2)
+    barrier()
+    if sampler:
+        sampler.mark()
+    with torch.no_grad():
+        step_ms = timed_loop(lambda i: dec.prefill(u_dev, state), K)
+    barrier()
+    if sampler:
+        sampler.mark()
+    total_ms = max_over_ranks(float(step_ms.sum()))
+    p50_all = max_over_ranks(float(np.percentile(step_ms, 50)))
+    value = world * batch * length * K / (total_ms / 1000.0)
+
+    # the prefill kernel alone, on prepared in_proj rows
+    es = 2 if wdtype == torch.bfloat16 else 4
+    with torch.no_grad():
+        zx = linear(u_dev.reshape(batch * length, -1), model.in_proj.weight)
+        y = torch.empty(batch * length, model.d_inner, device=dev, dtype=wdtype)
+        launch = dec._fused_launch(state)
+        k_ms = timed_loop(lambda i: launch.prefill(zx, y, length), min(K, 50))
+    k_mean = max_over_ranks(float(k_ms.mean()))
+    H, D, A = model.nheads, model.d_state, model.num_rope_angles
+    R, P = model.mimo_rank, model.headdim
+    nbytes = (batch * length * (model.d_in_proj + model.d_inner) * es + 16 * batch * H * D + 8 * batch * H * A
+              + es * (2 * H + 2 * D + 2 * H * R * D + 2 * H * R * P))
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes / (k_mean * 1e-3) / 1e9
+
+    # end to end through the public API: the prompt from pinned host memory,
+    # every output row back to the host
+    out_host = torch.empty(batch, length, kw["d_model"], dtype=wdtype).pin_memory()
+    u_stage = torch.empty_like(u_dev)
+
+    def e2e_step(i):
+        u_stage.copy_(u_host, non_blocking=True)
+        out, _ = dec.prefill(u_stage, state)
+        out_host.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    barrier()
+    with torch.no_grad():
+        e2e_ms = timed_loop(e2e_step, min(K, 50), pre_sync=True)
+    barrier()
+    e2e_total = max_over_ranks(float(e2e_ms.sum()))
+    e2e_value = world * batch * length * len(e2e_ms) / (e2e_total / 1000.0)
+    clocks = sampler.stop() if sampler else None
+    cpu = None
+    if rank == 0 and world == 1:
+        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
+        cpu = {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} oracle decode steps of {batch} sequences (a prefill on the host is one decode "
+                         f"step per prompt token; numpy float32 restatement with bf16 rounding)"}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        cfg = config_dict(args.workload, kw, batch, world, dtype_name)
+        cfg.update({"prompt_tokens": length, "step": "Mamba3Decoder.prefill of batch x prompt tokens: in_proj "
+                    "(cuBLAS bf16) over all tokens, one m3_mimo_prefill launch, out_proj (cuBLAS bf16)"})
+        line = {
+            "metric": "prefill tokens/s", "value": round(value, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
+            "p50_step_ms": round(p50_all, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": cfg,
+            "roofline": {"bound": "hbm", "kernel": "m3_mimo_prefill (streamed kernel, sequence form)",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
+                         "mean_launch_ms": round(k_mean, 5), "traffic": profile_traffic(args.workload, "prefill")},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": u_stage.numel() * es, "d2h_bytes_per_step": out_host.numel() * es,
+                    "ms_per_step": round(e2e_total / len(e2e_ms), 5)},
+            "gpu_launches": K,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -468,6 +622,9 @@ def main():
         return
     if args.workload in STACKS:
         run_stack(args, kw, batch, dtype_name, STACKS[args.workload], world, rank, local)
+        return
+    if args.workload in PREFILLS:
+        run_prefill(args, kw, batch, dtype_name, PREFILLS[args.workload], world, rank, local)
         return
 
     import datetime
