@@ -234,13 +234,21 @@ def run_reference(args, kw, batch, dtype_name, rank):
     rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=steps, warmup=0)
     rate /= layers
     ms = 1000.0 * batch / rate
+    cfg = config_dict(args.workload, kw, batch, 1, dtype_name, reference=True)
+    metric, sample = "decode tokens/s", f"{n} oracle decode steps of {batch} sequences (numpy, host cores)"
+    if args.workload in PREFILLS:
+        # a prefill on the host is one decode step per prompt token, so its
+        # tokens/s is the decode rate; ms_per_step stays one batch of tokens
+        metric = "prefill tokens/s"
+        cfg["prompt_tokens"] = PREFILLS[args.workload]
+        sample += " (a prefill on the host steps every prompt token)"
     line = {
-        "metric": "decode tokens/s", "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
+        "metric": metric, "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_dict(args.workload, kw, batch, 1, dtype_name, reference=True),
+        "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} oracle decode steps of {batch} sequences (numpy, host cores)"},
+                         "sample": sample},
         "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
