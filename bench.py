@@ -72,9 +72,10 @@ WORKLOADS["stack24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=
 LM_WORKLOADS = {"lm24_d2048_b256_bf16": 50277}
 LM_STACK_PROFILE = {"lm24_d2048_b256_bf16": "stack24_d2048_b256_bf16"}  # same fused kernel and shapes
 # prompt prefill of one MIMO layer (Mamba3Decoder.prefill): batch sequences x prompt tokens
-PREFILLS = {"prefill_d2048_b64_l512_bf16": 512}
+PREFILLS = {"prefill_d2048_b64_l512_bf16": 512, "prefill_siso_d2048_b64_l512_bf16": 512}
 WORKLOADS["prefill_d2048_b64_l512_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True,
                                                  mimo_rank=4), 64, "bf16")
+WORKLOADS["prefill_siso_d2048_b64_l512_bf16"] = (dict(d_model=2048, d_state=128, headdim=64), 64, "bf16")
 WORKLOADS["lm24_d2048_b256_bf16"] = WORKLOADS["stack24_d2048_b256_bf16"]
 DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
 # Published reference number for the default workload: MIMO d256 B=128
@@ -460,9 +461,10 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
 
 
 def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
-    """Prompt prefill of one MIMO layer: `batch` sequences of `length` tokens
+    """Prompt prefill of one layer: `batch` sequences of `length` tokens
     through Mamba3Decoder.prefill (one in_proj GEMM over all tokens, one
-    launch of the streamed kernel's prefill form, one out_proj GEMM).  A
+    prefill launch -- m3_mimo_prefill or m3_siso_prefill -- and one out_proj
+    GEMM).  A
     step is one whole prefill; L2 flushed and a CUDA event pair around every
     timed step, max over ranks.  `roofline` is the prefill kernel alone: the
     in_proj rows read once, y written once, the state read and written once."""
@@ -553,8 +555,15 @@ def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
     k_mean = max_over_ranks(float(k_ms.mean()))
     H, D, A = model.nheads, model.d_state, model.num_rope_angles
     R, P = model.mimo_rank, model.headdim
-    nbytes = (batch * length * (model.d_in_proj + model.d_inner) * es + 16 * batch * H * D + 8 * batch * H * A
-              + es * (2 * H + 2 * D + 2 * H * R * D + 2 * H * R * P))
+    # in_proj rows read once, y rows written once; h and bx_prev (MIMO: D per
+    # head, SISO: P x D per head) and the angles read once and written once;
+    # dt_bias, D, the norm weights, the B/C biases (and the MIMO projections)
+    if model.is_mimo:
+        state_elems, par_elems = H * D, 2 * H + 2 * D + 2 * H * R * D + 2 * H * R * P
+    else:
+        state_elems, par_elems = H * P * D, 2 * H + 2 * D + 2 * H * D
+    nbytes = (batch * length * (model.d_in_proj + model.d_inner) * es + 16 * batch * state_elems
+              + 8 * batch * H * A + es * par_elems)
     peak, peak_kind = hbm_peak()
     achieved = nbytes / (k_mean * 1e-3) / 1e9
 
@@ -586,14 +595,16 @@ def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
         dist.barrier()
     if rank == 0:
         cfg = config_dict(args.workload, kw, batch, world, dtype_name)
+        entry = "m3_mimo_prefill" if model.is_mimo else "m3_siso_prefill"
         cfg.update({"prompt_tokens": length, "step": "Mamba3Decoder.prefill of batch x prompt tokens: in_proj "
-                    "(cuBLAS bf16) over all tokens, one m3_mimo_prefill launch, out_proj (cuBLAS bf16)"})
+                    f"(cuBLAS bf16) over all tokens, one {entry} launch, out_proj (cuBLAS bf16)"})
         line = {
             "metric": "prefill tokens/s", "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
             "p50_step_ms": round(p50_all, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": cfg,
-            "roofline": {"bound": "hbm", "kernel": "m3_mimo_prefill (streamed kernel, sequence form)",
+            "roofline": {"bound": "hbm", "kernel": (f"{entry} (streamed kernel, sequence form)" if model.is_mimo else
+                                                   f"{entry} (state tile in registers)"),
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
                          "mean_launch_ms": round(k_mean, 5), "traffic": profile_traffic(args.workload, "prefill")},

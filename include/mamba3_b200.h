@@ -146,6 +146,14 @@ int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_
  * shapes the streamed kernel does not take (then step token by token). */
 int m3_mimo_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_len, m3_stream_t stream);
 
+/* Prefill of SISO layers: the full step of m3_siso_full_fused applied token
+ * after token to dims->batch sequences of seq_len tokens, with each head's
+ * (headdim, d_state) state tile kept on chip from the first token to the
+ * last (replaces the sequential loop of Mamba3.forward,
+ * src/models/mamba3.py:242-304, for is_mimo=False).  Row layout as
+ * m3_mimo_prefill; M3_ERR_UNSUPPORTED for shapes the kernel does not take. */
+int m3_siso_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_len, m3_stream_t stream);
+
 /* Small-batch fp32 linear layer of the decode step's projections (in_proj /
  * out_proj, nn.Linear without bias, src/models/mamba3.py:115,158, called at
  * src/models/inference.py:489,553):  C[m, n] = sum_k A[m, k] * W[n, k].

@@ -291,6 +291,19 @@ int m3_mimo_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_l
   return launch_status(e);
 }
 
+int m3_siso_prefill(const m3_dims *dims, const m3_full_args *args, int32_t seq_len, m3_stream_t stream) {
+  if (seq_len < 0) return M3_ERR_SHAPE;
+  KParams kp;
+  bool empty = false;
+  const int st = full_params(dims, args, false, &kp, &empty);
+  if (st != M3_OK || empty || seq_len == 0) return st;
+  kp.L = seq_len;
+  bool taken = false;
+  const cudaError_t e = m3::launch_siso_prefill(kp, reinterpret_cast<cudaStream_t>(stream), &taken);
+  if (!taken) return M3_ERR_UNSUPPORTED;
+  return launch_status(e);
+}
+
 int m3_mimo_full_fused(const m3_dims *dims, const m3_full_args *args, m3_stream_t stream) {
   return full_entry(dims, args, stream, true);
 }
@@ -362,8 +375,9 @@ int m3_device_error(int reset) {
   const int c = m3::step_device_error(reset != 0);
   const int d = m3::mimo_stream_device_error(reset != 0);
   const int e = m3::gemm_device_error(reset != 0);
-  if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0) return -1;
-  return a | b | c | d | e;
+  const int f = m3::siso_prefill_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0) return -1;
+  return a | b | c | d | e | f;
 }
 
 int m3_selftest_wait_timeout(m3_stream_t stream) {

@@ -469,6 +469,10 @@ cudaError_t launch_mimo_stream(const KParams &kp, cudaStream_t stream, bool *tak
 // The streamed kernel in prefill form: kp.B sequences of kp.L tokens each,
 // in_proj / y rows b * L + t, state rows b (m3_mimo_stream.cu).
 cudaError_t launch_mimo_prefill(const KParams &kp, cudaStream_t stream, bool *taken);
+// SISO prefill (m3_siso_prefill.cu): kp.B sequences of kp.L tokens, one CTA per
+// (sequence, head) with the state tile in registers; *taken false (nothing
+// enqueued) for shapes outside its range.
+cudaError_t launch_siso_prefill(const KParams &kp, cudaStream_t stream, bool *taken);
 // The tcgen05 bf16 projection GEMM (m3_gemm.cu): y = x . w^T.
 bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
                          int N, int K);
@@ -487,6 +491,7 @@ cudaError_t launch_linear_small_m(const float *A, int64_t lda, const float *W, i
 int siso_device_error(bool reset);
 int mimo_device_error(bool reset);
 int mimo_stream_device_error(bool reset);
+int siso_prefill_device_error(bool reset);
 int gemm_device_error(bool reset);
 
 // Heads handled by one CTA of the MIMO kernels.

@@ -148,10 +148,10 @@ class FullFusedLaunch:
         nat.check(st, self.fn.__name__)
 
     def prefill(self, zx: torch.Tensor, y: torch.Tensor, seq_len: int) -> bool:
-        """MIMO prefill (``m3_mimo_prefill``): ``zx`` / ``y`` hold
-        batch x seq_len rows (row b * seq_len + t); the state is stepped
-        through all tokens in one launch.  False (nothing enqueued) when the
-        layer's shape is outside the prefill kernel's range."""
+        """Prefill (``m3_mimo_prefill`` / ``m3_siso_prefill``): ``zx`` / ``y``
+        hold batch x seq_len rows (row b * seq_len + t); the state is
+        stepped through all tokens in one launch.  False (nothing enqueued)
+        when the layer's shape is outside the prefill kernel's range."""
         n = self.batch * seq_len
         assert zx.shape == (n, self.d_in_proj) and zx.stride(1) == 1 and zx.device == self.device
         assert y.shape == (n, self.d_inner) and y.stride(1) == 1 and y.device == self.device
@@ -159,11 +159,12 @@ class FullFusedLaunch:
         a.zx = zx.data_ptr(); a.zx_stride_b = zx.stride(0); a.zx_dtype = nat.dtype_code(zx)
         a.y = y.data_ptr(); a.y_stride_b = y.stride(0); a.y_dtype = nat.dtype_code(y)
         lib = nat.load()
+        fn = lib.m3_mimo_prefill if self.fn.__name__.startswith("m3_mimo") else lib.m3_siso_prefill
         with nat.device_guard(self.device):
-            st = lib.m3_mimo_prefill(self.dims, a, seq_len, nat.stream_handle(self.device))
+            st = fn(self.dims, a, seq_len, nat.stream_handle(self.device))
         if st == nat.M3_ERR_UNSUPPORTED:
             return False
-        nat.check(st, "m3_mimo_prefill")
+        nat.check(st, fn.__name__)
         return True
 
 

@@ -309,13 +309,15 @@ class Mamba3Decoder:
         length, d_model), state), the state advanced by all ``length`` tokens
         (what the reference computes with ``Mamba3.forward``'s sequential
         loop, src/models/mamba3.py:242-304, from a given state).  With the
-        CUDA full-fused backend a MIMO layer runs one in_proj GEMM over all
-        batch x length tokens, ONE launch of the streamed kernel's prefill
-        form (the carried state stays on chip from token to token) and one
-        out_proj GEMM; other layers and backends step token by token."""
+        CUDA full-fused backend a layer runs one in_proj GEMM over all
+        batch x length tokens, ONE prefill launch (MIMO: the streamed
+        kernel's sequence form; SISO: one CTA per sequence and head with the
+        head's state tile in registers; either way the carried state stays
+        on chip from token to token) and one out_proj GEMM; shapes outside
+        those kernels and other backends step token by token."""
         B, L = u.shape[0], u.shape[1]
         m = self.model
-        if self.use_triton_full_fused and m.is_mimo and B > 0 and L > 0:
+        if self.use_triton_full_fused and B > 0 and L > 0:
             flat = u.reshape(B * L, u.shape[2])
             zx = linear(flat, m.in_proj.weight)
             if zx.dtype not in (torch.float32, torch.bfloat16) or zx.stride(1) != 1:

@@ -31,7 +31,7 @@ def _declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 18, names
+    assert len(names) == 19, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
