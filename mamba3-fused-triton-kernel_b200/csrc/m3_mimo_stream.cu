@@ -53,36 +53,6 @@ struct StreamLayout {
   unsigned n_bBC, n_mxo, n_w, n_h8, n_par;
 };
 
-// sin and cos of an accumulated RoPE angle, which grows without bound over
-// a sequence: Cody-Waite reduction (Cody & Waite, "Software Manual for the
-// Elementary Functions", 1980) by 2*pi with the constant split into a float
-// head and a float tail -- each step one fma, whose product is exact -- then
-// the hardware approximations on [-pi, pi], where their absolute error is
-// about 4e-7.  Angles beyond 2^17 (and NaN) take the library's full-range
-// sincosf, N angles at a time with one warp vote for that fallback.  Every
-// lane of the warp must call it.
-template <int N>
-__device__ __forceinline__ void rope_sincos_n(const float (&x)[N], float (&s)[N], float (&c)[N]) {
-  constexpr float kInvTwoPi = 0x1.45f306p-3f;   // 1 / (2 pi)
-  constexpr float kTwoPiHi = 0x1.921fb6p+2f;    // 2 pi rounded to float
-  constexpr float kTwoPiLo = -0x1.777a5cp-23f;  // 2 pi - kTwoPiHi, rounded to float
-  bool big = false;
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const float k = rintf(x[i] * kInvTwoPi);
-    float r = fmaf(-k, kTwoPiHi, x[i]);
-    r = fmaf(-k, kTwoPiLo, r);
-    s[i] = __sinf(r);
-    c[i] = __cosf(r);
-    big = big || !(fabsf(x[i]) <= 131072.f);
-  }
-  if (__any_sync(kFullMask, big)) {
-#pragma unroll
-    for (int i = 0; i < N; ++i)
-      if (!(fabsf(x[i]) <= 131072.f)) sincosf(x[i], &s[i], &c[i]);
-  }
-}
-
 // Shared-memory loads of N consecutive elements (8- or 16-byte aligned for
 // N > 1) into floats.
 template <int N, typename T> __device__ __forceinline__ void lds_f(const T *p, float (&v)[N]);

@@ -12,12 +12,14 @@
 // B|C rows, the head's x and z, the scalar section) arrive by bulk copies
 // into one of two ring slots on one mbarrier.  Two producer warps prepare a
 // whole chunk while the update warps advance the state through the
-// previous one: warp 8 RMS-normalises the B rows, adds the head bias,
-// rotates them by the accumulated angles and computes the head scalars,
-// warp 9 does the same for the C rows and gates z.  The TC tokens of a
-// chunk are independent chains inside a producer warp (only the angle
-// accumulation runs token after token, per lane), so their latencies
-// overlap.  One CTA barrier per chunk hands a chunk from the producers to
+// previous one, each warp half of the chunk's tokens: RMSNorm of the B and
+// C rows, the norm weights and the head's biases, the rotation of both by
+// the accumulated angles (one sin/cos per angle serves both rows), x and
+// silu(z), and the head scalars (warp 8, every token).  The tokens a warp
+// prepares are independent chains (only the angle accumulation runs token
+// after token, per lane, and both warps run it over the whole chunk so
+// that each carries the angles on), so their latencies overlap.  One CTA
+// barrier per chunk hands a chunk from the producers to
 // the update warps, which run the chunk's tokens back to back; three chunk
 // buffers hold the chunk being updated, the one before it (its last token's
 // x and B) and the one being prepared.
@@ -158,9 +160,8 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
   // the same barrier.
   const int rsub = lane / S, j = lane % S;
   if (producer) {
-    const int row_sel = warp - kUpdWarps;  // 0: B rows, x, scalars; 1: C rows, silu(z)
-    const float *w = row_sel ? wC : wB;
-    const float *bias = row_sel ? bCh : bBh;
+    const int pw = warp - kUpdWarps;  // tokens [pw * TH, (pw + 1) * TH) of each chunk
+    constexpr int TH = TC / kPrepWarps;
     float ang[KPL];  // carried angles (written two or more kernels back)
 #pragma unroll
     for (int k = 0; k < KPL; ++k) {
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
       for (; issued < kSlots && issued < nchunk; ++issued) issue_chunk(issued);
 
     // Chunk c's parameters into its buffer: RMSNorm + weight + head bias +
-    // RoPE of one B or C row per token (src/models/mamba3.py:202-215,
+    // RoPE of the B and C rows of each token (src/models/mamba3.py:202-215,
     // 326-333; src/kernels/utils.py:31-44), the angles advanced by
     // angle_raw * DT token after token.
     auto prepare = [&](int c) -> bool {
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
       float DT[TC];
 #pragma unroll
       for (int i = 0; i < TC; ++i) DT[i] = __shfl_sync(kFullMask, dt_l, i);
-      if (row_sel == 0 && lane < n) {  // head scalars of token `lane`
+      if (pw == 0 && lane < n) {  // head scalars of token `lane`
         const T *scal = reinterpret_cast<const T *>(stage(c, lane) + lay.s_scal);
         const float sp = softplus_f(to_f(scal[H + hh]));
         const float Ah = -(sp > -p.A_floor ? -p.A_floor : sp);  // clamp keeps NaN like torch
@@ -198,49 +199,87 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
         sc[1] = dt_l * ((1.f - tr) + htr);
         sc[2] = dt_l * htr;
       }
-      // raw rows and the running angles of every token of the chunk
-      float v[TC][KPL], an[TC][KPL], ss[TC];
+      // the angle accumulation over the whole chunk; this warp keeps the
+      // angles of its own tokens
+      float an[TH][KPL];
 #pragma unroll
       for (int i = 0; i < TC; ++i) {
         const bool live = i < n;
-        const T *raw = reinterpret_cast<const T *>(stage(c, live ? i : 0) + lay.s_raw) + row_sel * D;
         const T *araw = reinterpret_cast<const T *>(stage(c, live ? i : 0) + lay.s_scal) + 3 * H;
-        ss[i] = 0.f;
 #pragma unroll
         for (int k = 0; k < KPL; ++k) {
           const int d = lane + 32 * k;
-          v[i][k] = (live && d < D) ? to_f(raw[d]) : 0.f;
-          ss[i] += v[i][k] * v[i][k];
           if (live && d < 2 * A) ang[k] = ang[k] + to_f(araw[d >> 1]) * DT[i];
-          an[i][k] = ang[k];
+          if (i / TH == pw) an[i % TH][k] = ang[k];
+        }
+      }
+      // raw B and C rows of this warp's tokens, their squared sums
+      float vb[TH][KPL], vc[TH][KPL], sb[TH], scq[TH];
+#pragma unroll
+      for (int u = 0; u < TH; ++u) {
+        const int i = pw * TH + u;
+        const bool live = i < n;
+        const T *raw = reinterpret_cast<const T *>(stage(c, live ? i : 0) + lay.s_raw);
+        sb[u] = 0.f;
+        scq[u] = 0.f;
+#pragma unroll
+        for (int k = 0; k < KPL; ++k) {
+          const int d = lane + 32 * k;
+          vb[u][k] = (live && d < D) ? to_f(raw[d]) : 0.f;
+          vc[u][k] = (live && d < D) ? to_f(raw[D + d]) : 0.f;
+          sb[u] += vb[u][k] * vb[u][k];
+          scq[u] += vc[u][k] * vc[u][k];
         }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int i = 0; i < TC; ++i) ss[i] += __shfl_xor_sync(kFullMask, ss[i], o);
+        for (int u = 0; u < TH; ++u) {
+          sb[u] += __shfl_xor_sync(kFullMask, sb[u], o);
+          scq[u] += __shfl_xor_sync(kFullMask, scq[u], o);
+        }
 #pragma unroll
-      for (int i = 0; i < TC; ++i) {
-        const float rms = sqrtf(ss[i] / (float)D + kRmsEps);
-        float *out = tok(c * TC + (i < n ? i : 0)) + row_sel * BD;
+      for (int u = 0; u < TH; ++u) {
+        const int i = pw * TH + u;
+        const float ib = 1.f / sqrtf(sb[u] / (float)D + kRmsEps);
+        const float ic = 1.f / sqrtf(scq[u] / (float)D + kRmsEps);
+        float sn[KPL], cs[KPL];
+        rope_sincos_n<KPL>(an[u], sn, cs);
+        float *out = tok(c * TC + (i < n ? i : 0));
 #pragma unroll
         for (int k = 0; k < KPL; ++k) {
           const int d = lane + 32 * k;
-          float x = v[i][k];
-          if (d < D) x = x / rms * w[d] + bias[d];
+          float xb = vb[u][k], xc = vc[u][k];
+          if (d < D) {
+            xb = xb * ib * wB[d] + bBh[d];
+            xc = xc * ic * wC[d] + bCh[d];
+          }
           const bool rot = d < 2 * A;
-          float sn = 0.f, cs = 1.f;
-          if (rot) sincosf(an[i][k], &sn, &cs);
-          const float o = __shfl_xor_sync(kFullMask, x, 1);
-          if (rot) x = (d & 1) ? o * sn + x * cs : x * cs - o * sn;
-          if (i < n && d < BD) out[d] = d < D ? x : 0.f;
+          const float ob = __shfl_xor_sync(kFullMask, xb, 1);
+          const float oc = __shfl_xor_sync(kFullMask, xc, 1);
+          if (rot) {
+            xb = (d & 1) ? ob * sn[k] + xb * cs[k] : xb * cs[k] - ob * sn[k];
+            xc = (d & 1) ? oc * sn[k] + xc * cs[k] : xc * cs[k] - oc * sn[k];
+          }
+          if (i < n && d < BD) {
+            out[d] = d < D ? xb : 0.f;
+            out[BD + d] = d < D ? xc : 0.f;
+          }
         }
       }
-      // x (warp 8) or silu(z) (warp 9) of every token
-      for (int i = 0; i < n; ++i) {
-        const T *src = reinterpret_cast<const T *>(stage(c, i) + (row_sel ? lay.s_z : lay.s_x));
-        float *dst = tok(c * TC + i) + 2 * BD + row_sel * P;
-        for (int e = lane; e < P; e += 32) dst[e] = row_sel ? silu_f(to_f(src[e])) : to_f(src[e]);
+      // x and silu(z) of this warp's tokens
+#pragma unroll
+      for (int u = 0; u < TH; ++u) {
+        const int i = pw * TH + u;
+        if (i >= n) break;
+        const T *xs = reinterpret_cast<const T *>(stage(c, i) + lay.s_x);
+        const T *zs = reinterpret_cast<const T *>(stage(c, i) + lay.s_z);
+        float *dst = tok(c * TC + i) + 2 * BD;
+        for (int e = lane; e < P; e += 32) {
+          const float z = to_f(zs[e]);
+          dst[e] = to_f(xs[e]);
+          dst[P + e] = __fdividef(z, 1.f + __expf(-z));
+        }
       }
       return true;
     };
@@ -261,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
           mbar_wait(smem_addr(&bars[k % kSlots]), (uint32_t)((k / kSlots) & 1), 1 << 16);
       return;
     }
-    if (row_sel == 0) {
+    if (pw == 0) {
 #pragma unroll
       for (int k = 0; k < KPL; ++k) {
         const int d = lane + 32 * k;
