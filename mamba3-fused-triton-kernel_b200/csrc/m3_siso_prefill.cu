@@ -10,15 +10,16 @@
 //
 // Tokens move in chunks of TC.  A chunk's slices of the in_proj rows (the
 // B|C rows, the head's x and z, the scalar section) arrive by bulk copies
-// into one of two ring slots on one mbarrier.  Two producer warps prepare a
-// whole chunk while the update warps advance the state through the
-// previous one, each warp half of the chunk's tokens: RMSNorm of the B and
+// into one of two ring slots on one mbarrier.  Four producer warps prepare
+// a whole chunk while the update warps advance the state through the
+// previous one, each warp a quarter of the chunk's tokens: RMSNorm of the B and
 // C rows, the norm weights and the head's biases, the rotation of both by
 // the accumulated angles (one sin/cos per angle serves both rows), x and
 // silu(z), and the head scalars (warp 8, every token).  The tokens a warp
 // prepares are independent chains (only the angle accumulation runs token
 // after token, per lane, and both warps run it over the whole chunk so
-// that each carries the angles on), so their latencies overlap.  One CTA
+// that each carries the angles on), so their latencies overlap; with two
+// producer warps the update warps still waited for them at the barrier.  One CTA
 // barrier per chunk hands a chunk from the producers to
 // the update warps, which run the chunk's tokens back to back; three chunk
 // buffers hold the chunk being updated, the one before it (its last token's
@@ -40,7 +41,7 @@ namespace m3 {
 namespace {
 
 constexpr int kUpdWarps = 8;
-constexpr int kPrepWarps = 2;
+constexpr int kPrepWarps = 4;
 constexpr int kThreads = (kUpdWarps + kPrepWarps) * 32;
 constexpr int kSlots = 2;        // ring slots (chunks in flight)
 constexpr int kChunkBufs = 3;    // prepared-chunk buffers
