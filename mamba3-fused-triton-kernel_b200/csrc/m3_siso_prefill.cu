@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
   const int rsub = lane / S, j = lane % S;
   if (producer) {
     const int pw = warp - kUpdWarps;  // tokens [pw * TH, (pw + 1) * TH) of each chunk
+    const float invD = 1.f / (float)D;
     constexpr int TH = TC / kPrepWarps;
     float ang[KPL];  // carried angles (written two or more kernels back)
 #pragma unroll
@@ -183,19 +184,23 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
     auto prepare = [&](int c) -> bool {
       if (!mbar_wait(smem_addr(&bars[c % kSlots]), (uint32_t)((c / kSlots) & 1))) return false;
       const int n = ntok(c);
+      // this chunk's ring slot and token buffers, addressed from two bases
+      const unsigned char *slot = stage(c, 0);
+      const int sbytes = lay.stage_bytes, tf = lay.tok_floats;
+      float *cbuf = tok(c * TC);
       // DT of token i on lane i, then to every lane
       float dt_l = 0.f;
-      if (lane < n) dt_l = softplus_f(to_f(reinterpret_cast<const T *>(stage(c, lane) + lay.s_scal)[hh]) + dtb);
+      if (lane < n) dt_l = softplus_f(to_f(reinterpret_cast<const T *>(slot + lane * sbytes + lay.s_scal)[hh]) + dtb);
       float DT[TC];
 #pragma unroll
       for (int i = 0; i < TC; ++i) DT[i] = __shfl_sync(kFullMask, dt_l, i);
       if (pw == 0 && lane < n) {  // head scalars of token `lane`
-        const T *scal = reinterpret_cast<const T *>(stage(c, lane) + lay.s_scal);
+        const T *scal = reinterpret_cast<const T *>(slot + lane * sbytes + lay.s_scal);
         const float sp = softplus_f(to_f(scal[H + hh]));
         const float Ah = -(sp > -p.A_floor ? -p.A_floor : sp);  // clamp keeps NaN like torch
         const float tr = sigmoid_f(to_f(scal[2 * H + hh]));
         const float htr = tr * 0.5f;
-        float *sc = tok(c * TC + lane) + 2 * BD + 2 * P;
+        float *sc = cbuf + lane * tf + 2 * BD + 2 * P;
         sc[0] = expf(Ah * dt_l);
         sc[1] = dt_l * ((1.f - tr) + htr);
         sc[2] = dt_l * htr;
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
 #pragma unroll
       for (int i = 0; i < TC; ++i) {
         const bool live = i < n;
-        const T *araw = reinterpret_cast<const T *>(stage(c, live ? i : 0) + lay.s_scal) + 3 * H;
+        const T *araw = reinterpret_cast<const T *>(slot + (live ? i : 0) * sbytes + lay.s_scal) + 3 * H;
 #pragma unroll
         for (int k = 0; k < KPL; ++k) {
           const int d = lane + 32 * k;
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
       for (int u = 0; u < TH; ++u) {
         const int i = pw * TH + u;
         const bool live = i < n;
-        const T *raw = reinterpret_cast<const T *>(stage(c, live ? i : 0) + lay.s_raw);
+        const T *raw = reinterpret_cast<const T *>(slot + (live ? i : 0) * sbytes + lay.s_raw);
         sb[u] = 0.f;
         scq[u] = 0.f;
 #pragma unroll
@@ -242,11 +247,11 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
 #pragma unroll
       for (int u = 0; u < TH; ++u) {
         const int i = pw * TH + u;
-        const float ib = 1.f / sqrtf(sb[u] / (float)D + kRmsEps);
-        const float ic = 1.f / sqrtf(scq[u] / (float)D + kRmsEps);
+        const float ib = rsqrtf(sb[u] * invD + kRmsEps);
+        const float ic = rsqrtf(scq[u] * invD + kRmsEps);
         float sn[KPL], cs[KPL];
         rope_sincos_n<KPL>(an[u], sn, cs);
-        float *out = tok(c * TC + (i < n ? i : 0));
+        float *out = cbuf + (i < n ? i : 0) * tf;
 #pragma unroll
         for (int k = 0; k < KPL; ++k) {
           const int d = lane + 32 * k;
@@ -273,9 +278,9 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
       for (int u = 0; u < TH; ++u) {
         const int i = pw * TH + u;
         if (i >= n) break;
-        const T *xs = reinterpret_cast<const T *>(stage(c, i) + lay.s_x);
-        const T *zs = reinterpret_cast<const T *>(stage(c, i) + lay.s_z);
-        float *dst = tok(c * TC + i) + 2 * BD;
+        const T *xs = reinterpret_cast<const T *>(slot + i * sbytes + lay.s_x);
+        const T *zs = reinterpret_cast<const T *>(slot + i * sbytes + lay.s_z);
+        float *dst = cbuf + i * tf + 2 * BD;
         for (int e = lane; e < P; e += 32) {
           const float z = to_f(zs[e]);
           dst[e] = to_f(xs[e]);
