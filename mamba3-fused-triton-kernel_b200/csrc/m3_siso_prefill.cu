@@ -336,13 +336,12 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
   pdl_trigger();
   __syncthreads();
 
-  // Token t: h advanced in registers, y rows stored.  FIRST: the previous
-  // B x comes from the bx_prev state, else from token t - 1.
+  // Token t (prepared parameters at cur, token t - 1's at prv): h advanced
+  // in registers, y rows stored.  FIRST: the previous B x comes from the
+  // bx_prev state, else from prv.
   const int64_t ybase = (int64_t)b * L * p.y_sb + (int64_t)hh * P;
-  auto update = [&](int t, auto first_tag) {
+  auto update = [&](int t, const float *cur, const float *prv, auto first_tag) {
     constexpr bool FIRST = decltype(first_tag)::value;
-    const float *cur = tok(t);
-    const float *prv = FIRST ? cur : tok(t - 1);
     const float *sc = cur + 2 * BD + 2 * P;
     const float2 dec2 = f2(sc[0]);
     const float a1 = sc[1], a2 = sc[2];
@@ -404,11 +403,17 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
   for (int c = 0; !failed && c < nchunk; ++c) {
     const int n = ntok(c);
     int i = 0;
+    const int tf = lay.tok_floats;
+    const float *cb = tok(c * TC);
     if (c == 0) {
-      update(0, std::true_type{});
+      update(0, cb, cb, std::true_type{});
       i = 1;
     }
-    for (; i < n; ++i) update(c * TC + i, std::false_type{});
+    // token i of the chunk follows token i - 1 (the previous chunk's last for i = 0)
+    for (const float *prv = i ? cb : tok(c * TC - 1); i < n; ++i) {
+      update(c * TC + i, cb + i * tf, prv, std::false_type{});
+      prv = cb + i * tf;
+    }
     failed = __syncthreads_or(false);
   }
   if (failed) return;
