@@ -55,7 +55,7 @@ struct PrefShape {
   static constexpr int RPW = 32 / S;            // rows per warp per pass
   static constexpr int ROWS = kUpdWarps * RPW;  // rows per pass of the CTA
   static constexpr int KPL = BD >= 32 ? BD / 32 : 1;  // producer elements per lane
-  static constexpr int TC = BD >= 256 ? 4 : 8;  // tokens per chunk
+  static constexpr int TC = BD >= 256 ? 4 : 12;  // tokens per chunk
 };
 
 // Byte offsets of the shared-memory regions.

@@ -5,7 +5,7 @@ to the last) and one out_proj GEMM must give the outputs and the final
 state of stepping the same prompt token by token -- and, in fp32, of the
 oracle's decode loop -- across state widths (16 .. 256, one not a multiple
 of 32), headdims, bf16, prompts of one token, prompts that are not a whole
-number of the kernel's 8-token chunks, many sequences and a non-zero
+number of the kernel's token chunks, many sequences and a non-zero
 starting state; shapes outside the kernel's range step token by token."""
 
 from __future__ import annotations
