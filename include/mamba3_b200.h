@@ -17,8 +17,10 @@
  *     would break the in-place contract.
  *   - Arguments are validated on the host before any launch; an invalid call
  *     returns a non-zero status and enqueues nothing.  Device code never traps.
- *   - Calls are safe to capture in a CUDA graph after one eager call on the
- *     device (the first call sets kernel attributes).
+ *   - Calls of the entry points other than m3_mimo_step_static are safe to
+ *     capture in a CUDA graph after one eager call on the device (the first
+ *     call sets kernel attributes).  This header states nothing about
+ *     capturing m3_mimo_step_static.
  */
 #ifndef MAMBA3_B200_H
 #define MAMBA3_B200_H
@@ -194,8 +196,13 @@ int64_t m3_linear_bf16_workspace_bytes(int32_t M, int32_t N, int32_t K);
  *   workspace    device scratch of at least m3_mimo_step_workspace_bytes,
  *                256-byte aligned, ZEROED ONCE before its first use and then
  *                left to the library (it holds the in_proj output, the gated
- *                output and grid-barrier counters that each launch returns to
- *                zero).  One workspace per concurrently running launch.
+ *                output and two grid-barrier words, a base and an arrival
+ *                counter, that are never reset: each launch advances the
+ *                base past its own arrivals).  After a launch on it reports
+ *                M3_DEVERR_TIMEOUT the words no longer agree, every later
+ *                launch on it times out as well, and the workspace must be
+ *                zeroed again before its next use.  One workspace per
+ *                concurrently running launch.
  * d_model, row strides and the weights' row strides multiples of 4; u and
  * the weights 16-byte (f32) / 8-byte (bf16) aligned. */
 typedef struct m3_step_args {
@@ -240,8 +247,9 @@ int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stre
  * m3_mimo_step, except that args->workspace must be NULL and
  * args->workspace_bytes 0: the workspace is a device array inside the
  * library, M3_STEP_STATIC_SCRATCH_BYTES long.  A layer and batch needing
- * more (m3_mimo_step_workspace_bytes) return M3_ERR_SCRATCH and enqueue
- * nothing.  Allocates nothing.  The first call on a device looks up the
+ * more (m3_mimo_step_workspace_bytes) return M3_ERR_SCRATCH; like every call
+ * that m3_mimo_step would reject, it enqueues nothing and leaves the array
+ * as it was.  Allocates nothing.  The first call on a device looks up the
  * array's device address (once, with that device current); make that first
  * call before any stream capture.  Each call clears the array's barrier
  * words on `stream` before its launch; every call on a device shares the
@@ -261,7 +269,11 @@ int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o
 
 /* Device-side error word of the library's kernels: 0, or a bit mask of
  * M3_DEVERR_* raised by a kernel that gave up a bounded wait (the kernel
- * then skipped its remaining work and returned).  Synchronises the device.
+ * then skipped its remaining work and returned).  The outputs and the state
+ * a launch that raised it was updating are undefined (a prefill may have
+ * stored the output rows of finished chunks while leaving the state as it
+ * was), and m3_mimo_step's workspace must be zeroed again.  Synchronises
+ * the device.
  * `reset` != 0 clears the word.  Returns -1 if it cannot be read.
  * Diagnostics only; no counterpart in the reference. */
 enum { M3_DEVERR_TIMEOUT = 1 };

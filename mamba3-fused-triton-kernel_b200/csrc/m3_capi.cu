@@ -187,7 +187,10 @@ int64_t step_workspace_bytes(const m3_dims *d, int32_t d_model, int32_t dtype) {
   return step_layout(d, d_in_proj, dtype == M3_BF16 ? 2 : 4).bytes;
 }
 
-int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
+// Every check m3_mimo_step makes before it enqueues anything; *empty is set
+// for a batch of zero rows (nothing to launch).
+int step_check(const m3_dims *d, const m3_step_args *a, bool *empty) {
+  *empty = false;
   if (!d || !a) return M3_ERR_NULL;
   int st = check_step_dims(d, a->d_model, a->dtype);
   if (st != M3_OK) return st;
@@ -209,7 +212,10 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
       !aligned_to(a->B_bias, va) || !aligned_to(a->C_bias, va) || !aligned_to(a->workspace, 256) ||
       !aligned16(a->ssm_state) || !aligned16(a->bx_prev) || !aligned_to(a->angle_state, 4))
     return M3_ERR_ALIGN;
-  if (d->batch == 0) return M3_OK;
+  if (d->batch == 0) {
+    *empty = true;
+    return M3_OK;
+  }
   st = check_device();
   if (st != M3_OK) return st;
   int dev = 0, coop = 0;
@@ -218,6 +224,17 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
     cudaGetLastError();
     return M3_ERR_DEVICE;
   }
+  return M3_OK;
+}
+
+int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
+  bool empty = false;
+  const int st = step_check(d, a, &empty);
+  if (st != M3_OK || empty) return st;
+  const int es = a->dtype == M3_BF16 ? 2 : 4;
+  const int R = d->mimo_rank;
+  const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * R + 3LL * d->nheads + d->num_rope_angles;
+  const StepLayout L = step_layout(d, d_in_proj, es);
 
   char *ws = static_cast<char *>(a->workspace);
   m3::StepParams sp = {};
@@ -255,6 +272,10 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
 }
 
 }  // namespace
+
+namespace m3 {
+int step_validate(const m3_dims *d, const m3_step_args *a, bool *empty) { return step_check(d, a, empty); }
+}  // namespace m3
 
 extern "C" {
 

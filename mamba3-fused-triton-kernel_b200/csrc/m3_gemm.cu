@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every copy this thread issued has landed before the CTA moves on
     // (immediate on the normal path, where the MMAs consumed them)
     for (int j = issued > S ? issued - S : 0; j < issued; ++j)
-      mbar_wait(smem_addr(&full[j % S]), (uint32_t)((j / S) & 1), 1 << 16);
+      mbar_wait(smem_addr(&full[j % S]), (uint32_t)((j / S) & 1));  // full bound: a copy may still land
   } else if (tid == 32) {
     // MMA issuer: D[128 x nb] (+)= W_tile[128 x 64] . X_tile[nb x 64]^T
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(g.nb >> 3) << 17) |
@@ -341,17 +341,7 @@ bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
+int sm_count() { return sm_count_current(); }
 
 // Tile width (batch rows per CTA) and K split of one call: the cheapest by
 // a simple model -- each k-tile moves its weight and batch tiles at about
@@ -433,12 +423,8 @@ cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t 
   CUtensorMap tw, tx;
   if (!make_map(&tw, w, N, K, ldw, kTileN) || !make_map(&tx, x, M, K, ldx, g.nb)) return cudaErrorInvalidValue;
 
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static LaunchCache cache;
+  if (cudaError_t e = ensure_smem_optin(cache, gemm_bf16_kernel, 227 * 1024); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.ntiles, (unsigned)pl.mchunks, (unsigned)g.nsplit);
   cfg.blockDim = dim3(kThreads);

@@ -29,6 +29,7 @@
 
 #include <utility>
 
+#include "m3_devcache.cuh"
 #include "mamba3_b200.h"
 
 namespace m3 {

@@ -35,17 +35,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, PRE ? 2 : 4) mimo_row_kernel(c
   });
 }
 
-int num_sms() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
+int num_sms() { return sm_count_current(); }
 
 bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -64,24 +54,12 @@ template <int BD, int R, typename T, int KP>
 cudaError_t launch_row_kp(const KParams &kp, cudaStream_t stream) {
   auto kern = mimo_row_kernel<BD, R, T, KP, (BD >= 128)>;
   const size_t smem = 2 * (size_t)row_block_floats(R, BD, kp.A) * sizeof(float);
-  static bool attr = false;
-  static size_t last_smem = (size_t)-1;
-  static int last_per_sm = 1;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  if (smem != last_smem) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, smem) != cudaSuccess ||
-        per_sm < 1)
-      per_sm = 1;
-    last_smem = smem;
-    last_per_sm = per_sm;
-  }
+  static LaunchCache cache;
+  if (cudaError_t e = ensure_smem_optin(cache, kern, 96 * 1024); e != cudaSuccess) return e;
+  int per_sm = 0;
+  if (occupancy_per_sm(cache, kern, kRowWarps * 32, smem, &per_sm) != cudaSuccess || per_sm < 1) per_sm = 1;
   const int ngrp = kp.H / kRowWarps;
-  const int slots = num_sms() * last_per_sm;
+  const int slots = num_sms() * per_sm;
   const int64_t items = (int64_t)kp.B * ngrp;
   int rows = (int)((items + slots - 1) / slots);
   if (rows < 1) rows = 1;

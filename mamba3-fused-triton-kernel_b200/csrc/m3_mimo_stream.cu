@@ -686,23 +686,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) mimo_stream_kernel(const KPara
   // (bounded) for this CTA's copies still in flight before leaving.
   if (tid == 0 && k < nrows) {
     for (int q = k; q < min(nrows, k + S - RP); ++q)
-      mbar_wait(smem_addr(&bars[q % S]), (uint32_t)((q / S) & 1), 1 << 16);
+      mbar_wait(smem_addr(&bars[q % S]), (uint32_t)((q / S) & 1));  // full bound: a copy may still land
   }
 }
 
 int align16(int x) { return (x + 15) & ~15; }
 
-int num_sms_cached() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
+int num_sms_cached() { return sm_count_current(); }
 
 bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -773,20 +763,15 @@ StreamLayout make_layout(const KParams &kp, int BD, int nstage, int rp, bool sta
 template <int BD, int R, typename T, int PL, int RP, bool SEQ>
 cudaError_t launch_stream_rp(const KParams &kp, const StreamLayout &L, cudaStream_t stream) {
   auto kern = mimo_stream_kernel<BD, R, T, PL, RP, SEQ>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static LaunchCache cache;
+  if (cudaError_t e = ensure_smem_optin(cache, kern, 227 * 1024); e != cudaSuccess) return e;
   const int ngrp = kp.H / kWarps;
   if constexpr (SEQ) {  // one CTA per (sequence, head group), all tokens of it
     const int64_t grid = (int64_t)ngrp * kp.B;
     return launch_pdl(kern, dim3((unsigned)grid), dim3(kWarps * 32), (size_t)L.smem, stream, kp, L, 0);
   }
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, L.smem) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
+  if (occupancy_per_sm(cache, kern, kWarps * 32, (size_t)L.smem, &per_sm) != cudaSuccess || per_sm < 1) per_sm = 1;
   const int sms = num_sms_cached();
   const int64_t slots = (int64_t)sms * per_sm;
   const int64_t items = (int64_t)kp.B * ngrp;

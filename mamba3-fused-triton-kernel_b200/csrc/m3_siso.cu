@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kSisoThreads) siso_stream_kernel(const KParams
   if (tid == 0) {
     for (int q2 = k; q2 < k + sp.nstage; ++q2)
       if (tile_of(q2) < ntiles)
-        mbar_wait(smem_addr(&bars[q2 % sp.nstage]), (uint32_t)((q2 / sp.nstage) & 1), 1 << 16);
+        mbar_wait(smem_addr(&bars[q2 % sp.nstage]), (uint32_t)((q2 / sp.nstage) & 1));  // full bound: a copy may still land
   }
 }
 
@@ -438,17 +438,7 @@ StreamPlan make_plan(const KParams &kp, int BD, bool staged, int nstage, int *sm
   return sp;
 }
 
-int num_sms() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
+int num_sms() { return sm_count_current(); }
 
 template <int BD, bool FULL, bool STAGED, typename T>
 cudaError_t launch_t(const KParams &kp, cudaStream_t stream) {
@@ -457,25 +447,14 @@ cudaError_t launch_t(const KParams &kp, cudaStream_t stream) {
   if (smem > kMaxSmem) sp = make_plan(kp, BD, STAGED, 2, &smem);
   if (smem > kMaxSmem) return cudaErrorInvalidValue;
   auto kern = siso_stream_kernel<BD, FULL, STAGED, T>;
-  // Once per kernel: opt in to the largest ring any call may need.  Then
-  // CTAs per SM for this ring size (cached for the last size seen).
-  static bool attr = false;
-  static int last_smem = -1, last_per_sm = 1;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  if (smem != last_smem) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSisoThreads, smem) != cudaSuccess ||
-        per_sm < 1)
-      per_sm = 1;
-    last_smem = smem;
-    last_per_sm = per_sm;
-  }
+  // Once per kernel and device: opt in to the largest ring any call may
+  // need.  Then CTAs per SM for this ring size (per device, last size seen).
+  static LaunchCache cache;
+  if (cudaError_t e = ensure_smem_optin(cache, kern, kMaxSmem); e != cudaSuccess) return e;
+  int per_sm = 0;
+  if (occupancy_per_sm(cache, kern, kSisoThreads, (size_t)smem, &per_sm) != cudaSuccess || per_sm < 1) per_sm = 1;
   const int ntiles = kp.B * kp.H;
-  int grid = num_sms() * last_per_sm;
+  int grid = num_sms() * per_sm;
   if (grid > ntiles) grid = ntiles;
   return launch_pdl(kern, dim3(grid), dim3(kSisoThreads), (size_t)smem, stream, kp, sp);
 }

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 2) siso_prefill_kernel(const KParams
       // chunks still in flight (the last kSlots issued) before leaving.
       if (issuer)
         for (int k = issued > kSlots ? issued - kSlots : 0; k < issued; ++k)
-          mbar_wait(smem_addr(&bars[k % kSlots]), (uint32_t)((k / kSlots) & 1), 1 << 16);
+          mbar_wait(smem_addr(&bars[k % kSlots]), (uint32_t)((k / kSlots) & 1));  // full bound: a copy may still land
       return;
     }
     if (pw == 0) {
@@ -454,12 +454,9 @@ int passes_for(int P) {
 template <int BD, int NP, typename T>
 cudaError_t launch_np(const KParams &kp, const PrefLayout &lay, cudaStream_t stream) {
   auto kern = siso_prefill_kernel<BD, NP, T>;
-  static int attr_smem = 0;
-  if (lay.smem > 48 * 1024 && lay.smem > attr_smem) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lay.smem);
-    if (e != cudaSuccess) return e;
-    attr_smem = lay.smem;
-  }
+  static LaunchCache cache;
+  if (lay.smem > 48 * 1024)
+    if (cudaError_t e = ensure_smem_optin(cache, kern, lay.smem); e != cudaSuccess) return e;
   return launch_pdl(kern, dim3((unsigned)(kp.B * kp.H)), dim3(kThreads), (size_t)lay.smem, stream, kp, lay);
 }
 

@@ -50,6 +50,9 @@ cudaError_t launch_mimo_step(StepParams &sp, cudaStream_t stream);
 cudaError_t launch_mimo_step_f32(StepParams &sp, cudaStream_t stream);
 cudaError_t launch_mimo_step_bf16(StepParams &sp, cudaStream_t stream);
 int step_device_error(bool reset);
+// The checks of m3_mimo_step without the launch (M3_OK when it would launch;
+// *empty when the batch has no rows).
+int step_validate(const m3_dims *d, const m3_step_args *a, bool *empty);
 int step_f32_device_error(bool reset);
 int step_bf16_device_error(bool reset);
 

@@ -341,17 +341,7 @@ __global__ void __launch_bounds__(kStepThreads, 2) mimo_step_kernel(const StepPa
 // host side
 // ---------------------------------------------------------------------------
 
-int num_sms_current() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
+int num_sms_current() { return sm_count_current(); }
 
 size_t step_smem_bytes(int R, int BD, int A) {
   int f = 2 * row_block_floats(R, BD, A);
@@ -366,27 +356,15 @@ template <int BD, int R, typename T, int KP>
 cudaError_t launch_step_t(StepParams &sp, cudaStream_t stream) {
   auto kern = mimo_step_kernel<BD, R, T, KP>;
   const size_t smem = step_smem_bytes(R, BD, sp.kp.A);
-  static int attr_dev[64] = {0};  // 1 + device once the attribute is set
-  static int per_sm_dev[64] = {0};
-  static size_t smem_dev[64] = {0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  static LaunchCache cache;
+  cudaError_t e = ensure_smem_optin(cache, kern, 96 * 1024);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (attr_dev[dev] == 0) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_dev[dev] = 1;
-  }
-  if (smem_dev[dev] != smem || per_sm_dev[dev] == 0) {
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStepThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    per_sm_dev[dev] = per_sm > 2 ? 2 : per_sm;
-    smem_dev[dev] = smem;
-  }
-  const int grid = num_sms_current() * per_sm_dev[dev];
+  int per_sm = 0;
+  e = occupancy_per_sm(cache, kern, kStepThreads, smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  if (per_sm > 2) per_sm = 2;
+  const int grid = num_sms_current() * per_sm;
 
   // phase-2 work items: (head group, run of rows), about one per CTA
   const int ngrp = sp.kp.H / kRowWarps;

@@ -65,14 +65,19 @@ extern "C" int m3_mimo_step_static(const m3_dims *dims, const m3_step_args *args
   void *scratch = nullptr;
   const int st = scratch_address(&scratch);
   if (st != M3_OK) return st;
+  m3_step_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kStaticScratchBytes;
+  // a call that m3_mimo_step would reject, or that has no rows, enqueues
+  // nothing (and leaves the array alone)
+  bool empty = false;
+  const int check = m3::step_validate(dims, &a, &empty);
+  if (check != M3_OK || empty) return check;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // the grid-barrier words start every call at zero
   if (cudaMemsetAsync(scratch, 0, m3::kStepBarBytes, s) != cudaSuccess) {
     cudaGetLastError();
     return M3_ERR_LAUNCH;
   }
-  m3_step_args a = *args;
-  a.workspace = scratch;
-  a.workspace_bytes = kStaticScratchBytes;
   return m3_mimo_step(dims, &a, stream);
 }
