@@ -118,6 +118,7 @@ class Mamba3Decoder:
         self._host_output = None
         self.use_single_launch = bool(use_single_launch)
         self._step_cache = None
+        self._host_calls = 0
 
     # ------------------------------------------------------------------
     # public API
@@ -146,6 +147,7 @@ class Mamba3Decoder:
         for _ in range(n_warmup):
             step_fn(self._graph_input, state)
         torch.cuda.synchronize(device)
+        self.check_device_error()
         self._cuda_graph = torch.cuda.CUDAGraph()
         self._host_graph = None
         self._host_output = None
@@ -194,7 +196,39 @@ class Mamba3Decoder:
             self._cuda_graph.replay()
             self._host_output.copy_(self._graph_output, non_blocking=True)
         torch.cuda.synchronize()
+        self._host_calls += 1
+        if self._host_calls % self.DEVICE_ERROR_INTERVAL == 0:
+            self.check_device_error()
         return self._host_output
+
+    # step_host reads the library's device error word every this many calls
+    # (the read costs a few small synchronous copies)
+    DEVICE_ERROR_INTERVAL = 256
+
+    def check_device_error(self) -> None:
+        """Raise if a library kernel gave up a bounded wait since the last
+        check (the word is process-wide and cleared by the read).
+
+        Such a kernel skipped the rest of its work: the outputs and the state
+        of the steps since the previous check are undefined, and the
+        single-launch step's grid-barrier words no longer agree, so every
+        later launch on its workspace would time out too.  Before raising,
+        the workspace is zeroed again, so the decoder can go on after the
+        caller has restored a state it trusts.  Synchronises the device.
+        Called by ``warmup_cuda_graph``, every ``DEVICE_ERROR_INTERVAL``
+        calls of ``step_host`` and at the end of ``decode_sequence``."""
+        err = _native.device_error(reset=True)
+        if err == 0:
+            return
+        launch = self._step_cache[1] if self._step_cache is not None else None
+        if launch is not None:
+            launch.workspace.zero_()
+            torch.cuda.synchronize(launch.workspace.device)
+        if err < 0:
+            raise RuntimeError("the library's device error word could not be read")
+        raise RuntimeError(f"a decode kernel gave up a bounded wait (device error {err:#x}): the outputs "
+                           "and state of the steps since the last check are undefined; the step "
+                           "workspace has been zeroed again")
 
     def step(self, u: torch.Tensor, state: dict) -> tuple:
         """One decode step: u (batch, d_model) -> (out (batch, d_model), state)."""
@@ -221,6 +255,9 @@ class Mamba3Decoder:
             out, state = self.step(token_embeddings[:, t], state)
             # graph replay returns one static buffer; keep each step's value
             outs.append(out.clone() if self._cuda_graph is not None else out)
+        if seq_len and token_embeddings.is_cuda and (self.use_triton or self.use_triton_fused
+                                                     or self.use_triton_full_fused):
+            self.check_device_error()
         return torch.stack(outs, dim=1), state
 
     # ------------------------------------------------------------------

@@ -246,3 +246,34 @@ def test_decode_sequence_graph_mode_keeps_every_output():
         o_e, _ = eager.decode_sequence(u)
         o_g, _ = graph.decode_sequence(u, st)
     torch.testing.assert_close(o_g, o_e, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_second_device_in_the_same_process():
+    """Kernels launched with a dynamic shared memory opt-in (the streamed
+    MIMO kernel, the SISO kernel, both prefill kernels) on cuda:1 after
+    cuda:0 in one process: the opt-in is made per device, so each device's
+    results match PyTorch eager on that device."""
+    for dev in ("cuda:0", "cuda:1"):
+        for mimo in (False, True):
+            with torch.cuda.device(dev):
+                torch.manual_seed(5)
+                model = Mamba3(d_model=512, d_state=128, headdim=64, is_mimo=mimo, mimo_rank=4, device=dev)
+                ref = Mamba3Decoder(model, use_triton=False)
+                fused = Mamba3Decoder(model, use_triton_full_fused=True)
+                B = 300
+                s_ref, s = ref.init_state(B, device=dev), fused.init_state(B, device=dev)
+                g = torch.Generator(device=dev).manual_seed(6)
+                u = torch.randn(B, 4, 512, device=dev, generator=g)
+                with torch.no_grad():
+                    for t in range(4):
+                        o_ref, s_ref = ref.step(u[:, t], s_ref)
+                    o, s = fused.prefill(u, s)
+                torch.testing.assert_close(o[:, -1], o_ref, rtol=1e-4, atol=1e-4)
+                for k in s_ref:
+                    torch.testing.assert_close(s[k], s_ref[k], rtol=1e-4, atol=1e-4)
+                with torch.no_grad():
+                    o_ref, s_ref = ref.step(u[:, 0], s_ref)
+                    o, s = fused.step(u[:, 0], s)
+                torch.testing.assert_close(o, o_ref, rtol=1e-4, atol=1e-4)
+                assert o.device == torch.device(dev)

@@ -123,6 +123,42 @@ def test_barrier_words_advance_by_two_grids():
     assert nat.device_error() == 0
 
 
+def test_decoder_reports_and_recovers_from_a_barrier_timeout():
+    """A base word that the arrival counter can never reach makes the step's
+    grid barriers wait out their bound (every CTA is resident, so nothing
+    faults or hangs; the kernel records the timeout and returns).  The
+    decoder's check raises, clears the error word and zeroes the workspace,
+    after which the same decoder decodes correctly from a fresh state."""
+    _, dims, params, model = _layer(256, 64, 32, 4, seed=6)
+    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    st = dec.init_state(8, device="cuda")
+    u = orc.synthetic_inputs(dims, 8, 3, 1)
+    assert nat.device_error(reset=True) == 0
+    with torch.no_grad():
+        dec.step(torch.from_numpy(u[0]).cuda(), st)
+        launch = dec._step_cache[1]
+        assert launch is not None
+        torch.cuda.synchronize()
+        dec.check_device_error()  # nothing to report yet
+        base = launch.workspace[:4].view(torch.int32)
+        base.fill_(0x40000000)  # far ahead of the arrival counter
+        dec.step(torch.from_numpy(u[1]).cuda(), st)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="bounded wait"):
+            dec.check_device_error()
+        assert nat.device_error() == 0
+        assert int(launch.workspace.view(torch.int32)[:64].abs().sum()) == 0
+        # recovered: a fresh state decodes like the oracle again
+        st = dec.init_state(8, device="cuda")
+        st_np = orc.init_state(dims, 8)
+        for t in range(3):
+            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            oe, st_np = orc.decode_step(u[t], params, dims, st_np)
+            np.testing.assert_allclose(o.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
+        assert dec._step_cache[1] is launch
+    assert nat.device_error() == 0
+
+
 def test_decoder_policy_bounds_the_projection_work():
     from src.models.inference import SINGLE_LAUNCH_MAX_BATCH, single_launch_preferred
     _, _, _, small = _layer(64, 16, 16, 2, seed=4)
