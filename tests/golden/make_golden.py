@@ -3,7 +3,7 @@
 Run in a container that has the reference checkout (read-only is fine):
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py \
-        --reference /root/reference --out tests/golden
+        --reference <reference checkout> --out tests/golden
 
 For every case the weights and token embeddings come from the seeded numpy
 generators in ``oracle/mamba3_oracle.py`` (``synthetic_params`` /
@@ -251,7 +251,7 @@ def make_init_case(mods, name, spec, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the reference checkout (its src/ is imported)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     mods = _ref_modules(args.reference)
