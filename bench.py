@@ -3,36 +3,47 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {native,reference}]
                     [--workload NAME]
 
-Default workload: one MIMO rank-4 Mamba-3 layer, d_model=256, d_inner=512,
-headdim=32 (16 heads), d_state=64, fp32 weights and state, 128 sequences per
-GPU (the reference's MIMO R4 d256 decode benchmark at its largest batch).
-Weights: torch.manual_seed(0), in_proj / out_proj ~ N(0, 0.02), the other
-parameters per the layer's own init; inputs u ~ N(0, 1) from seed 1;
-synthetic data, zero initial state.
+Default workload: the 24-layer MIMO rank-4 stack (residual + RMSNorm between
+blocks), d_model=2048, d_inner=4096, headdim=64 (64 heads), d_state=128,
+bf16 weights, fp32 state, a global batch of 256 sequences split evenly over
+the N GPUs (strong scaling: 256 / N sequences per GPU) -- the largest
+configuration of the reference's decode that one GPU holds.  Weights:
+torch.manual_seed(0), in_proj / out_proj ~ N(0, 0.02), the other parameters
+per the layer's own init; inputs u ~ N(0, 1) from seed 1 + rank; synthetic
+data, zero initial state.  Every workload's batch is global and split the
+same way.
 
-A step is one decode step of the whole batch through the captured CUDA graph
-(in_proj GEMM -> fused decode kernel -> out_proj GEMM; small fp32 batches run
-the library's small-batch GEMM, larger ones cuBLAS).  Between timed steps
-L2 is flushed by writing a 256 MiB buffer; each step is timed with its own
-CUDA event pair on the launching stream (the flush is outside the pair).
-``value`` = tokens / (sum of step times), max over ranks, all ranks' tokens.
+A step is one decode step of the rank's sequences through all layers,
+replayed from one captured CUDA graph.  Between timed steps L2 is flushed
+by writing a 256 MiB buffer; each step is timed with its own CUDA event
+pair on the launching stream (the flush is outside the pair).  ``value`` =
+global batch x K / (max over ranks of the summed step times).
 
 ``e2e`` times the public API end to end: per step, the pinned host input
-is copied to the device, ``Mamba3Decoder.step`` replays the graph on it,
-the output is copied back to pinned host memory and the stream is
-synchronised so the host holds the result; the event pair brackets all of
-it, after an L2 flush that has completed.
+is copied to the device, the decoder's ``step`` replays the graph, the
+output is copied back to pinned host memory and the stream synchronised
+so the host holds the result; the event pair brackets all of it.  Its mean
+and p50 are reported.
 
-``roofline`` is for the fused decode kernel: its algorithmic HBM bytes per
-launch over its mean duration in a K-launch event-timed loop with the same
-L2 flush (the kernel replayed from a one-node CUDA graph, so host dispatch
-stays out of the timing), against the measured HBM copy bandwidth.
-``kernels_ms`` times the step's three kernels the same way.  ``cpu_baseline`` times the numpy oracle (a restatement of the
-reference's PyTorch decode) on the host cores for a bounded sample.
+``roofline`` is the dominant kernel of one layer (the fused decode kernel,
+or the single-launch step where a layer runs as one kernel): algorithmic
+HBM bytes per launch over its mean duration in an event-timed loop with
+the same L2 flush (replayed from a one-node CUDA graph, so host dispatch
+stays out of the timing), against the measured HBM copy bandwidth.  At
+N=1 the default run adds ``fused_rooflines``: the same measurement for the
+fused kernel of the d512 bf16 SISO layer at batch 512 and of the d1024
+fp32 MIMO layers (R = 1, 2, 4, 8) at batch 4096.
 
-Multi-GPU (torchrun): every rank decodes its own 128 sequences with a full
-weight replica and its own graph; no collective runs on the decode path
-(NCCL is used for the barrier and the max-over-ranks timing only).
+``cpu_baseline`` and ``--impl reference`` time the reference's own
+PyTorch CPU decode (``Mamba3Decoder(model, use_triton=False).step``,
+composed over the stack's ``MambaBlock``s) on the host cores, unmodified,
+in a separate interpreter (``oracle/reference_cpu.py``, from the copy that
+``oracle/stage_reference.py`` staged under ``baseline/_ref``); without that
+copy they fall back to the numpy restatement (``kind: "port"``).
+
+Multi-GPU (torchrun): every rank decodes its share of the global batch with
+a full weight replica and its own graph; no collective runs on the decode
+path (NCCL is used for the barrier and the max-over-ranks timing only).
 """
 
 from __future__ import annotations
@@ -51,7 +62,7 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "mamba3-fused-triton-kernel_b200")]
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-# name -> (layer kwargs, batch per GPU, weight dtype)
+# name -> (layer kwargs, global batch, weight dtype)
 WORKLOADS = {
     "mimo_r4_d256_b128": (dict(d_model=256, d_state=64, headdim=32, is_mimo=True, mimo_rank=4), 128, "f32"),
     "siso_d256_b1": (dict(d_model=256, d_state=64, headdim=32), 1, "f32"),
@@ -77,7 +88,7 @@ WORKLOADS["prefill_d2048_b64_l512_bf16"] = (dict(d_model=2048, d_state=128, head
                                                  mimo_rank=4), 64, "bf16")
 WORKLOADS["prefill_siso_d2048_b64_l512_bf16"] = (dict(d_model=2048, d_state=128, headdim=64), 64, "bf16")
 WORKLOADS["lm24_d2048_b256_bf16"] = WORKLOADS["stack24_d2048_b256_bf16"]
-DEFAULT_WORKLOAD = "mimo_r4_d256_b128"
+DEFAULT_WORKLOAD = "stack24_d2048_b256_bf16"
 # Published reference number for the default workload: MIMO d256 B=128
 # full-fused + CUDA graph P50 step latency 0.295 ms on an A100-PCIE-40GB
 # (reference README.md:229) -> 128 / 0.295 ms tokens/s.
@@ -208,73 +219,251 @@ def cpu_oracle_rate(kw, batch, dtype_name, steps=None, budget_s=10.0, warmup=1):
     return batch * n / el, n, os.cpu_count() or 1
 
 
-def config_dict(workload, kw, batch, world, dtype_name, reference=False):
+def shard_rows(global_batch: int, world: int) -> int:
+    """Sequences each rank decodes: the global batch split evenly (strong
+    scaling); every sequence is independent, so no collective is needed."""
+    if global_batch % world:
+        raise SystemExit(f"the global batch {global_batch} does not split evenly over {world} GPUs")
+    return global_batch // world
+
+
+def reference_cpu_rate(kw, batch, dtype_name, layers=1, steps=0, budget_s=10.0, warmup=1):
+    """The reference's own PyTorch CPU decode of `batch` sequences through
+    `layers` blocks, timed on the host cores in its own interpreter
+    (oracle/reference_cpu.py, no GPU visible).  Returns (result dict, None)
+    or (None, why it is unavailable)."""
+    cmd = [sys.executable, os.path.join(ROOT, "oracle", "reference_cpu.py"), "--layer", json.dumps(kw),
+           "--dtype", dtype_name, "--batch", str(batch), "--layers", str(layers), "--warmup", str(warmup),
+           "--budget", str(budget_s)]
+    if steps:
+        cmd += ["--steps", str(steps)]
+    env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", CUDA_VISIBLE_DEVICES="")
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=1800)
+    except subprocess.TimeoutExpired:
+        return None, "the reference CPU run timed out"
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return None, f"the reference CPU run failed (rc {r.returncode}): {r.stderr.strip()[-200:]}"
+    d = json.loads(lines[-1])
+    if "unavailable" in d:
+        return None, d["unavailable"]
+    return d, None
+
+
+def cpu_baseline(kw, batch, dtype_name, layers=1, budget_s=10.0, steps=0, warmup=1):
+    """(cpu_baseline dict, ms per step, steps timed): the reference's own
+    CPU decode when its staged copy is present, else the numpy port."""
+    d, why = reference_cpu_rate(kw, batch, dtype_name, layers, steps, budget_s, warmup)
+    if d is not None:
+        what = f" through {layers} MambaBlocks (x <- x + step(norm(x)))" if layers > 1 else ""
+        return ({"value": round(d["tokens_per_s"], 1), "unit": "tokens/s", "cores": d["threads"],
+                 "kind": "reference",
+                 "sample": f"{d['steps']} steps of the reference's Mamba3Decoder(use_triton=False).step on "
+                           f"{batch} sequences{what}, {dtype_name} weights, torch CPU with {d['threads']} "
+                           f"threads, p50 {d['p50_ms']:.2f} ms"},
+                d["ms_per_step"], d["steps"])
+    rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=steps or None, budget_s=budget_s, warmup=warmup)
+    rate /= layers
+    return ({"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+             "sample": f"{n} oracle decode steps of one layer x {batch} sequences (numpy restatement), rate "
+                       f"divided by {layers} layers; the reference itself was unavailable: {why}"},
+            1000.0 * batch / rate, n)
+
+
+def config_dict(workload, kw, global_batch, world, dtype_name, reference=False):
     published = PUBLISHED.get(workload)
     if reference:
-        par, l2, step = ("rank 0 only (host cores)", "n/a (CPU)",
-                         "oracle decode step (numpy restatement of the reference PyTorch decode)")
+        par, l2, step = ("rank 0 only (host cores), the whole global batch", "n/a (CPU)",
+                         "the reference's PyTorch CPU decode step")
     else:
-        par = f"batch-sharded x{world}, no collective on the decode path"
+        par = f"batch-sharded x{world} ({global_batch // world} sequences per GPU), no collective on the decode path"
         l2 = "flushed (256 MiB write) before every timed step; per-step CUDA events"
         step = ("CUDA-graph replay of Mamba3Decoder.step: one single-launch kernel (in_proj, fused update, "
                 "out_proj) for MIMO layers it takes, else in_proj GEMM + fused decode kernel + out_proj GEMM")
-    return {"workload": workload, "batch_per_gpu": batch, "global_batch": batch * world,
+    return {"workload": workload, "batch_per_gpu": global_batch // world, "global_batch": global_batch,
             **kw, "weights": dtype_name, "state": "f32", "parallelism": par, "l2": l2, "step": step,
             "baseline": ("A100 full-fused+graph P50 0.295 ms at B=128 (reference README.md:229)"
                          if published else None)}
 
 
-def run_reference(args, kw, batch, dtype_name, rank):
-    """--impl reference: the oracle port of the reference's CPU decode (for a
-    stack: one layer's rate divided by the number of layers)."""
+def run_reference(args, kw, global_batch, dtype_name, rank):
+    """--impl reference: the reference's own PyTorch CPU decode of the whole
+    global batch on rank 0's host cores (stacks: through all their blocks),
+    each timed step one decode step; bounded to about a minute of steps."""
     if rank != 0:
         return
     layers = STACKS.get(args.workload, 1)
-    steps = args.steps if layers == 1 else min(args.steps, 3)
-    cpu_oracle_rate(kw, batch, dtype_name, steps=max(min(args.warmup, steps), 1), warmup=0)  # warm-up
-    rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, steps=steps, warmup=0)
-    rate /= layers
-    ms = 1000.0 * batch / rate
-    cfg = config_dict(args.workload, kw, batch, 1, dtype_name, reference=True)
-    metric, sample = "decode tokens/s", f"{n} oracle decode steps of {batch} sequences (numpy, host cores)"
+    cpu, ms, n = cpu_baseline(kw, global_batch, dtype_name, layers, budget_s=60.0, steps=args.steps,
+                              warmup=min(args.warmup, 3))
+    cfg = config_dict(args.workload, kw, global_batch, 1, dtype_name, reference=True)
+    cfg["layers"] = layers
+    metric = "decode tokens/s"
     if args.workload in PREFILLS:
         # a prefill on the host is one decode step per prompt token, so its
         # tokens/s is the decode rate; ms_per_step stays one batch of tokens
         metric = "prefill tokens/s"
         cfg["prompt_tokens"] = PREFILLS[args.workload]
-        sample += " (a prefill on the host steps every prompt token)"
+        cpu["sample"] += " (a prefill on the host steps every prompt token)"
+    if args.workload in LM_WORKLOADS:
+        cpu["sample"] += " (embedding and LM head not included)"
     line = {
-        "metric": metric, "value": round(rate, 1), "unit": "tokens/s", "impl": "reference",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": cfg,
-        "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": metric, "value": cpu["value"], "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype_name,
+        "data": "synthetic", "config": cfg, "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
+class Harness:
+    """Per-rank plumbing shared by every workload: the device, the process
+    group (N > 1), the L2 flush buffer, event-timed loops, max over ranks
+    and the clock sampler."""
+
+    def __init__(self, world: int, rank: int, local: int):
+        import datetime
+
+        import torch.distributed as dist
+
+        self.dist, self.world, self.rank = dist, world, rank
+        torch.cuda.set_device(local)
+        self.dev = torch.device("cuda", local)
+        if world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+        self.flush = torch.empty(FLUSH_BYTES // 4, device=self.dev, dtype=torch.float32)
+        self.stream = torch.cuda.current_stream(self.dev)
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        try:
+            gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
+        except ValueError:
+            gpus = list(range(world))
+        self.sampler = ClockSampler(gpus) if rank == 0 else None
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], device=self.dev, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed_loop(self, fn, n: int, pre_sync: bool = False) -> np.ndarray:
+        """n calls of fn(i), each bracketed by its own CUDA event pair on the
+        launching stream after an L2 flush; per-call milliseconds.  With
+        ``pre_sync`` the host waits for the flush before the pair (end-to-end
+        calls that synchronise themselves), else a short device sleep keeps
+        the GPU busy while the host enqueues the call."""
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            self.flush.zero_()
+            if pre_sync:
+                self.stream.synchronize()
+            else:
+                torch.cuda._sleep(20000)
+            ev[i][0].record(self.stream)
+            fn(i)
+            ev[i][1].record(self.stream)
+        torch.cuda.synchronize(self.dev)
+        return np.array([a.elapsed_time(b) for a, b in ev])
+
+    def graphed(self, fn, warm: int = 3):
+        """fn captured in a CUDA graph (after `warm` calls on a side stream)."""
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(self.stream)
+        with torch.cuda.stream(side):
+            for _ in range(warm):
+                fn()
+        self.stream.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    def clocks_start(self):
+        if self.sampler:
+            self.sampler.start()
+            time.sleep(0.2)
+
+    def clocks_mark(self):
+        if self.sampler:
+            self.sampler.mark()
+
+    def clocks_stop(self):
+        return self.sampler.stop() if self.sampler else None
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def e2e_summary(h: Harness, ms: np.ndarray, tokens_per_step: int, h2d: int, d2h: int, path: str) -> dict:
+    total = h.max_over_ranks(float(ms.sum()))
+    p50 = h.max_over_ranks(float(np.percentile(ms, 50)))
+    return {"value": round(tokens_per_step * len(ms) / (total / 1000.0), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(total / len(ms), 5),
+            "p50_ms": round(p50, 5), "steps": len(ms), "path": path}
+
+
+def fused_kernel_roofline(h: Harness, kw: dict, batch: int, dtype_name: str, n: int) -> dict:
+    """One layer's fused decode kernel alone (replayed from a one-node graph,
+    L2 flushed before every launch): mean CUDA-event time of n launches and
+    its algorithmic HBM bytes against the measured copy bandwidth."""
+    from src.kernels.linear import linear
+    from src.models.inference import Mamba3Decoder
+    from src.models.mamba3 import Mamba3
+
+    wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    torch.manual_seed(0)
+    model = Mamba3(**kw, device=h.dev, dtype=wdtype)
+    with torch.no_grad():
+        model.in_proj.weight.normal_(0.0, 0.02)
+        dec = Mamba3Decoder(model, use_triton_full_fused=True)
+        state = dec.init_state(batch, device=h.dev)
+        gen = torch.Generator(device=h.dev).manual_seed(1)
+        zx = linear(torch.randn(batch, model.d_model, device=h.dev, generator=gen).to(wdtype), model.in_proj.weight)
+        y = torch.zeros(batch, model.d_inner, device=h.dev, dtype=wdtype)
+        launch = dec._fused_launch(state)
+        g = h.graphed(lambda: launch.run(zx, y))
+        ms = h.timed_loop(lambda i: g.replay(), n)
+    del g
+    es = 2 if wdtype == torch.bfloat16 else 4
+    nbytes = fused_bytes_per_launch(model, batch, es, es)
+    mean = h.max_over_ranks(float(ms.mean()))
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes / (mean * 1e-3) / 1e9
+    return {"kernel": "m3_mimo_full_fused" if model.is_mimo else "m3_siso_full_fused", "batch": batch,
+            "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes, "mean_launch_ms": round(mean, 5)}
+
+
+# fused-kernel rooflines added to the default run at N=1: the wide SISO layer
+# at its largest batch and the throughput sweep's layer at every rank
+EXTRA_ROOFLINES = ["siso_d512_b512_bf16", "mimo_r1_d1024_b4096", "mimo_r2_d1024_b4096", "mimo_r4_d1024_b4096",
+                   "mimo_r8_d1024_b4096"]
+WORKLOADS["mimo_r2_d1024_b4096"] = (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=2), 4096,
+                                    "f32")
+
+
+def run_stack(args, kw, global_batch, dtype_name, layers, world, rank, local):
     """A residual stack of `layers` MIMO blocks decoded token by token through
-    Mamba3StackDecoder, the whole stack step in one CUDA graph.  Same timing
-    rules as the single-layer path: L2 flushed and a CUDA event pair around
-    every timed step, max over ranks.  `roofline` is the library's fused
-    decode kernel of one layer (the projections are cuBLAS bf16 GEMMs, whose
-    rate is reported beside it)."""
-    import datetime
-
-    import torch.distributed as dist
-
+    Mamba3StackDecoder, the whole stack step in one CUDA graph, each rank
+    decoding its share of the global batch.  `roofline` is one layer's fused
+    decode kernel; the projections' rate is reported beside it."""
     from src.kernels.linear import linear
     from src.models.lm import Mamba3LMDecoder
     from src.models.mamba3 import MambaBlock, MambaConfig, MambaLMHeadModel
     from src.models.stack import Mamba3StackDecoder
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    h = Harness(world, rank, local)
+    dev = h.dev
+    batch = shard_rows(global_batch, world)
     wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
     torch.manual_seed(0)
     mkw = {k: v for k, v in kw.items() if k != "d_model"}
@@ -307,58 +496,22 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         u_host = torch.randn(n_inputs, batch, kw["d_model"], generator=gen).to(wdtype).pin_memory()
         out_shape = (batch, kw["d_model"])
     u_dev = u_host.to(dev)
-    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
-    stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         dec.warmup_cuda_graph(states, n_warmup=2)
         for i in range(W):
             dec.step(u_dev[i % n_inputs], states)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def timed_loop(fn, n, pre_sync=False):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for i in range(n):
-            flush.zero_()
-            if pre_sync:
-                stream.synchronize()
-            else:
-                torch.cuda._sleep(20000)
-            ev[i][0].record(stream)
-            fn(i)
-            ev[i][1].record(stream)
-        torch.cuda.synchronize(dev)
-        return np.array([a.elapsed_time(b) for a, b in ev])
-
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    try:
-        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
-    except ValueError:
-        gpus = list(range(world))
-    sampler = ClockSampler(gpus) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.2)
-    barrier()
-    if sampler:
-        sampler.mark()
+    h.clocks_start()
+    h.barrier()
+    h.clocks_mark()
     with torch.no_grad():
-        step_ms = timed_loop(lambda i: dec.step(u_dev[i % n_inputs], states), K)
-    barrier()
-    if sampler:
-        sampler.mark()
-    total_ms = max_over_ranks(float(step_ms.sum()))
-    value = world * batch * K / (total_ms / 1000.0)
+        step_ms = h.timed_loop(lambda i: dec.step(u_dev[i % n_inputs], states), K)
+    h.barrier()
+    h.clocks_mark()
+    total_ms = h.max_over_ranks(float(step_ms.sum()))
+    p50_all = h.max_over_ranks(float(np.percentile(step_ms, 50)))
+    p99_all = h.max_over_ranks(float(np.percentile(step_ms, 99)))
+    value = global_batch * K / (total_ms / 1000.0)
 
     # one layer's fused kernel (roofline) and its two projections
     es = 2 if wdtype == torch.bfloat16 else 4
@@ -368,28 +521,19 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         zx = linear(xn, model.in_proj.weight)
         y = torch.zeros(batch, model.d_inner, device=dev, dtype=wdtype)
         launch = layer._fused_launch(states[0])
-        graphs = []
-        for fn in (lambda: launch.run(zx, y), lambda: linear(xn, model.in_proj.weight),
-                   lambda: linear(y, model.out_proj.weight)):
-            side = torch.cuda.Stream(dev)
-            side.wait_stream(stream)
-            with torch.cuda.stream(side):
-                for _ in range(2):
-                    fn()
-            stream.wait_stream(side)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                fn()
-            graphs.append(g)
+        graphs = [h.graphed(fn, warm=2) for fn in (lambda: launch.run(zx, y),
+                                                   lambda: linear(xn, model.in_proj.weight),
+                                                   lambda: linear(y, model.out_proj.weight))]
         n_k = min(K, 200)
-        f_ms, gi_ms, go_ms = (timed_loop(lambda i, g=g: g.replay(), n_k) for g in graphs)
+        f_ms, gi_ms, go_ms = (h.timed_loop(lambda i, g=g: g.replay(), n_k) for g in graphs)
     del graphs
-    k_mean = max_over_ranks(float(f_ms.mean()))
+    k_mean = h.max_over_ranks(float(f_ms.mean()))
+    gi_mean = h.max_over_ranks(float(gi_ms.mean()))
+    go_mean = h.max_over_ranks(float(go_ms.mean()))
     nbytes = fused_bytes_per_launch(model, batch, es, es)
     peak, peak_kind = hbm_peak()
     achieved = nbytes / (k_mean * 1e-3) / 1e9
     gemm_flop = 2.0 * batch * model.d_model * (model.d_in_proj + model.d_inner)
-    gemm_ms = float(gi_ms.mean() + go_ms.mean())
 
     # end to end through the public API: pinned input in, output back to the host
     out_host = torch.empty(*out_shape, dtype=wdtype).pin_memory()
@@ -399,43 +543,45 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
         u_stage.copy_(u_host[i % n_inputs], non_blocking=True)
         out, _ = dec.step(u_stage, states)
         out_host.copy_(out, non_blocking=True)
-        stream.synchronize()
+        h.stream.synchronize()
 
-    barrier()
+    h.barrier()
     with torch.no_grad():
-        e2e_ms = timed_loop(e2e_step, min(K, 200), pre_sync=True)
-    barrier()
-    e2e_total = max_over_ranks(float(e2e_ms.sum()))
-    e2e_value = world * batch * len(e2e_ms) / (e2e_total / 1000.0)
-    clocks = sampler.stop() if sampler else None
+        e2e_ms = h.timed_loop(e2e_step, max(min(K, 500), 1), pre_sync=True)
+    h.barrier()
+    e2e = e2e_summary(h, e2e_ms, global_batch, u_stage.numel() * u_stage.element_size(),
+                      out_host.numel() * out_host.element_size(),
+                      "pinned input copied in, graph replay, output copied to pinned host memory, stream sync")
+    clocks = h.clocks_stop()
 
+    extra = None
+    if world == 1 and args.fused_rooflines and vocab is None:
+        extra = {}
+        for name in EXTRA_ROOFLINES:
+            ekw, eb, edt = WORKLOADS[name]
+            extra[name] = fused_kernel_roofline(h, ekw, eb, edt, min(K, 50))
     cpu = None
     if rank == 0 and world == 1:
-        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
-        cpu = {"value": round(rate / layers, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{n} oracle decode steps of one layer x {batch} sequences, rate divided by "
-                         f"{layers} layers (numpy float32 restatement with bf16 rounding"
-                         + ("; embedding and LM head not included" if vocab is not None else "") + ")"}
-    # every rank takes part in every collective, so they all run before the
-    # rank-0-only report
-    p50_all = max_over_ranks(float(np.percentile(step_ms, 50)))
-    if world > 1:
-        dist.barrier()
+        cpu, _, _ = cpu_baseline(kw, global_batch, dtype_name, layers, budget_s=args.cpu_budget)
+        if vocab is not None:
+            cpu["sample"] += " (embedding and LM head not included)"
+    h.close()
     if rank == 0:
-        cfg = config_dict(args.workload, kw, batch, world, dtype_name)
+        cfg = config_dict(args.workload, kw, global_batch, world, dtype_name)
+        proj = "cuBLAS bf16" if dtype_name == "bf16" else "cuBLAS / small-batch fp32"
         cfg.update({"layers": layers, "step": "CUDA-graph replay of Mamba3StackDecoder.step: per layer "
-                    "in_proj (cuBLAS bf16) + fused decode kernel + out_proj (cuBLAS bf16), residual add + "
-                    "RMSNorm kernel between blocks"})
+                    f"in_proj ({proj}) + fused decode kernel + out_proj ({proj}), residual add + RMSNorm "
+                    "kernel between blocks"})
         if vocab is not None:
             cfg.update({"model": "MambaLMHeadModel", "vocab_size": vocab, "padded_vocab": lm.vocab_size,
                         "step": "CUDA-graph replay of Mamba3LMDecoder.step: token ids -> embedding, per layer "
-                        "in_proj (cuBLAS bf16) + fused decode kernel + out_proj (cuBLAS bf16) + residual add "
-                        "and RMSNorm kernel, final norm, LM head (cuBLAS bf16) -> logits"})
+                        f"in_proj ({proj}) + fused decode kernel + out_proj ({proj}) + residual add and RMSNorm "
+                        "kernel, final norm, LM head -> logits"})
         line = {
             "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
-            "p50_step_ms": round(p50_all, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "p50_step_ms": round(p50_all, 5), "p99_step_ms": round(p99_all, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": dtype_name, "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "kernel": "fused decode (m3_mimo_full_fused), one layer",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
@@ -443,43 +589,33 @@ def run_stack(args, kw, batch, dtype_name, layers, world, rank, local):
                          "mean_launch_ms": round(k_mean, 5),
                          "traffic": profile_traffic(LM_STACK_PROFILE.get(args.workload, args.workload), "fused")},
             "kernels_ms": {"fused_decode_per_layer": round(k_mean, 5),
-                           "in_proj_gemm_per_layer": round(float(gi_ms.mean()), 5),
-                           "out_proj_gemm_per_layer": round(float(go_ms.mean()), 5),
-                           "projection_tflops": round(gemm_flop / (gemm_ms * 1e-3) / 1e12, 1)},
-            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": u_stage.numel() * u_stage.element_size(),
-                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
-                    "ms_per_step": round(e2e_total / len(e2e_ms), 5)},
+                           "in_proj_gemm_per_layer": round(gi_mean, 5),
+                           "out_proj_gemm_per_layer": round(go_mean, 5),
+                           "projection_tflops": round(gemm_flop / ((gi_mean + go_mean) * 1e-3) / 1e12, 1)},
+            "fused_rooflines": extra,
+            "e2e": e2e,
             "gpu_launches": K * (2 * layers + 1),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     dec._graph = None
-    if world > 1:
-        dist.destroy_process_group()
 
 
-def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
-    """Prompt prefill of one layer: `batch` sequences of `length` tokens
-    through Mamba3Decoder.prefill (one in_proj GEMM over all tokens, one
-    prefill launch -- m3_mimo_prefill or m3_siso_prefill -- and one out_proj
-    GEMM).  A
-    step is one whole prefill; L2 flushed and a CUDA event pair around every
-    timed step, max over ranks.  `roofline` is the prefill kernel alone: the
-    in_proj rows read once, y written once, the state read and written once."""
-    import datetime
-
-    import torch.distributed as dist
-
+def run_prefill(args, kw, global_batch, dtype_name, length, world, rank, local):
+    """Prompt prefill of one layer: each rank's share of `global_batch`
+    sequences of `length` tokens through Mamba3Decoder.prefill (one in_proj
+    GEMM over all tokens, one prefill launch -- m3_mimo_prefill or
+    m3_siso_prefill -- and one out_proj GEMM).  A step is one whole prefill.
+    `roofline` is the prefill kernel alone: the in_proj rows read once, y
+    written once, the state read and written once."""
     from src.kernels.linear import linear
     from src.models.inference import Mamba3Decoder
     from src.models.mamba3 import Mamba3
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    h = Harness(world, rank, local)
+    dev = h.dev
+    batch = shard_rows(global_batch, world)
     wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
     torch.manual_seed(0)
     model = Mamba3(**kw, device=dev, dtype=wdtype)
@@ -492,58 +628,20 @@ def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
     gen = torch.Generator(device="cpu").manual_seed(1 + rank)
     u_host = torch.randn(batch, length, kw["d_model"], generator=gen).to(wdtype).pin_memory()
     u_dev = u_host.to(dev)
-    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
-    stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(W):
             dec.prefill(u_dev, state)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def timed_loop(fn, n, pre_sync=False):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for i in range(n):
-            flush.zero_()
-            if pre_sync:
-                stream.synchronize()
-            else:
-                torch.cuda._sleep(20000)
-            ev[i][0].record(stream)
-            fn(i)
-            ev[i][1].record(stream)
-        torch.cuda.synchronize(dev)
-        return np.array([a.elapsed_time(b) for a, b in ev])
-
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    try:
-        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
-    except ValueError:
-        gpus = list(range(world))
-    sampler = ClockSampler(gpus) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.2)
-    barrier()
-    if sampler:
-        sampler.mark()
+    h.clocks_start()
+    h.barrier()
+    h.clocks_mark()
     with torch.no_grad():
-        step_ms = timed_loop(lambda i: dec.prefill(u_dev, state), K)
-    barrier()
-    if sampler:
-        sampler.mark()
-    total_ms = max_over_ranks(float(step_ms.sum()))
-    p50_all = max_over_ranks(float(np.percentile(step_ms, 50)))
-    value = world * batch * length * K / (total_ms / 1000.0)
+        step_ms = h.timed_loop(lambda i: dec.prefill(u_dev, state), K)
+    h.barrier()
+    h.clocks_mark()
+    total_ms = h.max_over_ranks(float(step_ms.sum()))
+    p50_all = h.max_over_ranks(float(np.percentile(step_ms, 50)))
+    value = global_batch * length * K / (total_ms / 1000.0)
 
     # the prefill kernel alone, on prepared in_proj rows
     es = 2 if wdtype == torch.bfloat16 else 4
@@ -551,8 +649,8 @@ def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
         zx = linear(u_dev.reshape(batch * length, -1), model.in_proj.weight)
         y = torch.empty(batch * length, model.d_inner, device=dev, dtype=wdtype)
         launch = dec._fused_launch(state)
-        k_ms = timed_loop(lambda i: launch.prefill(zx, y, length), min(K, 50))
-    k_mean = max_over_ranks(float(k_ms.mean()))
+        k_ms = h.timed_loop(lambda i: launch.prefill(zx, y, length), min(K, 50))
+    k_mean = h.max_over_ranks(float(k_ms.mean()))
     H, D, A = model.nheads, model.d_state, model.num_rope_angles
     R, P = model.mimo_rank, model.headdim
     # in_proj rows read once, y rows written once; h and bx_prev (MIMO: D per
@@ -576,90 +674,54 @@ def run_prefill(args, kw, batch, dtype_name, length, world, rank, local):
         u_stage.copy_(u_host, non_blocking=True)
         out, _ = dec.prefill(u_stage, state)
         out_host.copy_(out, non_blocking=True)
-        stream.synchronize()
+        h.stream.synchronize()
 
-    barrier()
+    h.barrier()
     with torch.no_grad():
-        e2e_ms = timed_loop(e2e_step, min(K, 50), pre_sync=True)
-    barrier()
-    e2e_total = max_over_ranks(float(e2e_ms.sum()))
-    e2e_value = world * batch * length * len(e2e_ms) / (e2e_total / 1000.0)
-    clocks = sampler.stop() if sampler else None
+        e2e_ms = h.timed_loop(e2e_step, max(min(K, 50), 1), pre_sync=True)
+    h.barrier()
+    e2e = e2e_summary(h, e2e_ms, global_batch * length, u_stage.numel() * es, out_host.numel() * es,
+                      "pinned prompt copied in, prefill, every output row copied to pinned host memory, stream sync")
+    clocks = h.clocks_stop()
     cpu = None
     if rank == 0 and world == 1:
-        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
-        cpu = {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{n} oracle decode steps of {batch} sequences (a prefill on the host is one decode "
-                         f"step per prompt token; numpy float32 restatement with bf16 rounding)"}
-    if world > 1:
-        dist.barrier()
+        cpu, _, _ = cpu_baseline(kw, global_batch, dtype_name, 1, budget_s=args.cpu_budget)
+        cpu["sample"] += " (a prefill on the host is one decode step per prompt token)"
+    h.close()
     if rank == 0:
-        cfg = config_dict(args.workload, kw, batch, world, dtype_name)
+        cfg = config_dict(args.workload, kw, global_batch, world, dtype_name)
         entry = "m3_mimo_prefill" if model.is_mimo else "m3_siso_prefill"
         cfg.update({"prompt_tokens": length, "step": "Mamba3Decoder.prefill of batch x prompt tokens: in_proj "
-                    f"(cuBLAS bf16) over all tokens, one {entry} launch, out_proj (cuBLAS bf16)"})
+                    f"over all tokens, one {entry} launch, out_proj"})
         line = {
             "metric": "prefill tokens/s", "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
-            "p50_step_ms": round(p50_all, 5), "higher_is_better": True, "scaling": "weak",
+            "p50_step_ms": round(p50_all, 5), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "kernel": (f"{entry} (streamed kernel, sequence form)" if model.is_mimo else
                                                    f"{entry} (state tile in registers)"),
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
                          "mean_launch_ms": round(k_mean, 5), "traffic": profile_traffic(args.workload, "prefill")},
-            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": u_stage.numel() * es, "d2h_bytes_per_step": out_host.numel() * es,
-                    "ms_per_step": round(e2e_total / len(e2e_ms), 5)},
+            "e2e": e2e,
             "gpu_launches": K,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
-    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of oracle CPU timing")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    kw, batch, dtype_name = WORKLOADS[args.workload]
-
-    if args.impl == "reference":
-        run_reference(args, kw, batch, dtype_name, rank)
-        return
-    if args.workload in STACKS:
-        run_stack(args, kw, batch, dtype_name, STACKS[args.workload], world, rank, local)
-        return
-    if args.workload in PREFILLS:
-        run_prefill(args, kw, batch, dtype_name, PREFILLS[args.workload], world, rank, local)
-        return
-
-    import datetime
-
-    import torch.distributed as dist
-
-    from src.kernels.linear import linear
+def run_layer(args, kw, global_batch, dtype_name, world, rank, local):
+    """One layer decoded through Mamba3Decoder's captured graph, each rank
+    decoding its share of the global batch."""
+    from src.kernels.linear import linear, uses_small_m_kernel
     from src.models.inference import Mamba3Decoder
     from src.models.mamba3 import Mamba3
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    h = Harness(world, rank, local)
+    dev = h.dev
+    batch = shard_rows(global_batch, world)
     wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
-
     torch.manual_seed(0)
     model = Mamba3(**kw, device=dev, dtype=wdtype)
     with torch.no_grad():
@@ -670,121 +732,62 @@ def main():
     n_inputs = 64
     u_host = torch.randn(n_inputs, batch, model.d_model, generator=gen).to(wdtype).pin_memory()
     u_dev = u_host.to(dev)
-
     dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
     state = dec.init_state(batch, device=dev)
     dec.warmup_cuda_graph(state, n_warmup=3)
-    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
-    stream = torch.cuda.current_stream(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def timed_loop(fn, n, pre_sync=False):
-        """n iterations of fn, each bracketed by its own event pair after an
-        L2 flush; returns per-iteration milliseconds."""
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for i in range(n):
-            flush.zero_()
-            if pre_sync:
-                stream.synchronize()
-            else:
-                torch.cuda._sleep(20000)  # keep the GPU busy while the host enqueues the step
-            ev[i][0].record(stream)
-            fn(i)
-            ev[i][1].record(stream)
-        torch.cuda.synchronize(dev)
-        return np.array([a.elapsed_time(b) for a, b in ev])
-
-    # ---- warm-up (graph replays) ----
     with torch.no_grad():
         for i in range(W):
             dec.step(u_dev[i % n_inputs], state)
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    try:
-        gpus = [int(x) for x in vis.split(",")][:world] if vis else list(range(world))
-    except ValueError:
-        gpus = list(range(world))
-    sampler = ClockSampler(gpus) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.2)
 
-    # ---- timed region: K decode steps ----
-    barrier()
-    if sampler:
-        sampler.mark()
+    h.clocks_start()
+    h.barrier()
+    h.clocks_mark()
     with torch.no_grad():
-        step_ms = timed_loop(lambda i: dec.step(u_dev[i % n_inputs], state), K)
-    barrier()
-    if sampler:
-        sampler.mark()
-    total_ms = max_over_ranks(float(step_ms.sum()))
-    p50 = max_over_ranks(float(np.percentile(step_ms, 50)))
-    p99 = max_over_ranks(float(np.percentile(step_ms, 99)))
-    value = world * batch * K / (total_ms / 1000.0)
+        step_ms = h.timed_loop(lambda i: dec.step(u_dev[i % n_inputs], state), K)
+    h.barrier()
+    h.clocks_mark()
+    total_ms = h.max_over_ranks(float(step_ms.sum()))
+    p50 = h.max_over_ranks(float(np.percentile(step_ms, 50)))
+    p99 = h.max_over_ranks(float(np.percentile(step_ms, 99)))
+    value = global_batch * K / (total_ms / 1000.0)
     # our kernels per step: the single-launch step kernel, or the fused decode
     # kernel plus both projections when they run on the library's small-batch
     # GEMM (otherwise cuBLAS)
     single = dec._step_cache is not None and dec._step_cache[1] is not None
-    from src.kernels.linear import uses_small_m_kernel
     own_gemms = int(uses_small_m_kernel(u_dev[0], model.in_proj.weight)) + int(
         uses_small_m_kernel(torch.empty(batch, model.d_inner, device=dev, dtype=wdtype), model.out_proj.weight))
     gpu_launches = K if single else K * (1 + own_gemms)
 
-    # ---- fused kernel alone (roofline) and the two GEMMs, same flush ----
-    # Each component is captured in its own CUDA graph and replayed between
-    # the events, so host-side dispatch cost stays out of the device times.
-    zx = linear(u_dev[0], model.in_proj.weight)
-    y = torch.zeros(batch, model.d_inner, device=dev, dtype=wdtype)
-    launch = dec._fused_launch(state)
-
-    def graphed(fn):
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                fn()
-        stream.wait_stream(side)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        return g
-
-    es = 2 if wdtype == torch.bfloat16 else 4
+    # the fused kernel alone (roofline) and the two GEMMs, each replayed from
+    # its own graph so host dispatch stays out of the device times
     with torch.no_grad():
-        g_fused = graphed(lambda: launch.run(zx, y))
-        g_in = graphed(lambda: linear(u_dev[0], model.in_proj.weight))
-        g_out = graphed(lambda: linear(y, model.out_proj.weight))
-        f_ms = timed_loop(lambda i: g_fused.replay(), K)
-        gi_ms = timed_loop(lambda i: g_in.replay(), min(K, 500))
-        go_ms = timed_loop(lambda i: g_out.replay(), min(K, 500))
+        zx = linear(u_dev[0], model.in_proj.weight)
+        y = torch.zeros(batch, model.d_inner, device=dev, dtype=wdtype)
+        launch = dec._fused_launch(state)
+        g_fused = h.graphed(lambda: launch.run(zx, y))
+        g_in = h.graphed(lambda: linear(u_dev[0], model.in_proj.weight))
+        g_out = h.graphed(lambda: linear(y, model.out_proj.weight))
+        f_ms = h.timed_loop(lambda i: g_fused.replay(), K)
+        gi_ms = h.timed_loop(lambda i: g_in.replay(), min(K, 500))
+        go_ms = h.timed_loop(lambda i: g_out.replay(), min(K, 500))
         # the three-launch step (in_proj, fused kernel, out_proj) on its own state
         dec3 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=False)
         st3 = dec3.init_state(batch, device=dev)
         dec3.warmup_cuda_graph(st3, n_warmup=3)
-        t3_ms = timed_loop(lambda i: dec3.step(u_dev[i % n_inputs], st3), min(K, 500))
+        t3_ms = h.timed_loop(lambda i: dec3.step(u_dev[i % n_inputs], st3), min(K, 500))
         dec3._cuda_graph = None
         if single:
             step_launch = dec._step_cache[1]
             out_static = torch.empty(batch, model.d_model, device=dev, dtype=wdtype)
-            g_step = graphed(lambda: step_launch.run(u_dev[0], out_static))
-            s_ms = timed_loop(lambda i: g_step.replay(), K)
+            g_step = h.graphed(lambda: step_launch.run(u_dev[0], out_static))
+            s_ms = h.timed_loop(lambda i: g_step.replay(), K)
             del g_step
     del g_fused, g_in, g_out
-    f_mean = max_over_ranks(float(f_ms.mean()))
+    es = 2 if wdtype == torch.bfloat16 else 4
+    f_mean = h.max_over_ranks(float(f_ms.mean()))
     if single:
         kernel_name = "single-launch decode step (m3_mimo_step)"
-        k_mean = max_over_ranks(float(s_ms.mean()))
+        k_mean = h.max_over_ranks(float(s_ms.mean()))
         nbytes = step_bytes_per_launch(model, batch, es)
     else:
         kernel_name = "fused decode (m3_mimo_full_fused / m3_siso_full_fused)"
@@ -792,67 +795,82 @@ def main():
         nbytes = fused_bytes_per_launch(model, batch, es, es)
     peak, peak_kind = hbm_peak()
     achieved = nbytes / (k_mean * 1e-3) / 1e9
+    gi_mean = h.max_over_ranks(float(gi_ms.mean()))
+    go_mean = h.max_over_ranks(float(go_ms.mean()))
+    t3_mean = h.max_over_ranks(float(t3_ms.mean()))
 
-    # ---- end to end through the public API (pinned host in/out) ----
-    # Mamba3Decoder.step_host: the pinned input is copied into the graph's
-    # input, the step writes its output rows to pinned host memory (directly
-    # from the single-launch kernel, else by a copy), and the call returns
-    # once the host can read them
-    def e2e_step(i):
-        dec.step_host(u_host[i % n_inputs])
-
-    barrier()
+    # end to end through the public API: Mamba3Decoder.step_host copies the
+    # pinned input into the graph's input and returns once the host holds the
+    # output rows (written by the single-launch kernel straight into pinned
+    # host memory where it serves the layer, else copied back)
+    h.barrier()
     with torch.no_grad():
-        e2e_ms = timed_loop(e2e_step, K, pre_sync=True)
-    barrier()
-    e2e_total = max_over_ranks(float(e2e_ms.sum()))
-    e2e_value = world * batch * K / (e2e_total / 1000.0)
-    clocks = sampler.stop() if sampler else None
-
+        e2e_ms = h.timed_loop(lambda i: dec.step_host(u_host[i % n_inputs]), K, pre_sync=True)
+    h.barrier()
+    path = ("pinned input copied in; the single-launch kernel stores the output rows into pinned host memory; "
+            "device synchronise" if dec._host_graph is not None else
+            "pinned input copied in; graph replay; output copied to pinned host memory; device synchronise")
+    e2e = e2e_summary(h, e2e_ms, global_batch, batch * model.d_model * es, batch * model.d_model * es, path)
+    clocks = h.clocks_stop()
     cpu = None
     if rank == 0 and world == 1:
-        rate, n, cores = cpu_oracle_rate(kw, batch, dtype_name, budget_s=args.cpu_budget)
-        cpu = {"value": round(rate, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{n} oracle decode steps of {batch} sequences (numpy float32 restatement "
-                         f"of the reference PyTorch decode; BLAS threads = host cores)"}
-
-    # every rank takes part in every collective, so they all run before the
-    # rank-0-only report
-    t3_all = max_over_ranks(float(t3_ms.mean()))
-    if world > 1:
-        dist.barrier()
+        cpu, _, _ = cpu_baseline(kw, global_batch, dtype_name, 1, budget_s=args.cpu_budget)
+    h.close()
     if rank == 0:
         published = PUBLISHED.get(args.workload)
         line = {
             "metric": "decode tokens/s", "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total_ms / K, 5),
             "p50_step_ms": round(p50, 5), "p99_step_ms": round(p99, 5),
-            "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(value / (world * published), 3) if published else None,
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": round(value / published, 3) if published and world == 1 else None,
             "dtype": dtype_name, "data": "synthetic",
-            "config": config_dict(args.workload, kw, batch, world, dtype_name),
+            "config": config_dict(args.workload, kw, global_batch, world, dtype_name),
             "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes,
                          "mean_launch_ms": round(k_mean, 5),
                          "traffic": profile_traffic(args.workload, "step" if single else "fused")},
             "kernels_ms": {"decode_step": round(k_mean, 5) if single else None,
-                           "three_launch_step": round(t3_all, 5),
-                           "in_proj_gemm": round(float(gi_ms.mean()), 5),
+                           "three_launch_step": round(t3_mean, 5),
+                           "in_proj_gemm": round(gi_mean, 5),
                            "fused_decode": round(f_mean, 5),
-                           "out_proj_gemm": round(float(go_ms.mean()), 5)},
-            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": batch * model.d_model * u_host.element_size(),
-                    "d2h_bytes_per_step": batch * model.d_model * u_host.element_size(),
-                    "ms_per_step": round(e2e_total / K, 5)},
+                           "out_proj_gemm": round(go_mean, 5)},
+            "e2e": e2e,
             "gpu_launches": gpu_launches,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     dec._cuda_graph = None
-    if world > 1:
-        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of reference CPU timing")
+    ap.add_argument("--no-fused-rooflines", dest="fused_rooflines", action="store_false",
+                    help="skip the extra fused-kernel rooflines of the default run")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    kw, global_batch, dtype_name = WORKLOADS[args.workload]
+
+    if args.impl == "reference":
+        run_reference(args, kw, global_batch, dtype_name, rank)
+    elif args.workload in STACKS:
+        run_stack(args, kw, global_batch, dtype_name, STACKS[args.workload], world, rank, local)
+    elif args.workload in PREFILLS:
+        run_prefill(args, kw, global_batch, dtype_name, PREFILLS[args.workload], world, rank, local)
+    else:
+        run_layer(args, kw, global_batch, dtype_name, world, rank, local)
 
 
 if __name__ == "__main__":

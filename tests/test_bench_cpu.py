@@ -37,3 +37,49 @@ def test_no_collective_inside_a_rank_dependent_branch():
             bad.extend(_calls(node.body))
             bad.extend(_calls(node.orelse))
     assert not bad, f"collectives reached by only some ranks: {bad}"
+
+
+def _json_lines(text):
+    import json
+    return [json.loads(ln) for ln in text.splitlines() if ln.startswith("{")]
+
+
+def test_global_batch_splits_evenly_over_ranks():
+    import sys
+
+    import pytest
+    sys.path.insert(0, ROOT)
+    import bench
+    assert [bench.shard_rows(256, n) for n in (1, 2, 4, 8)] == [256, 128, 64, 32]
+    with pytest.raises(SystemExit):
+        bench.shard_rows(256, 3)
+    assert bench.DEFAULT_WORKLOAD == "stack24_d2048_b256_bf16"
+    assert bench.WORKLOADS[bench.DEFAULT_WORKLOAD][1] == 256
+
+
+def test_reference_arm_times_the_reference_cpu_decode():
+    """--impl reference runs the reference's own PyTorch CPU decode (from the
+    staged copy) on the workload's global batch, without a GPU; under
+    torchrun only rank 0 prints."""
+    import subprocess
+    import sys
+
+    import pytest
+    from oracle.stage_reference import DEFAULT_OUT, verify
+    why = verify(DEFAULT_OUT)
+    if why:
+        pytest.skip(why)
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", PYTHONDONTWRITEBYTECODE="1")
+    args = ["bench.py", "--impl", "reference", "--workload", "mimo_r4_d256_b128", "--steps", "3", "--warmup", "1"]
+    r = subprocess.run([sys.executable, *args], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    (line,) = _json_lines(r.stdout)
+    assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] == "reference"
+    assert line["config"]["global_batch"] == 128 and line["dtype"] == "f32" and line["steps"] == 3
+    assert line["value"] > 0 and line["e2e"]["value"] == line["value"]
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29517", *args, "--gpus", "2"],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    (line,) = _json_lines(r.stdout)
+    assert line["n_gpus"] == 2 and line["config"]["global_batch"] == 128
