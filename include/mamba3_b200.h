@@ -170,11 +170,15 @@ int m3_linear_f32(const float *A, int64_t lda, const float *W, int64_t ldw, floa
  * m3_linear_f32:  C[m, n] = sum_k A[m, k] * W[n, k].  A: (M, K) bf16 row
  * stride lda, W: (N, K) bf16 row stride ldw, C: (M, N) row stride ldc in
  * c_dtype (M3_BF16, rounded to nearest, or M3_F32).  16-byte aligned bases,
- * K >= 64, K, lda, ldw multiples of 8.  When the call splits K, the partial
- * tiles go through `workspace` (16-byte aligned, at least
- * m3_linear_bf16_workspace_bytes(M, N, K) bytes, M3_ERR_SHAPE otherwise;
- * NULL / 0 when that is 0); calls sharing a workspace must not overlap on
- * the GPU.  M3_ERR_UNSUPPORTED when the driver offers no tensor-map encoder. */
+ * K >= 64, K, lda, ldw multiples of 8.  Pairs of SMs (tcgen05.mma
+ * .cta_group::2) share each batch tile.  When the call splits K, the pairs
+ * add their partial tiles into an fp32 accumulator in `workspace` (16-byte
+ * aligned, at least m3_linear_bf16_workspace_bytes(M, N, K) bytes,
+ * M3_ERR_SHAPE otherwise; NULL / 0 when that is 0), which must be ZEROED
+ * before its first use and is left at zero by every call (zero it again
+ * after a call that reported M3_DEVERR_TIMEOUT); calls sharing a workspace
+ * must not overlap on the GPU.  M3_ERR_UNSUPPORTED when the driver offers
+ * no tensor-map encoder. */
 int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
                    int32_t N, int32_t K, int32_t c_dtype, void *workspace, int64_t workspace_bytes,
                    m3_stream_t stream);

@@ -1,29 +1,9 @@
-// bf16 projection GEMM on the 5th-generation tensor cores (tcgen05).
-//
-// y[M, N] = x[M, K] . w[N, K]^T for the decode step's projections
-// (nn.Linear without bias, src/models/mamba3.py:115,158), where M is the
-// batch and N, K are layer widths.  The weight rows are the MMA's M
-// dimension (128 per CTA) and the batch rows its N dimension (up to 256 per
-// CTA), so a decode batch of <= 256 rows is one tile column:
-//
-//   * warp 0 / lane 0 streams k-tiles of 64 elements through an S-stage
-//     shared-memory ring with TMA (cp.async.bulk.tensor.2d, 128-byte swizzle):
-//     the weight tile (128 x 64) and the batch tile (NB x 64);
-//   * warp 1 / lane 0 issues four tcgen05.mma (kind::f16: bf16 operands,
-//     fp32 accumulation) per k-tile into one TMEM accumulator of 128 lanes x
-//     NB columns, and hands each stage back with tcgen05.commit;
-//   * the tile width (batch rows per CTA) and a K split are planned per call
-//     so that the CTAs fill the SMs; a split runs its CTAs as one thread-block
-//     cluster (up to 4): every CTA writes its fp32 partial tile to the
-//     caller's workspace, and after a cluster barrier CTA j sums slice j of the
-//     batch rows over the cluster's partials (from L2) and writes it.
-//     Distributed shared memory was tried for that exchange and measured at
-//     about 15 GB/s per CTA -- far slower than L2.
-//
-// All four warps drain TMEM (tcgen05.ld, warp w owns lanes 32w..32w+31).
-// Every mbarrier wait is bounded and records M3_DEVERR_TIMEOUT when it gives
-// up; the cluster barrier is reached on every path.  No load uses cluster
-// multicast.
+// bf16 projection GEMM on the 5th-generation tensor cores (tcgen05), for
+// the decode step's projections (nn.Linear without bias,
+// src/models/mamba3.py:115,158): y[M, N] = x[M, K] . w[N, K]^T, M the batch.
+// One kernel, gemm_pair_kernel: pairs of SMs (tcgen05.mma.cta_group::2),
+// TMA-fed shared-memory rings, fp32 accumulation in TMEM, an optional K
+// split over independent pairs.  Design notes above the kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -36,28 +16,7 @@ namespace m3 {
 
 namespace {
 
-constexpr int kTileN = 128;  // weight rows per CTA (MMA M)
-constexpr int kTileK = 64;   // k per stage: one 128-byte swizzle row of bf16
-constexpr int kThreads = 128;
-constexpr int kMaxSplit = 4;
-constexpr int kSmemBudget = 200 * 1024;
-constexpr int kMaxStages = 8;
-
-struct GemmArgs {
-  int M, N;
-  int nb;          // batch rows per tile (multiple of 16, <= 256)
-  int ktiles;      // k-tiles per split
-  int ktotal;      // k-tiles of K
-  int nsplit;      // CTAs per cluster along K
-  int nstage;      // ring depth
-  int stage_a;     // bytes of a weight tile
-  int stage_b;     // bytes of a batch tile
-  int tmem_cols;   // allocated accumulator columns
-  void *y;
-  int64_t ldy;
-  int y_bf16;
-  float *ws;       // split-K partial tiles (nsplit > 1)
-};
+constexpr int kTileK = 64;  // k per stage: one 128-byte swizzle row of bf16
 
 // UMMA shared-memory descriptor of a K-major operand in the 128-byte swizzle
 // layout TMA writes: rows of 128 bytes, 8-row groups 1024 bytes apart
@@ -67,26 +26,6 @@ struct GemmArgs {
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -106,213 +45,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const GemmArgs g) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char *smem =
-      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int S = g.nstage;
-  unsigned char *ringA = smem;
-  unsigned char *ringB = smem + (size_t)S * g.stage_a;
-  const int ring_bytes = S * (g.stage_a + g.stage_b);
-  const int part_bytes = g.nb * kTileN * 4;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (ring_bytes > part_bytes ? ring_bytes : part_bytes));
-  uint64_t *full = bars, *empty = bars + S, *accum = bars + 2 * S;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kTileN, m0 = blockIdx.y * g.nb;
-  const int split = blockIdx.z;  // rank in the cluster (cluster dims 1 x 1 x nsplit)
-  const int kt0 = split * g.ktiles;
-  const int nkt = max(0, min(g.ktiles, g.ktotal - kt0));
-
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                 "r"(g.tmem_cols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (tid == 32) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(smem_addr(&full[s]), 1);
-      mbar_init(smem_addr(&empty[s]), 1);
-    }
-    mbar_init(smem_addr(accum), 1);
-    mbar_init_fence();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  // the weights are constant: the first stages' weight tiles are requested
-  // before waiting for the preceding kernel, whose product the batch rows are
-  const int npre = min(S, nkt);
-  if (tid == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
-    for (int i = 0; i < npre; ++i) {
-      const uint32_t bar = smem_addr(&full[i]);
-      mbar_arrive_expect_tx(bar, (uint32_t)(g.stage_a + g.stage_b));
-      tma_load_2d(smem_addr(ringA + (size_t)i * g.stage_a), &tw, (kt0 + i) * kTileK, n0, bar);
-    }
-  }
-  pdl_wait();
-  pdl_trigger();
-
-  if (tid == 0) {
-    // producer: k-tile i into stage i % S, after the MMAs of k-tile i - S
-    // have released it
-    for (int i = 0; i < npre; ++i)
-      tma_load_2d(smem_addr(ringB + (size_t)i * g.stage_b), &tx, (kt0 + i) * kTileK, m0, smem_addr(&full[i]));
-    int s = npre % S;
-    uint32_t ph = npre == S ? 1u : 0u;
-    int issued = npre;
-    for (int i = npre; i < nkt; ++i) {
-      if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1u)) break;
-      const uint32_t bar = smem_addr(&full[s]);
-      mbar_arrive_expect_tx(bar, (uint32_t)(g.stage_a + g.stage_b));
-      const int kx = (kt0 + i) * kTileK;
-      tma_load_2d(smem_addr(ringA + (size_t)s * g.stage_a), &tw, kx, n0, bar);
-      tma_load_2d(smem_addr(ringB + (size_t)s * g.stage_b), &tx, kx, m0, bar);
-      issued = i + 1;
-      if (++s == S) {
-        s = 0;
-        ph ^= 1u;
-      }
-    }
-    // every copy this thread issued has landed before the CTA moves on
-    // (immediate on the normal path, where the MMAs consumed them)
-    for (int j = issued > S ? issued - S : 0; j < issued; ++j)
-      mbar_wait(smem_addr(&full[j % S]), (uint32_t)((j / S) & 1));  // full bound: a copy may still land
-  } else if (tid == 32) {
-    // MMA issuer: D[128 x nb] (+)= W_tile[128 x 64] . X_tile[nb x 64]^T
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(g.nb >> 3) << 17) |
-                           ((uint32_t)(kTileN >> 4) << 24);
-    int s = 0;
-    uint32_t ph = 0;
-    for (int i = 0; i < nkt; ++i) {
-      if (!mbar_wait(smem_addr(&full[s]), ph)) break;
-      tc_fence_after();
-      const uint32_t a0 = smem_addr(ringA + (size_t)s * g.stage_a);
-      const uint32_t b0 = smem_addr(ringB + (size_t)s * g.stage_b);
-#pragma unroll
-      for (int j = 0; j < kTileK / 16; ++j)
-        mma_bf16(tmem, sw128_desc(a0 + 32 * j), sw128_desc(b0 + 32 * j), idesc, (i | j) != 0 ? 1u : 0u);
-      mma_commit(smem_addr(&empty[s]));
-      if (++s == S) {
-        s = 0;
-        ph ^= 1u;
-      }
-    }
-    mma_commit(smem_addr(accum));  // arrives once every MMA issued above has completed
-  }
-  __syncwarp();
-
-  mbar_wait(smem_addr(accum), 0);
-  __syncwarp();
-  tc_fence_after();
-  const int nl = 32 * warp + lane;
-  const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-  // Drain the accumulator 64 columns (batch rows) at a time: up to four
-  // tcgen05.ld per wait; `put(m, value)` stores column m of this thread's row.
-  auto drain = [&](auto &&put) {
-    for (int c0 = 0; c0 < g.nb; c0 += 64) {  // nb is a multiple of 16
-      uint32_t v[4][16];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (c0 + 16 * q < g.nb) tmem_ld16(trow + (uint32_t)(c0 + 16 * q), v[q]);
-      tmem_wait();
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (c0 + 16 * q < g.nb)
-#pragma unroll
-          for (int j = 0; j < 16; ++j) put(c0 + 16 * q + j, nkt > 0 ? __uint_as_float(v[q][j]) : 0.f);
-    }
-  };
-  const int n = n0 + 4 * lane;
-  auto store_row = [&](int m, const float4 a4) {
-    const float o[4] = {a4.x, a4.y, a4.z, a4.w};
-    if (g.y_bf16) {
-      __nv_bfloat16 *yr = static_cast<__nv_bfloat16 *>(g.y) + (int64_t)m * g.ldy;
-      if (n + 3 < g.N && ((g.ldy | n) & 3) == 0) {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t *>(&lo);
-        pk.y = *reinterpret_cast<uint32_t *>(&hi);
-        *reinterpret_cast<uint2 *>(yr + n) = pk;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (n + e < g.N) yr[n + e] = __float2bfloat16_rn(o[e]);
-      }
-    } else {
-      float *yr = static_cast<float *>(g.y) + (int64_t)m * g.ldy;
-      if (n + 3 < g.N && ((g.ldy | n) & 3) == 0) {
-        *reinterpret_cast<float4 *>(yr + n) = a4;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (n + e < g.N) yr[n + e] = o[e];
-      }
-    }
-  };
-
-  if (g.nsplit > 1) {
-    // split-K: this CTA's fp32 partial tile -> workspace [m][n] (each warp
-    // store one 128-byte row segment), a cluster barrier, then CTA `split`
-    // sums batch rows [r0, r1) of the tile over the cluster's partials from L2
-    const size_t tile = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
-    float *tws = g.ws + tile * g.nsplit * g.nb * kTileN;
-    float *mine = tws + (size_t)split * g.nb * kTileN;
-    drain([&](int m, float v) { __stcg(mine + (size_t)m * kTileN + nl, v); });
-    tc_fence_before();
-    cluster_sync();  // release / acquire at cluster scope: every partial is visible
-    const int per = (g.nb + g.nsplit - 1) / g.nsplit;
-    const int r0 = split * per, r1 = min(g.nb, r0 + per);
-    constexpr int RU = 4;  // rows per warp and pass: RU x nsplit loads in flight
-    for (int base = r0; base < r1; base += 4 * RU) {
-      float4 acc[RU];
-#pragma unroll
-      for (int u = 0; u < RU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int q = 0; q < kMaxSplit; ++q) {
-        if (q < g.nsplit) {
-#pragma unroll
-          for (int u = 0; u < RU; ++u) {
-            const int mm = base + 4 * u + warp;
-            if (mm < r1) {
-              const float4 t = __ldcg(reinterpret_cast<const float4 *>(tws + ((size_t)q * g.nb + mm) * kTileN + 4 * lane));
-              acc[u].x += t.x; acc[u].y += t.y; acc[u].z += t.z; acc[u].w += t.w;
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < RU; ++u) {
-        const int mm = base + 4 * u + warp;
-        if (mm < r1 && m0 + mm < g.M) store_row(m0 + mm, acc[u]);
-      }
-    }
-  } else {
-    // whole K here: accumulator -> shared memory part[m][n] (the ring it
-    // overwrites was last written by TMA and read by the finished MMAs),
-    // then coalesced row stores
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    float *part = reinterpret_cast<float *>(smem);
-    drain([&](int m, float v) { part[m * kTileN + nl] = v; });
-    tc_fence_before();
-    __syncthreads();
-    for (int mm = warp; mm < g.nb && m0 + mm < g.M; mm += 4)
-      store_row(m0 + mm, *reinterpret_cast<const float4 *>(part + mm * kTileN + 4 * lane));
-  }
-
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(g.tmem_cols) : "memory");
-}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -343,39 +75,489 @@ bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int
 
 int sm_count() { return sm_count_current(); }
 
-// Tile width (batch rows per CTA) and K split of one call: the cheapest by
-// a simple model -- each k-tile moves its weight and batch tiles at about
-// 100 GB/s per SM (the operands mostly come from L2), CTAs beyond one per SM
-// run in further waves, and a split adds the partial tiles' write and read.
-struct GemmPlan {
-  int nb, ntiles, mchunks, ktotal, ktiles, nsplit;
+// ---------------------------------------------------------------------------
+// Paired-SM projection GEMM (tcgen05 .cta_group::2).
+//
+// y[M, N] = x[M, K] . w[N, K]^T for the decode step's projections, with the
+// batch rows as the MMA's M and the weight rows as its N: a pair of SMs (a
+// two-CTA cluster) owns 256 batch rows (128 per CTA, on its TMEM lanes) and
+// nt weight rows (nt / 2 loaded by each CTA), and the even CTA issues one
+// tcgen05.mma.cta_group::2 per 16 k that reads both CTAs' shared memory.
+// Each SM therefore streams half of the pair's weight tile; the batch rows
+// (at decode sizes a few hundred KB, resident in L2) are re-read per tile.
+// A thread owns one batch row of the accumulator, so the epilogue writes
+// contiguous 32-byte row segments straight from TMEM.  Batch rows past M are
+// zero-filled by TMA and cost no memory traffic.
+//
+// K may be split over `nsplit` pairs for shapes with few weight tiles: every
+// pair but the last to finish writes its fp32 partial tile to the caller's
+// workspace and takes a ticket; the last sums all partials in split order
+// (its own from TMEM), so the result does not depend on arrival order, and
+// resets the ticket.  Nobody waits on anybody; no co-scheduling is assumed.
+//
+//   warp 0 / lane 0   TMA producer (both CTAs): its 128 batch rows and its
+//                     nt / 2 weight rows per 64-k tile into an S-stage ring;
+//                     both CTAs' copies complete on the even CTA's barrier
+//   warp 1            TMEM allocation for the pair (both CTAs); lane 0 of
+//                     the even CTA issues the MMAs and releases each stage
+//                     in BOTH CTAs with one multicast tcgen05.commit
+//   warps 2-5         epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31
+//
+// No copy uses cluster multicast.  Every mbarrier wait is bounded; on a
+// timeout the thread records M3_DEVERR_TIMEOUT and carries on, so both CTAs
+// reach every cluster barrier.
+// ---------------------------------------------------------------------------
+
+constexpr int kPairBatch = 128;   // batch rows per CTA (MMA M = 256 per pair)
+constexpr int kPairThreads = 192;
+constexpr int kPairMaxSplit = 16;
+constexpr int kPairSmem = 200 * 1024;
+// Split-K tickets live at the start of the workspace, before any partial
+// tile, at the same place for every shape (a workspace serves many shapes).
+constexpr int kPairMaxTickets = 8192;
+constexpr int64_t kPairTicketBytes = kPairMaxTickets * 4;
+constexpr int kPairMaxStages = 8;
+
+struct PairArgs {
+  int M, N;
+  int nt;          // weight rows per pair tile (multiple of 32, <= 256)
+  int ntn;         // pair tiles along N
+  int ktiles;      // k-tiles per split
+  int ktotal;      // k-tiles of K
+  int nsplit;      // pairs along K
+  int nstage;      // ring depth
+  int stage_b;     // bytes of this CTA's half of a weight tile (nt / 2 rows)
+  int nacc;        // accumulators the k-tiles alternate between (1 or 2)
+  int tmem_cols;   // accumulator columns allocated per CTA (>= nacc * nt)
+  void *y;
+  int64_t ldy;
+  int y_bf16;
+  float *part;        // split K: fp32 partials, [tile][half][split][128][nt]
+  unsigned *tickets;  // split K: arrivals per [tile][half], zero between calls
 };
 
-GemmPlan plan_gemm(int M, int N, int K) {
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of `addr` (a shared::cta address of this CTA's
+// layout) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+
+// 2-D TMA load into this CTA's shared memory whose completion is counted on
+// the pair's even CTA's barrier `bar` (a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive once on barrier `bar` (same shared::cta offset) of every CTA in
+// `cta_mask` when all MMAs this thread issued have completed.
+__device__ __forceinline__ void mma_commit_to_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster"
+      ".multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Named barrier of the four epilogue warps.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 16 consecutive outputs v of row m from column n: 32-byte bf16 / 4 x
+// 16-byte fp32 stores where the row allows, else element by element.
+__device__ __forceinline__ void store16(const PairArgs &g, int m, int n, const float (&v)[16]) {
+  if (m >= g.M || n >= g.N) return;
+  const bool vec = n + 15 < g.N && ((g.ldy | n) & 7) == 0;
+  if (g.y_bf16) {
+    __nv_bfloat16 *yr = static_cast<__nv_bfloat16 *>(g.y) + (int64_t)m * g.ldy + n;
+    if (vec) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        pk[i] = *reinterpret_cast<uint32_t *>(&b);
+      }
+      reinterpret_cast<uint4 *>(yr)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      reinterpret_cast<uint4 *>(yr)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n + i < g.N) yr[i] = __float2bfloat16_rn(v[i]);
+    }
+  } else {
+    float *yr = static_cast<float *>(g.y) + (int64_t)m * g.ldy + n;
+    if (vec) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4 *>(yr)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n + i < g.N) yr[i] = v[i];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kPairThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const PairArgs g) {
+  extern __shared__ unsigned char smem_raw[];  // no static shared memory: the opt-in is the whole 227 KB
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  constexpr int kStageA = kPairBatch * kTileK * 2;  // this CTA's batch rows x 64 k
+  const int S = g.nstage;
+  unsigned char *ringA = smem;
+  unsigned char *ringB = smem + (size_t)S * kStageA;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * (kStageA + g.stage_b));
+  uint64_t *full = bars, *empty = bars + S, *accum = bars + 2 * S, *redbar = bars + 2 * S + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
+  int *s_last = reinterpret_cast<int *>(tmem_slot + 1);  // shares the slot's 8 bytes
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();  // the cluster is the pair: rank 0 (even CTA) or 1
+  const int half = (int)(rank & 1u);
+  const bool leader = half == 0;
+  const int pair = (int)blockIdx.x >> 1;
+  const int kq = pair % g.nsplit, tile = pair / g.nsplit;
+  const int tn = tile % g.ntn, tm = tile / g.ntn;
+  const int n0 = tn * g.nt;                             // the pair's weight rows (output columns)
+  const int nw = n0 + half * (g.nt >> 1);               // this CTA's half of them
+  const int mb = tm * 2 * kPairBatch + half * kPairBatch;  // this CTA's batch rows
+  const int kt0 = kq * g.ktiles;
+  const int nkt = max(0, min(g.ktiles, g.ktotal - kt0));
+  // Every pair reads the same batch rows; walking K in the same order, all
+  // pairs would ask L2 for the same lines at once.  Each pair tile starts
+  // its walk at its own k-tile (both CTAs of the pair alike), which spreads
+  // the requests over the batch tile.
+  const int krot = nkt > 0 ? (int)(((unsigned)tile * 7u) % (unsigned)nkt) : 0;
+  auto kx_of = [&](int i) { int k = i + krot; return (kt0 + (k >= nkt ? k - nkt : k)) * kTileK; };
+  const uint16_t pair_mask = 3;
+  const uint32_t stage_tx = 2u * (uint32_t)(kStageA + g.stage_b);  // both CTAs' copies of a stage
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    mbar_init(smem_addr(accum), 1);
+    mbar_init(smem_addr(redbar), 1);
+    mbar_init_fence();
+  }
+  if (warp == 1) {  // the pair's accumulator: the same columns in both CTAs
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(g.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised and their TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t full_lead = peer_addr(smem_addr(&full[0]), 0);  // the even CTA's `full` barriers
+
+  // the weights are constant: the first stages' weight tiles are requested
+  // before waiting for the preceding kernel, whose product the batch rows are
+  const int npre = min(S, nkt);
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+    for (int i = 0; i < npre; ++i) {
+      if (leader) mbar_arrive_expect_tx(smem_addr(&full[i]), stage_tx);
+      tma_load_2d_pair(smem_addr(ringB + (size_t)i * g.stage_b), &tw, kx_of(i), nw, full_lead + 8u * i);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: k-tile i into stage i % S once the MMAs of k-tile i - S
+      // (in both CTAs) have released it
+      for (int i = 0; i < npre; ++i)
+        tma_load_2d_pair(smem_addr(ringA + (size_t)i * kStageA), &tx, kx_of(i), mb, full_lead + 8u * i);
+      int s = npre % S;
+      uint32_t ph = npre == S ? 1u : 0u;
+      int issued = npre;
+      for (int i = npre; i < nkt; ++i) {
+        if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1u)) break;
+        if (leader) mbar_arrive_expect_tx(smem_addr(&full[s]), stage_tx);
+        const int kx = kx_of(i);
+        tma_load_2d_pair(smem_addr(ringB + (size_t)s * g.stage_b), &tw, kx, nw, full_lead + 8u * s);
+        tma_load_2d_pair(smem_addr(ringA + (size_t)s * kStageA), &tx, kx, mb, full_lead + 8u * s);
+        issued = i + 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      // the even CTA waits until the last stages' copies (both CTAs') have
+      // landed before the pair moves on (immediate on the normal path, where
+      // the MMAs consumed them)
+      if (leader)
+        for (int j = issued > S ? issued - S : 0; j < issued; ++j)
+          mbar_wait(smem_addr(&full[j % S]), (uint32_t)((j / S) & 1));
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      // D[256 x nt] (+)= X_pair[256 x 64] . W_pair[nt x 64]^T per k-tile
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(g.nt >> 3) << 17) |
+                             ((uint32_t)((2 * kPairBatch) >> 4) << 24);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int i = 0; i < nkt; ++i) {
+        if (!mbar_wait(smem_addr(&full[s]), ph)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(ringA + (size_t)s * kStageA);
+        const uint32_t b0 = smem_addr(ringB + (size_t)s * g.stage_b);
+        // with two accumulators, k-tile i adds into accumulator i % 2: two
+        // independent chains of MMAs
+        const int ai = g.nacc == 2 ? (i & 1) : 0;
+        const uint32_t d = tmem + (uint32_t)(ai * g.nt);
+#pragma unroll
+        for (int j = 0; j < kTileK / 16; ++j)
+          mma_bf16_pair(d, sw128_desc(a0 + 32 * j), sw128_desc(b0 + 32 * j), idesc, (i >> (g.nacc - 1) | j) != 0 ? 1u : 0u);
+        mma_commit_to_pair(smem_addr(&empty[s]), pair_mask);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      mma_commit_to_pair(smem_addr(accum), pair_mask);  // once every MMA above has completed
+    }
+    __syncwarp();
+  } else {
+    // epilogue: TMEM lane q is batch row mb + q; its nt columns are the
+    // output columns n0 .. n0 + nt - 1 of that row
+    mbar_wait(smem_addr(accum), 0);
+    __syncwarp();
+    tc_fence_after();
+    const int q = 32 * (warp & 3) + lane, m = mb + q;
+    const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    // 32 accumulator columns from c0 (both accumulators added), zero when
+    // this split had no k-tile (a second accumulator gets one only when nkt >= 2)
+    auto load32 = [&](int c0, float (&f)[32]) {
+      uint32_t v[2][16], w[2][16];
+      tmem_ld16(trow + (uint32_t)c0, v[0]);
+      tmem_ld16(trow + (uint32_t)(c0 + 16), v[1]);
+      if (g.nacc == 2) {
+        tmem_ld16(trow + (uint32_t)(g.nt + c0), w[0]);
+        tmem_ld16(trow + (uint32_t)(g.nt + c0 + 16), w[1]);
+      }
+      tmem_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float a = nkt > 0 ? __uint_as_float(v[j >> 4][j & 15]) : 0.f;
+        if (g.nacc == 2 && nkt > 1) a += __uint_as_float(w[j >> 4][j & 15]);
+        f[j] = a;
+      }
+    };
+    if (g.nsplit == 1) {
+      for (int c0 = 0; c0 < g.nt; c0 += 32) {
+        float f[32];
+        load32(c0, f);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = f[16 * h + j];
+          store16(g, m, n0 + c0 + 16 * h, o);
+        }
+      }
+    } else {
+      // split K: this pair's partial tile -> its slot, stored column-major
+      // ([nt][128]: a warp writes 128 contiguous bytes per column); the
+      // last of the nsplit pairs to take a ticket sums the slots in split
+      // order (its own from TMEM) and writes the rows
+      const size_t slot_elems = (size_t)kPairBatch * g.nt;
+      float *slot0 = g.part + ((size_t)tile * 2 + half) * g.nsplit * slot_elems;
+      float *mine = slot0 + (size_t)kq * slot_elems;
+      for (int c0 = 0; c0 < g.nt; c0 += 32) {
+        float f[32];
+        load32(c0, f);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) __stcg(mine + (size_t)(c0 + j) * kPairBatch + q, f[j]);
+      }
+      __threadfence();
+      epi_sync();
+      if (warp == 2 && lane == 0) *s_last = atomicAdd(&g.tickets[tile * 2 + half], 1u) == (unsigned)(g.nsplit - 1);
+      epi_sync();
+      if (*s_last) {
+        __threadfence();
+        // the other pairs' slots, into the idle ring when they fit (one
+        // bulk copy each), else read from L2 column by column
+        const uint32_t slot_bytes = (uint32_t)(slot_elems * 4);
+        const bool staged = (int64_t)(g.nsplit - 1) * slot_bytes <= (int64_t)S * (kStageA + g.stage_b);
+        float *ring = reinterpret_cast<float *>(smem);
+        auto other = [&](int p) -> int { return p < kq ? p : p - 1; };  // staging index of slot p
+        if (staged) {
+          if (warp == 2 && lane == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // the slots were written by generic stores
+            const uint32_t rb = smem_addr(redbar);
+            mbar_arrive_expect_tx(rb, (uint32_t)(g.nsplit - 1) * slot_bytes);
+            for (int p = 0; p < g.nsplit; ++p) {
+              if (p == kq) continue;
+              const char *src = reinterpret_cast<const char *>(slot0 + (size_t)p * slot_elems);
+              const uint32_t dst = smem_addr(ring + (size_t)other(p) * slot_elems);
+              for (uint32_t off = 0; off < slot_bytes; off += 32768u) {
+                const uint32_t len = slot_bytes - off < 32768u ? slot_bytes - off : 32768u;
+                bulk_g2s(dst + off, src + off, len, rb);
+              }
+            }
+          }
+          mbar_wait(smem_addr(redbar), 0);
+        }
+        for (int c0 = 0; c0 < g.nt; c0 += 32) {
+          float own[32], f[32];
+          load32(c0, own);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = 0.f;
+          for (int p = 0; p < g.nsplit; ++p) {
+            if (p == kq) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] += own[j];
+            } else if (staged) {
+              const float *src = ring + (size_t)other(p) * slot_elems + (size_t)c0 * kPairBatch + q;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] += src[(size_t)j * kPairBatch];
+            } else {
+              const float *src = slot0 + (size_t)p * slot_elems + (size_t)c0 * kPairBatch + q;
+              float t[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) t[j] = __ldcg(src + (size_t)j * kPairBatch);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] += t[j];
+            }
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = f[16 * h + j];
+            store16(g, m, n0 + c0 + 16 * h, o);
+          }
+        }
+        if (warp == 2 && lane == 0) g.tickets[tile * 2 + half] = 0u;
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs are done with their accumulators
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(g.tmem_cols) : "memory");
+  }
+}
+
+// Pair tiles and K split of one call, the cheapest by a model measured on
+// B200: a pair spends about 0.33 us per 64-k tile whatever the tile width
+// (at nt = 256 that is the tensor cores' full rate), pairs beyond one per SM
+// pair run in further waves, and a split adds about a microsecond plus the
+// last pair's copy of the other partial tiles (~200 GB/s).
+struct PairPlan {
+  int nt, ntn, ntm, ktotal, ktiles, nsplit, nacc;
+};
+
+PairPlan plan_pair(int M, int N, int K) {
   const int sms = sm_count();
-  const int ntiles = (N + kTileN - 1) / kTileN, ktotal = (K + kTileK - 1) / kTileK;
-  const int mr = (M + 15) / 16 * 16;
-  GemmPlan best = {};
+  const int ntm = (M + 2 * kPairBatch - 1) / (2 * kPairBatch);
+  const int ktotal = (K + kTileK - 1) / kTileK;
+  PairPlan best = {};
   double best_cost = 1e30;
-  for (int nb : {256, 128, 64, 32, 16}) {
-    if (nb > mr && nb != 16 && (nb >> 1) >= mr) continue;  // skip widths twice the batch or more
-    const int b = nb < mr ? nb : mr;
-    const int mchunks = (M + b - 1) / b, tiles = ntiles * mchunks;
-    int nsplit = tiles >= sms ? 1 : sms / tiles;
-    nsplit = nsplit < 1 ? 1 : nsplit > kMaxSplit ? kMaxSplit : nsplit;
-    if (nsplit > ktotal) nsplit = ktotal;
-    const int ktiles = (ktotal + nsplit - 1) / nsplit;
-    nsplit = (ktotal + ktiles - 1) / ktiles;  // every split gets at least one k-tile
-    const int waves = (tiles * nsplit + sms - 1) / sms;
-    const double us_per_ktile = (kTileN * kTileK * 2.0 + b * kTileK * 2.0) / 1.0e5;
-    double cost = waves * ktiles * us_per_ktile + b * kTileN * 4.0 / 1.0e5;
-    if (nsplit > 1) cost += 2.0 * b * kTileN * 4.0 / 1.0e5 + 0.7;
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = {b, ntiles, mchunks, ktotal, ktiles, nsplit};
+  for (int nt : {256, 128, 64, 32}) {
+    const int ntn = (N + nt - 1) / nt;
+    int nsmax = sms / (2 * ntn * ntm);
+    nsmax = nsmax < 1 ? 1 : nsmax > kPairMaxSplit ? kPairMaxSplit : nsmax;
+    for (int ns0 = 1; ns0 <= nsmax && ns0 <= ktotal; ns0 *= 2) {
+      const int ktiles = (ktotal + ns0 - 1) / ns0;
+      const int ns = (ktotal + ktiles - 1) / ktiles;
+      const int waves = (2 * ntn * ntm * ns + sms - 1) / sms;
+      double cost = waves * ktiles * 0.33;  // us
+      if (ns > 1) cost += waves * (1.0 + (ns - 1) * (double)kPairBatch * nt * 4.0 / 2.0e5);
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = {nt, ntn, ntm, ktotal, ktiles, ns, 1};
+      }
     }
   }
   return best;
+}
+
+// Split-K workspace: the tickets (fixed region), then the partial tiles.
+int64_t pair_workspace_bytes(const PairPlan &p) {
+  return p.nsplit > 1 ? kPairTicketBytes + (int64_t)p.ntn * p.ntm * 2 * p.nsplit * kPairBatch * p.nt * 4 : 0;
+}
+
+cudaError_t launch_gemm_pair(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
+                             int N, int K, bool y_bf16, void *workspace, const PairPlan &pl, cudaStream_t stream) {
+  PairArgs g = {};
+  g.M = M;
+  g.N = N;
+  g.nt = pl.nt;
+  g.ntn = pl.ntn;
+  g.ktotal = pl.ktotal;
+  g.ktiles = pl.ktiles;
+  g.nsplit = pl.nsplit;
+  if (g.nt % 32 != 0 || g.nt > 256 || g.nsplit < 1 || g.nsplit > kPairMaxSplit) return cudaErrorInvalidValue;
+  if (g.nsplit > 1) {
+    if (workspace == nullptr || pl.ntn * pl.ntm * 2 > kPairMaxTickets) return cudaErrorInvalidValue;
+    g.tickets = static_cast<unsigned *>(workspace);
+    g.part = reinterpret_cast<float *>(static_cast<char *>(workspace) + kPairTicketBytes);
+  }
+  g.nacc = pl.nacc == 2 && 2 * pl.nt <= 512 ? 2 : 1;
+  g.stage_b = (g.nt / 2) * kTileK * 2;
+  const int stage = kPairBatch * kTileK * 2 + g.stage_b;
+  int S = kPairSmem / stage;
+  S = S > kPairMaxStages ? kPairMaxStages : S;
+  if (S > g.ktiles) S = g.ktiles < 2 ? 2 : g.ktiles;
+  g.nstage = S;
+  g.tmem_cols = 32;
+  while (g.tmem_cols < g.nacc * g.nt) g.tmem_cols <<= 1;
+  g.y = y;
+  g.ldy = ldy;
+  g.y_bf16 = y_bf16 ? 1 : 0;
+  const int smem = 1024 + S * stage + (2 * S + 3) * 8;
+
+  CUtensorMap tw, tx;
+  if (!make_map(&tw, w, N, K, ldw, g.nt / 2) || !make_map(&tx, x, M, K, ldx, kPairBatch))
+    return cudaErrorInvalidValue;
+
+  static LaunchCache cache;
+  if (cudaError_t e = ensure_smem_optin(cache, gemm_pair_kernel, 227 * 1024); e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * g.nsplit * pl.ntn * pl.ntm));
+  cfg.blockDim = dim3(kPairThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;
+  attrs[1].val.clusterDim.x = 2;
+  attrs[1].val.clusterDim.y = 1;
+  attrs[1].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, tw, tx, g);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -389,64 +571,12 @@ bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw,
 
 int64_t gemm_bf16_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K < kTileK) return 0;
-  const GemmPlan pl = plan_gemm(M, N, K);
-  if (pl.nsplit <= 1) return 0;
-  return (int64_t)pl.ntiles * pl.mchunks * pl.nsplit * pl.nb * kTileN * 4;
+  return pair_workspace_bytes(plan_pair(M, N, K));
 }
 
 cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
                              int N, int K, bool y_bf16, float *workspace, cudaStream_t stream) {
-  const GemmPlan pl = plan_gemm(M, N, K);
-  GemmArgs g = {};
-  g.M = M;
-  g.N = N;
-  g.nb = pl.nb;
-  g.ktotal = pl.ktotal;
-  g.ktiles = pl.ktiles;
-  g.nsplit = pl.nsplit;
-  if (g.nsplit > 1 && workspace == nullptr) return cudaErrorInvalidValue;
-  g.ws = workspace;
-  g.stage_a = kTileN * kTileK * 2;
-  g.stage_b = g.nb * kTileK * 2;
-  int S = kSmemBudget / (g.stage_a + g.stage_b);
-  S = S > kMaxStages ? kMaxStages : S;
-  if (S > g.ktiles) S = g.ktiles < 2 ? 2 : g.ktiles;
-  g.nstage = S;
-  g.tmem_cols = 32;
-  while (g.tmem_cols < g.nb) g.tmem_cols <<= 1;
-  g.y = y;
-  g.ldy = ldy;
-  g.y_bf16 = y_bf16 ? 1 : 0;
-  const int ring = S * (g.stage_a + g.stage_b), part = g.nb * kTileN * 4;
-  const int smem = 1024 + (ring > part ? ring : part) + (2 * S + 2) * 8;
-
-  CUtensorMap tw, tx;
-  if (!make_map(&tw, w, N, K, ldw, kTileN) || !make_map(&tx, x, M, K, ldx, g.nb)) return cudaErrorInvalidValue;
-
-  static LaunchCache cache;
-  if (cudaError_t e = ensure_smem_optin(cache, gemm_bf16_kernel, 227 * 1024); e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)pl.ntiles, (unsigned)pl.mchunks, (unsigned)g.nsplit);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attrs[2];
-  int na = 0;
-  attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[na].val.programmaticStreamSerializationAllowed = 1;
-  ++na;
-  if (g.nsplit > 1) {
-    attrs[na].id = cudaLaunchAttributeClusterDimension;
-    attrs[na].val.clusterDim.x = 1;
-    attrs[na].val.clusterDim.y = 1;
-    attrs[na].val.clusterDim.z = (unsigned)g.nsplit;
-    ++na;
-  }
-  cfg.attrs = attrs;
-  cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, tw, tx, g);
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
+  return launch_gemm_pair(x, ldx, w, ldw, y, ldy, M, N, K, y_bf16, workspace, plan_pair(M, N, K), stream);
 }
 
 int gemm_device_error(bool reset) { return device_error_of_this_unit(reset); }
