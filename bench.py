@@ -443,6 +443,14 @@ def fused_kernel_roofline(h: Harness, kw: dict, batch: int, dtype_name: str, n: 
             "frac": round(achieved / peak, 4), "bytes_per_launch": nbytes, "mean_launch_ms": round(mean, 5)}
 
 
+# the stack's projections alone: 24 layers of in_proj (9440 x 2048) and
+# out_proj (2048 x 4096), bf16, batch 256, in one CUDA graph, timed for the
+# library's tcgen05 GEMM (m3_linear_bf16) and for cuBLAS
+PROJECTIONS = {"proj24_d2048_b256_bf16": 24}
+WORKLOADS["proj24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 256,
+                                       "bf16")
+
+
 # fused-kernel rooflines added to the default run at N=1: the wide SISO layer
 # at its largest batch and the throughput sweep's layer at every rank
 EXTRA_ROOFLINES = ["siso_d512_b512_bf16", "mimo_r1_d1024_b4096", "mimo_r2_d1024_b4096", "mimo_r4_d1024_b4096",
@@ -600,6 +608,72 @@ def run_stack(args, kw, global_batch, dtype_name, layers, world, rank, local):
         }
         print(json.dumps(line), flush=True)
     dec._graph = None
+
+
+def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, local):
+    """The stack's projection GEMMs alone: per layer in_proj (d_in_proj x
+    d_model) and out_proj (d_model x d_inner) with their own bf16 weights,
+    all layers in one CUDA graph, replayed without an L2 flush (the 1.3 GB
+    of weights stream from HBM anyway); timed for the library's tcgen05 GEMM
+    (m3_linear_bf16) and for cuBLAS.  `value` is the library GEMM's rate in
+    tokens/s (batch x steps / time); the per-layer times and the FLOP rates
+    of both are beside it."""
+    import torch.nn.functional as F
+
+    from src.kernels.linear import linear_bf16
+    from src.models.mamba3 import Mamba3
+
+    h = Harness(world, rank, local)
+    dev = h.dev
+    batch = shard_rows(global_batch, world)
+    m = Mamba3(**kw, device="meta")
+    n_in, k_in, n_out, k_out = m.d_in_proj, m.d_model, m.d_model, m.d_inner
+    torch.manual_seed(0)
+    w_in = [(torch.randn(n_in, k_in, device=dev) * 0.02).bfloat16() for _ in range(layers)]
+    w_out = [(torch.randn(n_out, k_out, device=dev) * 0.02).bfloat16() for _ in range(layers)]
+    x = torch.randn(batch, k_in, device=dev).bfloat16()
+    y = torch.randn(batch, k_out, device=dev).bfloat16()
+    ref = (x.double() @ w_in[0].double().T)
+    err = float((linear_bf16(x, w_in[0], torch.float32).double() - ref).abs().max())
+
+    def chain(lin):
+        def f():
+            for l in range(layers):
+                lin(x, w_in[l])
+                lin(y, w_out[l])
+        return f
+
+    K, W = args.steps, args.warmup
+    results = {}
+    h.clocks_start()
+    h.barrier()
+    h.clocks_mark()
+    for name, lin in (("m3_linear_bf16", lambda a, b: linear_bf16(a, b)), ("cublas", F.linear)):
+        g = h.graphed(chain(lin), warm=max(W, 1))
+        ms = h.timed_loop(lambda i: g.replay(), K)
+        del g
+        results[name] = h.max_over_ranks(float(np.median(ms)))
+    h.barrier()
+    h.clocks_mark()
+    clocks = h.clocks_stop()
+    h.close()
+    if rank == 0:
+        flop = 2.0 * batch * layers * (n_in * k_in + n_out * k_out)
+        per = {k: round(v / layers * 1000.0, 2) for k, v in results.items()}
+        line = {
+            "metric": "projection tokens/s", "value": round(global_batch / (results["m3_linear_bf16"] * 1e-3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(results["m3_linear_bf16"], 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**config_dict(args.workload, kw, global_batch, world, dtype_name), "layers": layers,
+                       "step": "24 x (in_proj, out_proj) GEMMs in one CUDA graph, no L2 flush (weights > L2)"},
+            "us_per_layer": per,
+            "tflops": {k: round(flop / (v * 1e-3) / 1e12, 1) for k, v in results.items()},
+            "max_abs_err_vs_float64": err,
+            "gpu_launches": K * 2 * layers,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
 
 
 def run_prefill(args, kw, global_batch, dtype_name, length, world, rank, local):
@@ -869,6 +943,8 @@ def main():
         run_stack(args, kw, global_batch, dtype_name, STACKS[args.workload], world, rank, local)
     elif args.workload in PREFILLS:
         run_prefill(args, kw, global_batch, dtype_name, PREFILLS[args.workload], world, rank, local)
+    elif args.workload in PROJECTIONS:
+        run_projections(args, kw, global_batch, dtype_name, PROJECTIONS[args.workload], world, rank, local)
     else:
         run_layer(args, kw, global_batch, dtype_name, world, rank, local)
 
