@@ -227,16 +227,18 @@ def shard_rows(global_batch: int, world: int) -> int:
     return global_batch // world
 
 
-def reference_cpu_rate(kw, batch, dtype_name, layers=1, steps=0, budget_s=10.0, warmup=1):
+def reference_cpu_rate(kw, batch, dtype_name, layers=1, steps=0, budget_s=10.0, warmup=1, ssm=False):
     """The reference's own PyTorch CPU decode of `batch` sequences through
-    `layers` blocks, timed on the host cores in its own interpreter
-    (oracle/reference_cpu.py, no GPU visible).  Returns (result dict, None)
-    or (None, why it is unavailable)."""
+    `layers` blocks (with `ssm`: its state-update-only MIMO decode), timed on
+    the host cores in its own interpreter (oracle/reference_cpu.py, no GPU
+    visible).  Returns (result dict, None) or (None, why it is unavailable)."""
     cmd = [sys.executable, os.path.join(ROOT, "oracle", "reference_cpu.py"), "--layer", json.dumps(kw),
            "--dtype", dtype_name, "--batch", str(batch), "--layers", str(layers), "--warmup", str(warmup),
            "--budget", str(budget_s)]
     if steps:
         cmd += ["--steps", str(steps)]
+    if ssm:
+        cmd += ["--ssm"]
     env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", CUDA_VISIBLE_DEVICES="")
     try:
         r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=1800)
@@ -292,6 +294,25 @@ def run_reference(args, kw, global_batch, dtype_name, rank):
     global batch on rank 0's host cores (stacks: through all their blocks),
     each timed step one decode step; bounded to about a minute of steps."""
     if rank != 0:
+        return
+    if args.workload in SSM_WORKLOADS:
+        d, why = reference_cpu_rate(kw, global_batch, dtype_name, 1, args.steps, 60.0, min(args.warmup, 3), ssm=True)
+        if d is None:
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+            return
+        cpu = {"value": round(d["tokens_per_s"], 1), "unit": "sequences/s", "cores": d["threads"],
+               "kind": "reference",
+               "sample": f"{d['steps']} calls of the reference's mamba3_mimo_decode_ref on {global_batch} "
+                         f"sequences, torch CPU with {d['threads']} threads, p50 {d['p50_ms']:.2f} ms"}
+        line = {"metric": "state-update sequences/s", "value": cpu["value"], "unit": "sequences/s",
+                "impl": "reference", "n_gpus": args.gpus, "steps": d["steps"], "warmup": args.warmup,
+                "ms_per_step": round(d["ms_per_step"], 4), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": config_dict(args.workload, kw, global_batch, 1, dtype_name, reference=True),
+                "cpu_baseline": cpu,
+                "e2e": {"value": cpu["value"], "unit": "sequences/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     layers = STACKS.get(args.workload, 1)
     cpu, ms, n = cpu_baseline(kw, global_batch, dtype_name, layers, budget_s=60.0, steps=args.steps,
@@ -676,6 +697,90 @@ def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, loc
         print(json.dumps(line), flush=True)
 
 
+# the kernel-level state-update entry point alone (the reference's
+# mamba3_mimo_decode_triton, src/kernels/mimo_decode.py:394-457) on the
+# throughput sweep's layer shape, and a d_state-32 layer whose fused step
+# runs the row kernel (the streamed kernel takes d_state >= 36)
+SSM_WORKLOADS = {"ssm_mimo_r4_d1024_b4096"}
+WORKLOADS["ssm_mimo_r4_d1024_b4096"] = (dict(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=4),
+                                        4096, "f32")
+WORKLOADS["mimo_r4_d1024_n32_b4096"] = (dict(d_model=1024, d_state=32, headdim=64, is_mimo=True, mimo_rank=4),
+                                        4096, "f32")
+
+
+def ssm_bytes_per_launch(m, batch: int) -> int:
+    """Algorithmic HBM bytes of one state-update-only MIMO launch (fp32
+    inputs): x (read), the B and C projections (read), the three head
+    scalars (read), ssm_state and bx_prev (read + write), y (write) and the
+    per-head parameters (D, mimo_x, mimo_o; read once)."""
+    H, P, D, R = m.nheads, m.headdim, m.d_state, m.mimo_rank
+    return 4 * (2 * batch * H * P + 2 * batch * R * H * D + 3 * batch * H + 4 * batch * H * D + H + 2 * H * R * P)
+
+
+def run_ssm(args, kw, global_batch, dtype_name, world, rank, local):
+    """The kernel-level MIMO state update (mamba3_mimo_decode_triton) on
+    precomputed, already rotated B / C projections, each rank on its share
+    of the batch: one launch per step, replayed from a one-node graph with
+    an L2 flush before every step.  `value` = sequences updated per second;
+    `roofline` is the launch's algorithmic bytes over its mean time."""
+    from src.kernels.mimo_decode import mamba3_mimo_decode_triton
+    from src.models.mamba3 import Mamba3
+
+    h = Harness(world, rank, local)
+    dev = h.dev
+    batch = shard_rows(global_batch, world)
+    m = Mamba3(**kw, device="meta")
+    H, P, D, R = m.nheads, m.headdim, m.d_state, m.mimo_rank
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(*shape, device=dev, generator=gen) * scale
+
+    x = rnd(batch, H, P)
+    Bp, Cp = rnd(batch, R, H, D), rnd(batch, R, H, D)
+    DT = torch.rand(batch, H, device=dev, generator=gen) * 0.1 + 1e-3
+    ADT = DT * 1e-4
+    trap = torch.rand(batch, H, device=dev, generator=gen)
+    Dsk = torch.ones(H, device=dev)
+    mx, mo = rnd(H, R, P, scale=0.1), rnd(H, R, P, scale=0.1)
+    hs, bx = rnd(batch, H, D, scale=0.5), rnd(batch, H, D, scale=0.5)
+    K, W = args.steps, args.warmup
+    with torch.no_grad():
+        g = h.graphed(lambda: mamba3_mimo_decode_triton(x, Bp, Cp, ADT, DT, trap, Dsk, mx, mo, hs, bx), warm=W)
+        h.clocks_start()
+        h.barrier()
+        h.clocks_mark()
+        ms = h.timed_loop(lambda i: g.replay(), K)
+        h.barrier()
+        h.clocks_mark()
+    del g
+    clocks = h.clocks_stop()
+    total = h.max_over_ranks(float(ms.sum()))
+    mean = h.max_over_ranks(float(ms.mean()))
+    p50 = h.max_over_ranks(float(np.percentile(ms, 50)))
+    h.close()
+    if rank == 0:
+        nbytes = ssm_bytes_per_launch(m, batch)
+        peak, peak_kind = hbm_peak()
+        achieved = nbytes / (mean * 1e-3) / 1e9
+        line = {
+            "metric": "state-update sequences/s", "value": round(global_batch * K / (total / 1000.0), 1),
+            "unit": "sequences/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(total / K, 5),
+            "p50_step_ms": round(p50, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {**config_dict(args.workload, kw, global_batch, world, dtype_name),
+                       "step": "one mamba3_mimo_decode_triton launch (state update + readout on precomputed "
+                               "B / C projections), one-node CUDA graph, L2 flushed before every step"},
+            "roofline": {"bound": "hbm", "kernel": "state update (m3_mimo_decode)", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "bytes_per_launch": nbytes, "mean_launch_ms": round(mean, 5),
+                         "traffic": profile_traffic(args.workload, "ssm")},
+            "gpu_launches": K,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_prefill(args, kw, global_batch, dtype_name, length, world, rank, local):
     """Prompt prefill of one layer: each rank's share of `global_batch`
     sequences of `length` tokens through Mamba3Decoder.prefill (one in_proj
@@ -945,6 +1050,8 @@ def main():
         run_prefill(args, kw, global_batch, dtype_name, PREFILLS[args.workload], world, rank, local)
     elif args.workload in PROJECTIONS:
         run_projections(args, kw, global_batch, dtype_name, PROJECTIONS[args.workload], world, rank, local)
+    elif args.workload in SSM_WORKLOADS:
+        run_ssm(args, kw, global_batch, dtype_name, world, rank, local)
     else:
         run_layer(args, kw, global_batch, dtype_name, world, rank, local)
 

@@ -17,8 +17,11 @@ the way its ``forward`` composes them, ``x <- x + mixer_step(norm(x))``
 (the reference has no stack decode API).  Weights: ``torch.manual_seed(0)``,
 the reference's own init, then in_proj / out_proj ~ N(0, 0.02); inputs
 u ~ N(0, 1) from seed 1, cast to the weight dtype (a bf16 model needs bf16
-inputs); zero initial state.  Prints one JSON line: tokens/s (batch x
-timed steps / their wall time), ms per step, p50, steps timed, threads.
+inputs); zero initial state.  With ``--ssm`` what is timed is the
+reference's state-update-only MIMO decode, ``mamba3_mimo_decode_ref``
+(src/kernels/utils.py:109-148), on random fp32 inputs of the layer's shapes.
+Prints one JSON line: tokens/s (batch x timed steps / their wall time), ms
+per step, p50, steps timed, threads.
 """
 
 from __future__ import annotations
@@ -43,6 +46,7 @@ def main() -> int:
     ap.add_argument("--budget", type=float, default=10.0, help="stop timing after this many seconds")
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--threads", type=int, default=0, help="torch threads (0: every host core)")
+    ap.add_argument("--ssm", action="store_true", help="time the state-update-only MIMO decode")
     args = ap.parse_args()
 
     sys.dont_write_bytecode = True
@@ -80,8 +84,23 @@ def main() -> int:
     states = [d.init_state(args.batch) for d in decs]
     gen = torch.Generator().manual_seed(1)
     us = torch.randn(4, args.batch, kw["d_model"], generator=gen).to(dtype)
+    if args.ssm:
+        from src.kernels.utils import mamba3_mimo_decode_ref  # the reference's
+
+        m = mixers[0]
+        Bz, H, P, D, R = args.batch, m.nheads, m.headdim, m.d_state, m.mimo_rank
+        xs = torch.randn(Bz, H, P, generator=gen)
+        Bp, Cp = torch.randn(Bz, R, H, D, generator=gen), torch.randn(Bz, R, H, D, generator=gen)
+        DT = torch.rand(Bz, H, generator=gen) * 0.1 + 1e-3
+        ADT, trap = DT * 1e-4, torch.rand(Bz, H, generator=gen)
+        mx, mo = torch.randn(H, R, P, generator=gen) * 0.1, torch.randn(H, R, P, generator=gen) * 0.1
+        ssm = [torch.zeros(Bz, H, D), torch.zeros(Bz, H, D)]
 
     def step(u):
+        if args.ssm:
+            _, ssm[0], ssm[1] = mamba3_mimo_decode_ref(xs, Bp, Cp, ADT, DT, trap, m.D.float(), mx, mo, ssm[0],
+                                                       ssm[1])
+            return None
         if blocks[0] is None:
             out, states[0] = decs[0].step(u, states[0])
             return out
