@@ -187,6 +187,30 @@ int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void 
  * (0 when it does not split K); negative for an invalid shape. */
 int64_t m3_linear_bf16_workspace_bytes(int32_t M, int32_t N, int32_t K);
 
+/* fp32 linear layer of the decode step's projections for batches beyond the
+ * small-batch kernel's (same operation and call sites as m3_linear_f32,
+ * src/models/mamba3.py:115,158 called at src/models/inference.py:489,553),
+ * on the tensor cores in split precision: each fp32 operand is given as a
+ * TF32 head and its remainder (m3_split_tf32), and every k step issues the
+ * three tcgen05.mma (kind::tf32) products hi.hi + hi.lo + lo.hi, which
+ * carry about as many significant bits as fp32 (the dropped lo.lo term is
+ * ~2^-22 relative); accumulation in fp32.
+ *   C[m, n] = sum_k (A_hi + A_lo)[m, k] * (W_hi + W_lo)[n, k]
+ * A_hi / A_lo: (M, K) row stride lda; W_hi / W_lo: (N, K) row stride ldw;
+ * C: (M, N) fp32 row stride ldc.  16-byte aligned bases, K >= 32, K, lda and
+ * ldw multiples of 4.  No workspace.  M3_ERR_UNSUPPORTED when the driver
+ * offers no tensor-map encoder. */
+int m3_linear_f32_tc(const float *A_hi, const float *A_lo, int64_t lda, const float *W_hi, const float *W_lo,
+                     int64_t ldw, float *C, int64_t ldc, int32_t M, int32_t N, int32_t K, m3_stream_t stream);
+
+/* The operand split m3_linear_f32_tc takes: hi = x with the 13 low mantissa
+ * bits cleared (exactly a TF32 value), lo = x - hi (exact in fp32).
+ * x: (rows, cols) row stride ldx; hi, lo: row stride ld; 16-byte aligned,
+ * cols, ldx, ld multiples of 4.  No reference counterpart (the reference's
+ * projections are plain fp32 nn.Linear calls). */
+int m3_split_tf32(const float *x, int64_t ldx, float *hi, float *lo, int64_t ld, int32_t rows, int32_t cols,
+                  m3_stream_t stream);
+
 /* Arguments of the single-launch decode step (m3_mimo_step).
  *   dtype        M3_F32 or M3_BF16: u, both projection weights, the per-head
  *                parameters (as in m3_full_args), out and the workspace's

@@ -12,7 +12,7 @@ namespace {
 
 using m3::KParams;
 
-constexpr int kVersion = 10200;  // 1.2.0
+constexpr int kVersion = 10300;  // 1.3.0
 constexpr int kMaxHeaddim = 4096;
 
 bool dtype_ok(int32_t dt) { return dt == M3_F32 || dt == M3_BF16; }
@@ -364,6 +364,33 @@ int m3_linear_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, void 
   if (need > 0 && !aligned16(workspace)) return M3_ERR_ALIGN;
   return launch_status(m3::launch_gemm_bf16(A, lda, W, ldw, C, ldc, M, N, K, c_dtype == M3_BF16,
                                             static_cast<float *>(workspace), reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int m3_linear_f32_tc(const float *A_hi, const float *A_lo, int64_t lda, const float *W_hi, const float *W_lo,
+                     int64_t ldw, float *C, int64_t ldc, int32_t M, int32_t N, int32_t K, m3_stream_t stream) {
+  if (!A_hi || !A_lo || !W_hi || !W_lo || !C) return M3_ERR_NULL;
+  if (M < 0 || N <= 0 || K < 32 || lda < K || ldw < K || ldc < N) return M3_ERR_SHAPE;
+  if (K % 4 || lda % 4 || ldw % 4) return M3_ERR_ALIGN;
+  if (!aligned16(A_hi) || !aligned16(A_lo) || !aligned16(W_hi) || !aligned16(W_lo) || !aligned16(C))
+    return M3_ERR_ALIGN;
+  if (M == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  if (!m3::gemm_tf32x3_supported(A_hi, A_lo, lda, W_hi, W_lo, ldw, C, ldc, M, N, K)) return M3_ERR_UNSUPPORTED;
+  return launch_status(m3::launch_gemm_tf32x3(A_hi, A_lo, lda, W_hi, W_lo, ldw, C, ldc, M, N, K,
+                                              reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int m3_split_tf32(const float *x, int64_t ldx, float *hi, float *lo, int64_t ld, int32_t rows, int32_t cols,
+                  m3_stream_t stream) {
+  if (!x || !hi || !lo) return M3_ERR_NULL;
+  if (rows < 0 || cols < 0 || ldx < cols || ld < cols) return M3_ERR_SHAPE;
+  if (cols % 4 || ldx % 4 || ld % 4) return M3_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(hi) || !aligned16(lo)) return M3_ERR_ALIGN;
+  if (rows == 0 || cols == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  return launch_status(m3::launch_tf32_split(x, ldx, hi, lo, ld, rows, cols, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o, int64_t ldo, const float *w,

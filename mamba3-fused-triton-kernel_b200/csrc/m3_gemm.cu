@@ -18,6 +18,27 @@ namespace {
 
 constexpr int kTileK = 64;  // k per stage: one 128-byte swizzle row of bf16
 
+// Operand kinds of the paired-SM GEMM.
+//   kKindBF16    bf16 operands, one tcgen05.mma (kind::f16) per 16 k
+//   kKindTF32x3  fp32 operands given as TF32 heads and remainders
+//                (x = hi + lo, hi exactly representable in TF32), three
+//                tcgen05.mma (kind::tf32) per 8 k: hi.hi + hi.lo + lo.hi, the
+//                split-precision product of ~fp32 accuracy (the dropped
+//                lo.lo term is ~2^-22 relative)
+constexpr int kKindBF16 = 0;
+constexpr int kKindTF32x3 = 1;
+template <int KIND> struct PairKind;
+template <> struct PairKind<kKindBF16> {
+  static constexpr int kTileK = 64;  // elements of a 128-byte row
+  static constexpr int kPlanes = 1;  // operand planes per matrix
+  static constexpr uint32_t kFormat = 1;  // BF16
+};
+template <> struct PairKind<kKindTF32x3> {
+  static constexpr int kTileK = 32;
+  static constexpr int kPlanes = 2;  // hi, lo
+  static constexpr uint32_t kFormat = 2;  // TF32
+};
+
 // UMMA shared-memory descriptor of a K-major operand in the 128-byte swizzle
 // layout TMA writes: rows of 128 bytes, 8-row groups 1024 bytes apart
 // (stride byte offset), descriptor version 1, layout type 2 (128B swizzle).
@@ -59,18 +80,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map: `rows` rows of `cols` elements, `ld` elements apart;
-// boxes of 64 columns x `box_rows` rows, 128-byte swizzle, zero fill.
-bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 2-D tensor map of bf16 (f32 = false) or fp32 elements: `rows` rows of
+// `cols` elements, `ld` elements apart; boxes of one 128-byte row (64 bf16 or
+// 32 fp32 columns) x `box_rows` rows, 128-byte swizzle, zero fill.
+bool make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+              bool f32 = false) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
+  const int es = f32 ? 4 : 2;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)kTileK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int sm_count() { return sm_count_current(); }
@@ -167,6 +191,13 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t tmem, uint64_t a, uint64_
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
 
 // Arrive once on barrier `bar` (same shared::cta offset) of every CTA in
 // `cta_mask` when all MMAs this thread issued have completed.
@@ -216,16 +247,25 @@ __device__ __forceinline__ void store16(const PairArgs &g, int m, int n, const f
   }
 }
 
+// tw / tx: the weight and batch operands (bf16; TF32 heads for kKindTF32x3),
+// twl / txl: their TF32 remainders (kKindTF32x3 only; unused otherwise).
+// A stage holds, per plane, this CTA's 128 batch rows and nt / 2 weight rows
+// of one 128-byte k-tile.
+template <int KIND>
 __global__ void __launch_bounds__(kPairThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const PairArgs g) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+                     const __grid_constant__ CUtensorMap twl, const __grid_constant__ CUtensorMap txl,
+                     const PairArgs g) {
+  using K_ = PairKind<KIND>;
+  constexpr int kTileK = K_::kTileK, NPL = K_::kPlanes;
   extern __shared__ unsigned char smem_raw[];  // no static shared memory: the opt-in is the whole 227 KB
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  constexpr int kStageA = kPairBatch * kTileK * 2;  // this CTA's batch rows x 64 k
+  constexpr int kStageA = kPairBatch * 128;  // this CTA's batch rows x one 128-byte k-tile, per plane
   const int S = g.nstage;
-  unsigned char *ringA = smem;
-  unsigned char *ringB = smem + (size_t)S * kStageA;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * (kStageA + g.stage_b));
+  unsigned char *ringA = smem;                                  // [S][NPL][kStageA]
+  unsigned char *ringB = smem + (size_t)S * NPL * kStageA;      // [S][NPL][stage_b]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * NPL * (kStageA + g.stage_b));
   uint64_t *full = bars, *empty = bars + S, *accum = bars + 2 * S, *redbar = bars + 2 * S + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
   int *s_last = reinterpret_cast<int *>(tmem_slot + 1);  // shares the slot's 8 bytes
@@ -249,7 +289,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int krot = nkt > 0 ? (int)(((unsigned)tile * 7u) % (unsigned)nkt) : 0;
   auto kx_of = [&](int i) { int k = i + krot; return (kt0 + (k >= nkt ? k - nkt : k)) * kTileK; };
   const uint16_t pair_mask = 3;
-  const uint32_t stage_tx = 2u * (uint32_t)(kStageA + g.stage_b);  // both CTAs' copies of a stage
+  const uint32_t stage_tx = 2u * (uint32_t)(NPL * (kStageA + g.stage_b));  // both CTAs' copies of a stage
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -278,9 +318,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+    if constexpr (NPL == 2) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&twl)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&txl)) : "memory");
+    }
     for (int i = 0; i < npre; ++i) {
       if (leader) mbar_arrive_expect_tx(smem_addr(&full[i]), stage_tx);
-      tma_load_2d_pair(smem_addr(ringB + (size_t)i * g.stage_b), &tw, kx_of(i), nw, full_lead + 8u * i);
+      unsigned char *b = ringB + (size_t)i * NPL * g.stage_b;
+      tma_load_2d_pair(smem_addr(b), &tw, kx_of(i), nw, full_lead + 8u * i);
+      if constexpr (NPL == 2) tma_load_2d_pair(smem_addr(b + g.stage_b), &twl, kx_of(i), nw, full_lead + 8u * i);
     }
   }
   pdl_wait();
@@ -290,8 +336,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0) {
       // producer: k-tile i into stage i % S once the MMAs of k-tile i - S
       // (in both CTAs) have released it
-      for (int i = 0; i < npre; ++i)
-        tma_load_2d_pair(smem_addr(ringA + (size_t)i * kStageA), &tx, kx_of(i), mb, full_lead + 8u * i);
+      for (int i = 0; i < npre; ++i) {
+        unsigned char *a = ringA + (size_t)i * NPL * kStageA;
+        tma_load_2d_pair(smem_addr(a), &tx, kx_of(i), mb, full_lead + 8u * i);
+        if constexpr (NPL == 2) tma_load_2d_pair(smem_addr(a + kStageA), &txl, kx_of(i), mb, full_lead + 8u * i);
+      }
       int s = npre % S;
       uint32_t ph = npre == S ? 1u : 0u;
       int issued = npre;
@@ -299,8 +348,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (!mbar_wait(smem_addr(&empty[s]), ph ^ 1u)) break;
         if (leader) mbar_arrive_expect_tx(smem_addr(&full[s]), stage_tx);
         const int kx = kx_of(i);
-        tma_load_2d_pair(smem_addr(ringB + (size_t)s * g.stage_b), &tw, kx, nw, full_lead + 8u * s);
-        tma_load_2d_pair(smem_addr(ringA + (size_t)s * kStageA), &tx, kx, mb, full_lead + 8u * s);
+        unsigned char *b = ringB + (size_t)s * NPL * g.stage_b;
+        unsigned char *a = ringA + (size_t)s * NPL * kStageA;
+        tma_load_2d_pair(smem_addr(b), &tw, kx, nw, full_lead + 8u * s);
+        if constexpr (NPL == 2) tma_load_2d_pair(smem_addr(b + g.stage_b), &twl, kx, nw, full_lead + 8u * s);
+        tma_load_2d_pair(smem_addr(a), &tx, kx, mb, full_lead + 8u * s);
+        if constexpr (NPL == 2) tma_load_2d_pair(smem_addr(a + kStageA), &txl, kx, mb, full_lead + 8u * s);
         issued = i + 1;
         if (++s == S) {
           s = 0;
@@ -317,23 +370,36 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      // D[256 x nt] (+)= X_pair[256 x 64] . W_pair[nt x 64]^T per k-tile
-      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(g.nt >> 3) << 17) |
-                             ((uint32_t)((2 * kPairBatch) >> 4) << 24);
+      // D[256 x nt] (+)= X_pair[256 x k] . W_pair[nt x k]^T per k-tile;
+      // instruction descriptor: fp32 accumulator, A and B in the kind's
+      // format, both K-major, N / 8 and M / 16
+      const uint32_t idesc = (1u << 4) | (K_::kFormat << 7) | (K_::kFormat << 10) |
+                             ((uint32_t)(g.nt >> 3) << 17) | ((uint32_t)((2 * kPairBatch) >> 4) << 24);
       int s = 0;
       uint32_t ph = 0;
       for (int i = 0; i < nkt; ++i) {
         if (!mbar_wait(smem_addr(&full[s]), ph)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_addr(ringA + (size_t)s * kStageA);
-        const uint32_t b0 = smem_addr(ringB + (size_t)s * g.stage_b);
+        const uint32_t a0 = smem_addr(ringA + (size_t)s * NPL * kStageA);
+        const uint32_t b0 = smem_addr(ringB + (size_t)s * NPL * g.stage_b);
         // with two accumulators, k-tile i adds into accumulator i % 2: two
         // independent chains of MMAs
         const int ai = g.nacc == 2 ? (i & 1) : 0;
         const uint32_t d = tmem + (uint32_t)(ai * g.nt);
+        // four 32-byte k steps per 128-byte row (16 bf16 or 8 TF32 each)
 #pragma unroll
-        for (int j = 0; j < kTileK / 16; ++j)
-          mma_bf16_pair(d, sw128_desc(a0 + 32 * j), sw128_desc(b0 + 32 * j), idesc, (i >> (g.nacc - 1) | j) != 0 ? 1u : 0u);
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t acc = (i >> (g.nacc - 1) | j) != 0 ? 1u : 0u;
+          if constexpr (KIND == kKindBF16) {
+            mma_bf16_pair(d, sw128_desc(a0 + 32 * j), sw128_desc(b0 + 32 * j), idesc, acc);
+          } else {
+            const uint64_t ah = sw128_desc(a0 + 32 * j), al = sw128_desc(a0 + kStageA + 32 * j);
+            const uint64_t bh = sw128_desc(b0 + 32 * j), bl = sw128_desc(b0 + g.stage_b + 32 * j);
+            mma_tf32_pair(d, ah, bh, idesc, acc);
+            mma_tf32_pair(d, ah, bl, idesc, 1u);
+            mma_tf32_pair(d, al, bh, idesc, 1u);
+          }
+        }
         mma_commit_to_pair(smem_addr(&empty[s]), pair_mask);
         if (++s == S) {
           s = 0;
@@ -404,7 +470,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // the other pairs' slots, into the idle ring when they fit (one
         // bulk copy each), else read from L2 column by column
         const uint32_t slot_bytes = (uint32_t)(slot_elems * 4);
-        const bool staged = (int64_t)(g.nsplit - 1) * slot_bytes <= (int64_t)S * (kStageA + g.stage_b);
+        const bool staged = (int64_t)(g.nsplit - 1) * slot_bytes <= (int64_t)S * NPL * (kStageA + g.stage_b);
         float *ring = reinterpret_cast<float *>(smem);
         auto other = [&](int p) -> int { return p < kq ? p : p - 1; };  // staging index of slot p
         if (staged) {
@@ -505,8 +571,36 @@ int64_t pair_workspace_bytes(const PairPlan &p) {
   return p.nsplit > 1 ? kPairTicketBytes + (int64_t)p.ntn * p.ntm * 2 * p.nsplit * kPairBatch * p.nt * 4 : 0;
 }
 
-cudaError_t launch_gemm_pair(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
-                             int N, int K, bool y_bf16, void *workspace, const PairPlan &pl, cudaStream_t stream) {
+// TF32x3 tile plan: no K split (the fp32 path is taken for batches of
+// several hundred rows and more, which give enough pair tiles); the tile
+// width with the fewest waves x k-tiles, a 256-wide k-tile costing about
+// three times the bf16 one (three products at half the bf16 rate).
+PairPlan plan_pair_tf32(int M, int N, int K) {
+  const int sms = sm_count();
+  const int ntm = (M + 2 * kPairBatch - 1) / (2 * kPairBatch);
+  const int ktotal = (K + PairKind<kKindTF32x3>::kTileK - 1) / PairKind<kKindTF32x3>::kTileK;
+  PairPlan best = {};
+  double best_cost = 1e30;
+  for (int nt : {256, 128}) {
+    const int ntn = (N + nt - 1) / nt;
+    const int waves = (2 * ntn * ntm + sms - 1) / sms;
+    const double cost = waves * ktotal * (0.1 + 0.85 * nt / 256.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = {nt, ntn, ntm, ktotal, ktotal, 1, 1};
+    }
+  }
+  return best;
+}
+
+// x / w: the batch and weight operands (TF32 heads for kKindTF32x3), xl / wl
+// their TF32 remainders (kKindTF32x3 only).
+template <int KIND>
+cudaError_t launch_gemm_pair(const void *x, const void *xl, int64_t ldx, const void *w, const void *wl, int64_t ldw,
+                             void *y, int64_t ldy, int M, int N, int K, bool y_bf16, void *workspace,
+                             const PairPlan &pl, cudaStream_t stream) {
+  using K_ = PairKind<KIND>;
+  constexpr bool kF32 = KIND == kKindTF32x3;
   PairArgs g = {};
   g.M = M;
   g.N = N;
@@ -522,8 +616,8 @@ cudaError_t launch_gemm_pair(const void *x, int64_t ldx, const void *w, int64_t 
     g.part = reinterpret_cast<float *>(static_cast<char *>(workspace) + kPairTicketBytes);
   }
   g.nacc = pl.nacc == 2 && 2 * pl.nt <= 512 ? 2 : 1;
-  g.stage_b = (g.nt / 2) * kTileK * 2;
-  const int stage = kPairBatch * kTileK * 2 + g.stage_b;
+  g.stage_b = (g.nt / 2) * 128;
+  const int stage = K_::kPlanes * (kPairBatch * 128 + g.stage_b);
   int S = kPairSmem / stage;
   S = S > kPairMaxStages ? kPairMaxStages : S;
   if (S > g.ktiles) S = g.ktiles < 2 ? 2 : g.ktiles;
@@ -534,13 +628,22 @@ cudaError_t launch_gemm_pair(const void *x, int64_t ldx, const void *w, int64_t 
   g.ldy = ldy;
   g.y_bf16 = y_bf16 ? 1 : 0;
   const int smem = 1024 + S * stage + (2 * S + 3) * 8;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
 
-  CUtensorMap tw, tx;
-  if (!make_map(&tw, w, N, K, ldw, g.nt / 2) || !make_map(&tx, x, M, K, ldx, kPairBatch))
+  CUtensorMap tw, tx, twl, txl;
+  if (!make_map(&tw, w, N, K, ldw, g.nt / 2, kF32) || !make_map(&tx, x, M, K, ldx, kPairBatch, kF32))
     return cudaErrorInvalidValue;
+  if (kF32) {
+    if (!make_map(&twl, wl, N, K, ldw, g.nt / 2, true) || !make_map(&txl, xl, M, K, ldx, kPairBatch, true))
+      return cudaErrorInvalidValue;
+  } else {
+    twl = tw;
+    txl = tx;
+  }
 
+  auto kern = gemm_pair_kernel<KIND>;
   static LaunchCache cache;
-  if (cudaError_t e = ensure_smem_optin(cache, gemm_pair_kernel, 227 * 1024); e != cudaSuccess) return e;
+  if (cudaError_t e = ensure_smem_optin(cache, kern, 227 * 1024); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * g.nsplit * pl.ntn * pl.ntm));
   cfg.blockDim = dim3(kPairThreads);
@@ -555,9 +658,35 @@ cudaError_t launch_gemm_pair(const void *x, int64_t ldx, const void *w, int64_t 
   attrs[1].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, tw, tx, g);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, twl, txl, g);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+// The TF32 head / remainder split of an fp32 matrix (rows x cols, rows ld
+// elements apart): hi = x with its 13 low mantissa bits cleared (exactly a
+// TF32 value), lo = x - hi (exact in fp32).  One thread per 4 elements.
+__global__ void __launch_bounds__(256) tf32_split_kernel(const float *__restrict__ x, int64_t ldx,
+                                                         float *__restrict__ hi, float *__restrict__ lo, int64_t ld,
+                                                         int rows, int cols4) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n = (int64_t)rows * cols4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols4, c = (i - r * cols4) * 4;
+    const float4 v = *reinterpret_cast<const float4 *>(x + r * ldx + c);
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    l.x = v.x - h.x;
+    l.y = v.y - h.y;
+    l.z = v.z - h.z;
+    l.w = v.w - h.w;
+    *reinterpret_cast<float4 *>(hi + r * ld + c) = h;
+    *reinterpret_cast<float4 *>(lo + r * ld + c) = l;
+  }
 }
 
 }  // namespace
@@ -576,7 +705,32 @@ int64_t gemm_bf16_workspace_bytes(int M, int N, int K) {
 
 cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
                              int N, int K, bool y_bf16, float *workspace, cudaStream_t stream) {
-  return launch_gemm_pair(x, ldx, w, ldw, y, ldy, M, N, K, y_bf16, workspace, plan_pair(M, N, K), stream);
+  return launch_gemm_pair<kKindBF16>(x, nullptr, ldx, w, nullptr, ldw, y, ldy, M, N, K, y_bf16, workspace,
+                                     plan_pair(M, N, K), stream);
+}
+
+bool gemm_tf32x3_supported(const void *x, const void *xl, int64_t ldx, const void *w, const void *wl, int64_t ldw,
+                           const void *y, int64_t ldy, int M, int N, int K) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return M > 0 && N > 0 && K >= 32 && K % 4 == 0 && ldx % 4 == 0 && ldw % 4 == 0 && ldx >= K && ldw >= K &&
+         ldy >= N && al(x) && al(xl) && al(w) && al(wl) && al(y) && encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_tf32x3(const float *x, const float *xl, int64_t ldx, const float *w, const float *wl,
+                               int64_t ldw, float *y, int64_t ldy, int M, int N, int K, cudaStream_t stream) {
+  return launch_gemm_pair<kKindTF32x3>(x, xl, ldx, w, wl, ldw, y, ldy, M, N, K, false, nullptr,
+                                       plan_pair_tf32(M, N, K), stream);
+}
+
+cudaError_t launch_tf32_split(const float *x, int64_t ldx, float *hi, float *lo, int64_t ld, int rows, int cols,
+                              cudaStream_t stream) {
+  const int cols4 = cols / 4;
+  const int64_t n = (int64_t)rows * cols4;
+  int64_t blocks = (n + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return launch_pdl(tf32_split_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, x, ldx, hi, lo, ld, rows, cols4);
 }
 
 int gemm_device_error(bool reset) { return device_error_of_this_unit(reset); }

@@ -510,6 +510,15 @@ bool gemm_bf16_supported(const void *x, int64_t ldx, const void *w, int64_t ldw,
 int64_t gemm_bf16_workspace_bytes(int M, int N, int K);
 cudaError_t launch_gemm_bf16(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
                              int N, int K, bool y_bf16, float *workspace, cudaStream_t stream);
+// The split-precision fp32 GEMM on the same kernel (kind::tf32, three
+// products per k step): y = (x + xl) . (w + wl)^T with x / w TF32 heads and
+// xl / wl their remainders; and the head / remainder split of a matrix.
+bool gemm_tf32x3_supported(const void *x, const void *xl, int64_t ldx, const void *w, const void *wl, int64_t ldw,
+                           const void *y, int64_t ldy, int M, int N, int K);
+cudaError_t launch_gemm_tf32x3(const float *x, const float *xl, int64_t ldx, const float *w, const float *wl,
+                               int64_t ldw, float *y, int64_t ldy, int M, int N, int K, cudaStream_t stream);
+cudaError_t launch_tf32_split(const float *x, int64_t ldx, float *hi, float *lo, int64_t ld, int rows, int cols,
+                              cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
                                     int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,

@@ -2,9 +2,13 @@
 
 ``linear(x, weight)`` computes ``x @ weight.T`` (``nn.Linear`` without bias,
 src/models/mamba3.py:115,158).  Small fp32 batches -- the latency-bound
-decode regime -- run the library's ``m3_linear_f32`` kernel; with
-``TC_ROUTE`` set, bf16 batches up to ``TC_MAX_M`` rows run the library's
-tcgen05 GEMM (``m3_linear_bf16``: pairs of SMs sharing each batch tile,
+decode regime -- run the library's ``m3_linear_f32`` kernel; larger fp32
+batches run the library's split-precision tensor-core GEMM
+(``m3_linear_f32_tc``: each operand split into a TF32 head and remainder,
+three tcgen05 kind::tf32 products per k step, about fp32 accuracy; the
+weight's split is computed once and cached); with ``TC_ROUTE`` set, bf16
+batches up to ``TC_MAX_M`` rows run the library's tcgen05 GEMM
+(``m3_linear_bf16``: pairs of SMs sharing each batch tile,
 ``cta_group::2``); everything else uses cuBLAS through
 ``torch.nn.functional.linear``.  ``TC_ROUTE`` is off: at the decode shapes
 measured on B200 cuBLAS is faster (24 layers of in_proj + out_proj at
@@ -21,6 +25,7 @@ from src import _native as nat
 SMALL_M_MAX = 256  # batch rows up to which the latency-optimised kernel is used
 TC_MAX_M = 512     # bf16 batch rows up to which TC_ROUTE uses the tcgen05 GEMM
 TC_ROUTE = False   # route bf16 projections to m3_linear_bf16 (off: cuBLAS is faster at the decode shapes)
+TF32X3_ROUTE = True  # route fp32 batches above SMALL_M_MAX rows to m3_linear_f32_tc
 
 
 def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
@@ -36,6 +41,58 @@ def uses_tc_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.shape[1] % 8 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
             and weight.stride(1) == 1 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
+
+
+def uses_tf32x3(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    return (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype == torch.float32
+            and weight.dtype == torch.float32 and x.shape[0] > SMALL_M_MAX and x.shape[1] >= 32
+            and x.shape[1] % 4 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
+            and weight.stride(1) == 1 and x.stride(0) % 4 == 0 and weight.stride(0) % 4 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
+
+
+_weight_splits: dict = {}  # (device, data_ptr, version, shape, stride) -> (hi, lo) of a weight
+
+
+def tf32_split(x: torch.Tensor):
+    """(hi, lo): x with its 13 low mantissa bits cleared and the exact
+    remainder, contiguous fp32 (m3_split_tf32)."""
+    M, K = x.shape
+    hi = torch.empty(M, K, device=x.device, dtype=torch.float32)
+    lo = torch.empty_like(hi)
+    with nat.device_guard(x.device):
+        st = nat.load().m3_split_tf32(x.data_ptr(), x.stride(0), hi.data_ptr(), lo.data_ptr(), K, M, K,
+                                      nat.stream_handle(x.device))
+    nat.check(st, "m3_split_tf32")
+    return hi, lo
+
+
+def _weight_split(weight: torch.Tensor):
+    """The weight's TF32 head and remainder, computed once per weight (and
+    again after an in-place change, which bumps the tensor's version)."""
+    key = (weight.device.index, weight.data_ptr(), weight._version, tuple(weight.shape), tuple(weight.stride()))
+    hit = _weight_splits.get(key)
+    if hit is None:
+        for k in [k for k in _weight_splits if k[:2] == key[:2]]:
+            del _weight_splits[k]  # stale split of an earlier version of this storage
+        hit = tf32_split(weight)
+        _weight_splits[key] = hit
+    return hit
+
+
+def linear_tf32x3(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """``x @ weight.T`` for fp32 x (M, K), weight (N, K) on the tensor cores
+    in split precision (m3_linear_f32_tc)."""
+    M, K = x.shape
+    N = weight.shape[0]
+    out = torch.empty(M, N, device=x.device, dtype=torch.float32)
+    w_hi, w_lo = _weight_split(weight)
+    x_hi, x_lo = tf32_split(x)
+    with nat.device_guard(x.device):
+        st = nat.load().m3_linear_f32_tc(x_hi.data_ptr(), x_lo.data_ptr(), K, w_hi.data_ptr(), w_lo.data_ptr(), K,
+                                         out.data_ptr(), out.stride(0), M, N, K, nat.stream_handle(x.device))
+    nat.check(st, "m3_linear_f32_tc")
+    return out
 
 
 _workspaces: dict = {}  # device index -> split-K workspace, grown on demand and kept
@@ -78,6 +135,8 @@ def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """``x @ weight.T`` for x (M, K), weight (N, K)."""
     if TC_ROUTE and uses_tc_bf16(x, weight):
         return linear_bf16(x, weight)
+    if TF32X3_ROUTE and uses_tf32x3(x, weight):
+        return linear_tf32x3(x, weight)
     if not uses_small_m_kernel(x, weight):
         return F.linear(x, weight)
     M, K = x.shape

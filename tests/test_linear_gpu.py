@@ -1,14 +1,16 @@
-"""GPU checks of the small-batch projection kernel (``m3_linear_f32``):
-x @ W^T against a float64 product, over batch sizes, widths and depths that
-do and do not fill the 16 x 16 CTA tile and the 128-wide K slices, strided
-rows, and the size-based dispatch to cuBLAS."""
+"""GPU checks of the projection GEMMs against float64 products: the
+small-batch fp32 kernel (``m3_linear_f32``) over batch sizes, widths and
+depths that do and do not fill the 16 x 16 CTA tile and the 128-wide K
+slices, strided rows; the split-precision fp32 tensor-core GEMM
+(``m3_linear_f32_tc``) that larger fp32 batches take; the bf16 tcgen05 GEMM
+(``m3_linear_bf16``); and the size-based dispatch between them and cuBLAS."""
 
 from __future__ import annotations
 
 import pytest
 import torch
 
-from src.kernels.linear import SMALL_M_MAX, linear, uses_small_m_kernel
+from src.kernels.linear import SMALL_M_MAX, linear, linear_tf32x3, tf32_split, uses_small_m_kernel, uses_tf32x3
 
 pytestmark = pytest.mark.gpu
 
@@ -34,11 +36,12 @@ def test_strided_rows_and_views():
     torch.testing.assert_close(linear(x, w), (x.double() @ w.double().T).float(), rtol=2e-5, atol=4e-4)
 
 
-def test_dispatch_to_cublas_outside_the_small_batch_regime():
+def test_dispatch_outside_the_small_batch_regime():
     w = torch.randn(64, 128, device="cuda")
     big = torch.randn(SMALL_M_MAX + 1, 128, device="cuda")
     assert not uses_small_m_kernel(big, w)
-    torch.testing.assert_close(linear(big, w), big @ w.T)
+    assert uses_tf32x3(big, w)
+    torch.testing.assert_close(linear(big, w), (big.double() @ w.double().T).float(), rtol=1e-5, atol=1e-4)
     xb = torch.randn(8, 128, device="cuda").bfloat16()
     assert not uses_small_m_kernel(xb, w.bfloat16())
     torch.testing.assert_close(linear(xb, w.bfloat16()), xb @ w.bfloat16().T)
@@ -91,5 +94,56 @@ def test_tc_bf16_dispatch():
     assert not uses_tc_bf16(torch.randn(TC_MAX_M + 1, 128, device="cuda").bfloat16(), w)
     assert not uses_tc_bf16(torch.randn(4, 128, device="cuda"), w.float())
     assert not uses_tc_bf16(torch.randn(4, 60, device="cuda").bfloat16(), torch.randn(8, 60, device="cuda").bfloat16())
+    from src import _native as nat
+    assert nat.device_error() == 0
+
+
+# ---- fp32 projections of larger batches: split-precision tcgen05 GEMM ----
+
+F32TC_SHAPES = [  # M, N, K: the d1024 layer's in_proj (R 4) / out_proj at batch 4096, tails, odd K
+    (4096, 5248, 1024), (4096, 1024, 2048), (257, 64, 32), (300, 1000, 100), (1000, 4480, 1024), (600, 257, 36),
+    (513, 6272, 1024),
+]
+
+
+@pytest.mark.parametrize("M,N,K", F32TC_SHAPES)
+def test_tf32x3_matches_float64(M, N, K):
+    """Each product is taken as hi.hi + hi.lo + lo.hi of TF32 heads and
+    remainders (the dropped lo.lo and the remainders' own TF32 rounding are
+    ~2^-22 relative), accumulated in fp32: the error must stay at the size of
+    an fp32 GEMM's, 2e-6 sqrt(K) of the outputs' scale (the bound the bf16
+    GEMM's exact products are held to), and within a small factor of cuBLAS
+    fp32 on the same inputs."""
+    g = torch.Generator(device="cuda").manual_seed(M + 7 * N + 13 * K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.05
+    assert uses_tf32x3(x, w)
+    y = linear(x, w)
+    assert y.dtype == torch.float32 and y.shape == (M, N)
+    ref = x.double() @ w.double().T
+    err = (y.double() - ref).abs().max().item()
+    scale = max(1.0, ref.abs().max().item())
+    assert err <= 2e-6 * K ** 0.5 * scale, err
+    err_cublas = ((x @ w.T).double() - ref).abs().max().item()
+    assert err <= 8.0 * err_cublas + 1e-6 * scale, (err, err_cublas)
+
+
+def test_tf32_split_is_exact():
+    x = torch.randn(300, 260, device="cuda") * 1e3
+    hi, lo = tf32_split(x)
+    assert torch.equal(hi + lo, x)
+    assert torch.equal(hi.view(torch.int32) & 0x1FFF, torch.zeros_like(hi, dtype=torch.int32))
+    assert (lo.abs() <= hi.abs() * 2.0 ** -10).all()
+
+
+def test_tf32x3_strided_rows_and_weight_cache():
+    xb = torch.randn(400, 136, device="cuda")
+    wb = torch.randn(96, 140, device="cuda") * 0.05
+    x, w = xb[:, :128], wb[:, :128]
+    assert uses_tf32x3(x, w)
+    ref = x.double() @ w.double().T
+    torch.testing.assert_close(linear_tf32x3(x, w).double(), ref, rtol=0, atol=2e-5)
+    w.mul_(2.0)  # an in-place change: the cached split must not be reused
+    torch.testing.assert_close(linear_tf32x3(x, w).double(), 2.0 * ref, rtol=0, atol=4e-5)
     from src import _native as nat
     assert nat.device_error() == 0

@@ -93,3 +93,4 @@ def test_stream_large_angles():
     np.testing.assert_allclose(y.cpu().numpy(), ye, **TOL)
     np.testing.assert_allclose(st["ssm_state"].cpu().numpy(), h, **TOL)
     np.testing.assert_allclose(st["bx_prev"].cpu().numpy(), bx, **TOL)
+
