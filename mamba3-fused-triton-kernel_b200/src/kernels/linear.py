@@ -17,6 +17,8 @@ batch 256, d_model 2048: 473 us against 860 us).
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 import torch.nn.functional as F
 
@@ -51,7 +53,10 @@ def uses_tf32x3(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
 
 
-_weight_splits: dict = {}  # (device, data_ptr, version, shape, stride) -> (hi, lo) of a weight
+# id(weight) -> ((data_ptr, version, shape, stride), hi, lo); an entry is
+# dropped when its weight tensor is freed, so a later tensor that reuses the
+# memory (or the id) never meets a stale split
+_weight_splits: dict = {}
 
 
 def tf32_split(x: torch.Tensor):
@@ -68,16 +73,20 @@ def tf32_split(x: torch.Tensor):
 
 
 def _weight_split(weight: torch.Tensor):
-    """The weight's TF32 head and remainder, computed once per weight (and
-    again after an in-place change, which bumps the tensor's version)."""
-    key = (weight.device.index, weight.data_ptr(), weight._version, tuple(weight.shape), tuple(weight.stride()))
-    hit = _weight_splits.get(key)
+    """The weight's TF32 head and remainder, computed once per weight tensor
+    (and again after an in-place change, which bumps its version).  A CUDA
+    graph that captured a projection keeps using the split it captured, so a
+    weight changed after capture needs a new capture."""
+    k = id(weight)
+    sig = (weight.device.index, weight.data_ptr(), weight._version, tuple(weight.shape), tuple(weight.stride()))
+    hit = _weight_splits.get(k)
+    if hit is not None and hit[0] == sig:
+        return hit[1], hit[2]
     if hit is None:
-        for k in [k for k in _weight_splits if k[:2] == key[:2]]:
-            del _weight_splits[k]  # stale split of an earlier version of this storage
-        hit = tf32_split(weight)
-        _weight_splits[key] = hit
-    return hit
+        weakref.finalize(weight, _weight_splits.pop, k, None)
+    hi, lo = tf32_split(weight)
+    _weight_splits[k] = (sig, hi, lo)
+    return hi, lo
 
 
 def linear_tf32x3(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:

@@ -145,5 +145,14 @@ def test_tf32x3_strided_rows_and_weight_cache():
     torch.testing.assert_close(linear_tf32x3(x, w).double(), ref, rtol=0, atol=2e-5)
     w.mul_(2.0)  # an in-place change: the cached split must not be reused
     torch.testing.assert_close(linear_tf32x3(x, w).double(), 2.0 * ref, rtol=0, atol=4e-5)
+    # a new weight in memory freed by an earlier one of the same shape
+    ptr = w.data_ptr()
+    del w, wb
+    for _ in range(4):
+        w2 = torch.randn(96, 140, device="cuda")[:, :128] * 0.05
+        torch.testing.assert_close(linear_tf32x3(x, w2).double(), x.double() @ w2.double().T, rtol=0, atol=2e-5)
+        if w2.data_ptr() == ptr:
+            break
+        del w2
     from src import _native as nat
     assert nat.device_error() == 0
