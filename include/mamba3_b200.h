@@ -263,6 +263,26 @@ int64_t m3_mimo_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32
  * launches. */
 int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream);
 
+/* Workspace bytes m3_siso_step needs for this layer and batch (dims with
+ * mimo_rank 1), or the negated status; -M3_ERR_UNSUPPORTED for a valid
+ * layer outside the kernel's range (headdim > 1024, d_model or d_inner not a
+ * multiple of 4). */
+int64_t m3_siso_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32_t dtype);
+
+/* The whole decode step of one SISO layer (is_mimo=False) in ONE launch:
+ * in_proj, the full-step fused SISO update (m3_siso_full_fused) and
+ * out_proj, the sequence of Mamba3Decoder._step_triton_full_fused
+ * (src/models/inference.py:476-559) for SISO layers.  Same arguments,
+ * workspace rules and grid barriers as m3_mimo_step; the state is the SISO
+ * layout (batch, nheads, headdim, d_state), B_bias / C_bias are (nheads,
+ * d_state), and mimo_x / mimo_o are not read (may be NULL).  Each (batch
+ * row, head) state tile is updated by one CTA.  For callers that want one
+ * launch per step (eager decoding, where each launch costs host time);
+ * replayed from a CUDA graph the three launches measured faster on B200
+ * (18.9 against 24.6 us a step for the d256 layer at batch 1), so the
+ * Python decoder keeps them for SISO layers. */
+int m3_siso_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream);
+
 /* Bytes of the library's own device scratch array behind m3_mimo_step_static
  * (held on every GPU that loads the library until the process exits). */
 #define M3_STEP_STATIC_SCRATCH_BYTES (4 * 1024 * 1024)

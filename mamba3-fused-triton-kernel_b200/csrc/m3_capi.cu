@@ -148,16 +148,18 @@ StepLayout step_layout(const m3_dims *d, int64_t d_in_proj, int es) {
   return L;
 }
 
-// Shape checks of the single-launch step; M3_ERR_UNSUPPORTED for a valid
-// layer the kernel does not take.
-int check_step_dims(const m3_dims *d, int32_t d_model, int32_t dtype) {
-  int st = check_dims(d, true);
+// Shape checks of the single-launch step (MIMO or SISO layer);
+// M3_ERR_UNSUPPORTED for a valid layer the kernel does not take.
+int check_step_dims(const m3_dims *d, int32_t d_model, int32_t dtype, bool mimo) {
+  int st = check_dims(d, mimo);
   if (st != M3_OK) return st;
   if (!dtype_ok(dtype)) return M3_ERR_DTYPE;
   if (d->ngroups != 1 || d->d_inner != d->nheads * d->headdim || d_model <= 0) return M3_ERR_SHAPE;
   if (d->num_rope_angles <= 0 || 2 * d->num_rope_angles > d->d_state) return M3_ERR_SHAPE;
-  if (d->nheads % 8 != 0 || d->headdim > 128 || d->d_state > 128 || d_model % 4 != 0 || d->d_inner % 4 != 0)
-    return M3_ERR_UNSUPPORTED;
+  if (!mimo && d->mimo_rank != 1) return M3_ERR_SHAPE;
+  if (d_model % 4 != 0 || d->d_inner % 4 != 0) return M3_ERR_UNSUPPORTED;
+  if (mimo && (d->nheads % 8 != 0 || d->headdim > 128 || d->d_state > 128)) return M3_ERR_UNSUPPORTED;
+  if (!mimo && d->headdim > 1024) return M3_ERR_UNSUPPORTED;
   return M3_OK;
 }
 
@@ -180,23 +182,23 @@ void add_prefetch(m3::StepParams &sp, const void *p, int64_t bytes) {
   ++sp.n_prefetch;
 }
 
-int64_t step_workspace_bytes(const m3_dims *d, int32_t d_model, int32_t dtype) {
-  const int st = check_step_dims(d, d_model, dtype);
+int64_t step_workspace_bytes(const m3_dims *d, int32_t d_model, int32_t dtype, bool mimo) {
+  const int st = check_step_dims(d, d_model, dtype, mimo);
   if (st != M3_OK) return -(int64_t)st;
   const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * d->mimo_rank + 3LL * d->nheads + d->num_rope_angles;
   return step_layout(d, d_in_proj, dtype == M3_BF16 ? 2 : 4).bytes;
 }
 
-// Every check m3_mimo_step makes before it enqueues anything; *empty is set
-// for a batch of zero rows (nothing to launch).
-int step_check(const m3_dims *d, const m3_step_args *a, bool *empty) {
+// Every check m3_mimo_step / m3_siso_step makes before it enqueues
+// anything; *empty is set for a batch of zero rows (nothing to launch).
+int step_check(const m3_dims *d, const m3_step_args *a, bool *empty, bool mimo) {
   *empty = false;
   if (!d || !a) return M3_ERR_NULL;
-  int st = check_step_dims(d, a->d_model, a->dtype);
+  int st = check_step_dims(d, a->d_model, a->dtype, mimo);
   if (st != M3_OK) return st;
   if (!a->u || !a->in_proj_w || !a->out_proj_w || !a->dt_bias || !a->D || !a->B_norm_w || !a->C_norm_w ||
-      !a->B_bias || !a->C_bias || !a->mimo_x || !a->mimo_o || !a->ssm_state || !a->bx_prev || !a->angle_state ||
-      !a->out || !a->workspace)
+      !a->B_bias || !a->C_bias || (mimo && (!a->mimo_x || !a->mimo_o)) || !a->ssm_state || !a->bx_prev ||
+      !a->angle_state || !a->out || !a->workspace)
     return M3_ERR_NULL;
   const int es = a->dtype == M3_BF16 ? 2 : 4;
   const int R = d->mimo_rank;
@@ -227,12 +229,12 @@ int step_check(const m3_dims *d, const m3_step_args *a, bool *empty) {
   return M3_OK;
 }
 
-int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
+int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream, bool mimo) {
   bool empty = false;
-  const int st = step_check(d, a, &empty);
+  const int st = step_check(d, a, &empty, mimo);
   if (st != M3_OK || empty) return st;
   const int es = a->dtype == M3_BF16 ? 2 : 4;
-  const int R = d->mimo_rank;
+  const int R = mimo ? d->mimo_rank : 1;
   const int64_t d_in_proj = 2LL * d->d_inner + 2LL * d->d_state * R + 3LL * d->nheads + d->num_rope_angles;
   const StepLayout L = step_layout(d, d_in_proj, es);
 
@@ -242,10 +244,10 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
   kp.B = d->batch; kp.H = d->nheads; kp.P = d->headdim; kp.D = d->d_state; kp.R = R;
   kp.A = d->num_rope_angles; kp.A_floor = d->A_floor;
   kp.d_inner = d->d_inner; kp.d_bc = d->d_state * R;
-  kp.heads_per_cta = m3::mimo_heads_per_cta(kp.H);
+  kp.heads_per_cta = mimo ? m3::mimo_heads_per_cta(kp.H) : 1;
   kp.zx = ws + L.zx_off; kp.zx_sb = L.ldzx; kp.zx_dt = a->dtype; kp.par_dt = a->dtype;
   kp.dt_bias = a->dt_bias; kp.Dp = a->D; kp.wB = a->B_norm_w; kp.wC = a->C_norm_w;
-  kp.bB = a->B_bias; kp.bC = a->C_bias; kp.mx = a->mimo_x; kp.mo = a->mimo_o;
+  kp.bB = a->B_bias; kp.bC = a->C_bias; kp.mx = mimo ? a->mimo_x : nullptr; kp.mo = mimo ? a->mimo_o : nullptr;
   kp.h = a->ssm_state; kp.bx = a->bx_prev; kp.ang = a->angle_state;
   kp.y = ws + L.y_off; kp.y_sb = d->d_inner; kp.y_sh = d->headdim; kp.y_sp = 1; kp.y_dt = a->dtype;
   sp.g_in = {a->u, a->u_stride_b, a->in_proj_w, a->in_proj_stride, ws + L.zx_off, L.ldzx,
@@ -254,13 +256,15 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
               d->batch, a->d_model, d->d_inner};
   sp.bar = reinterpret_cast<unsigned *>(ws);
 
-  const int64_t S = (int64_t)d->batch * d->nheads * d->d_state * 4;
+  const int64_t S = (int64_t)d->batch * d->nheads * (mimo ? 1 : d->headdim) * d->d_state * 4;
   add_prefetch(sp, a->out_proj_w, ((int64_t)(a->d_model - 1) * a->out_proj_stride + d->d_inner) * es);
   add_prefetch(sp, a->ssm_state, S);
   add_prefetch(sp, a->bx_prev, S);
   add_prefetch(sp, a->angle_state, (int64_t)d->batch * d->nheads * d->num_rope_angles * 4);
-  add_prefetch(sp, a->mimo_x, (int64_t)d->nheads * R * d->headdim * es);
-  add_prefetch(sp, a->mimo_o, (int64_t)d->nheads * R * d->headdim * es);
+  if (mimo) {
+    add_prefetch(sp, a->mimo_x, (int64_t)d->nheads * R * d->headdim * es);
+    add_prefetch(sp, a->mimo_o, (int64_t)d->nheads * R * d->headdim * es);
+  }
   add_prefetch(sp, a->B_bias, (int64_t)d->nheads * R * d->d_state * es);
   add_prefetch(sp, a->C_bias, (int64_t)d->nheads * R * d->d_state * es);
   add_prefetch(sp, a->B_norm_w, (int64_t)d->d_state * es);
@@ -268,13 +272,14 @@ int step_entry(const m3_dims *d, const m3_step_args *a, m3_stream_t stream) {
   add_prefetch(sp, a->dt_bias, (int64_t)d->nheads * es);
   add_prefetch(sp, a->D, (int64_t)d->nheads * es);
   add_prefetch(sp, a->in_proj_w, ((d_in_proj - 1) * a->in_proj_stride + a->d_model) * es);
-  return launch_status(m3::launch_mimo_step(sp, reinterpret_cast<cudaStream_t>(stream)));
+  return launch_status(mimo ? m3::launch_mimo_step(sp, reinterpret_cast<cudaStream_t>(stream))
+                            : m3::launch_siso_step(sp, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 }  // namespace
 
 namespace m3 {
-int step_validate(const m3_dims *d, const m3_step_args *a, bool *empty) { return step_check(d, a, empty); }
+int step_validate(const m3_dims *d, const m3_step_args *a, bool *empty) { return step_check(d, a, empty, true); }
 }  // namespace m3
 
 extern "C" {
@@ -410,11 +415,20 @@ int m3_residual_rmsnorm(int32_t dtype, const void *x, int64_t ldx, const void *o
 
 int64_t m3_mimo_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32_t dtype) {
   if (!dims) return -(int64_t)M3_ERR_NULL;
-  return step_workspace_bytes(dims, d_model, dtype);
+  return step_workspace_bytes(dims, d_model, dtype, true);
 }
 
 int m3_mimo_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream) {
-  return step_entry(dims, args, stream);
+  return step_entry(dims, args, stream, true);
+}
+
+int64_t m3_siso_step_workspace_bytes(const m3_dims *dims, int32_t d_model, int32_t dtype) {
+  if (!dims) return -(int64_t)M3_ERR_NULL;
+  return step_workspace_bytes(dims, d_model, dtype, false);
+}
+
+int m3_siso_step(const m3_dims *dims, const m3_step_args *args, m3_stream_t stream) {
+  return step_entry(dims, args, stream, false);
 }
 
 int m3_device_error(int reset) {

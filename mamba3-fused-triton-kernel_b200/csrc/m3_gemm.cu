@@ -573,8 +573,9 @@ int64_t pair_workspace_bytes(const PairPlan &p) {
 
 // TF32x3 tile plan: no K split (the fp32 path is taken for batches of
 // several hundred rows and more, which give enough pair tiles); the tile
-// width with the fewest waves x k-tiles, a 256-wide k-tile costing about
-// three times the bf16 one (three products at half the bf16 rate).
+// width with the least waves x k-tiles x per-k-tile time, measured on B200
+// at 1.5x the 128-wide tile's for the 256-wide one (4096 x 5248 x 1024:
+// 213 us at nt 256 in 5 waves, 254 us at nt 128 in 9).
 PairPlan plan_pair_tf32(int M, int N, int K) {
   const int sms = sm_count();
   const int ntm = (M + 2 * kPairBatch - 1) / (2 * kPairBatch);
@@ -584,7 +585,7 @@ PairPlan plan_pair_tf32(int M, int N, int K) {
   for (int nt : {256, 128}) {
     const int ntn = (N + nt - 1) / nt;
     const int waves = (2 * ntn * ntm + sms - 1) / sms;
-    const double cost = waves * ktotal * (0.1 + 0.85 * nt / 256.0);
+    const double cost = waves * ktotal * (nt == 256 ? 1.0 : 0.66);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = {nt, ntn, ntm, ktotal, ktotal, 1, 1};

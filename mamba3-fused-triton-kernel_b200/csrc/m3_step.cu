@@ -28,6 +28,10 @@ cudaError_t launch_mimo_step(StepParams &sp, cudaStream_t stream) {
   return sp.kp.par_dt == M3_BF16 ? launch_mimo_step_bf16(sp, stream) : launch_mimo_step_f32(sp, stream);
 }
 
+cudaError_t launch_siso_step(StepParams &sp, cudaStream_t stream) {
+  return sp.kp.par_dt == M3_BF16 ? launch_siso_step_bf16(sp, stream) : launch_siso_step_f32(sp, stream);
+}
+
 int step_device_error(bool reset) {
   const int a = step_f32_device_error(reset), b = step_bf16_device_error(reset);
   return a < 0 || b < 0 ? -1 : a | b;

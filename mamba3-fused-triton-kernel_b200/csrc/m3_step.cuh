@@ -49,6 +49,10 @@ int step_gemm_cfg(int M, int N, int K, int grid);
 cudaError_t launch_mimo_step(StepParams &sp, cudaStream_t stream);
 cudaError_t launch_mimo_step_f32(StepParams &sp, cudaStream_t stream);
 cudaError_t launch_mimo_step_bf16(StepParams &sp, cudaStream_t stream);
+// The SISO single-launch step (phase 2: one (batch row, head) tile per item).
+cudaError_t launch_siso_step(StepParams &sp, cudaStream_t stream);
+cudaError_t launch_siso_step_f32(StepParams &sp, cudaStream_t stream);
+cudaError_t launch_siso_step_bf16(StepParams &sp, cudaStream_t stream);
 int step_device_error(bool reset);
 // The checks of m3_mimo_step without the launch (M3_OK when it would launch;
 // *empty when the batch has no rows).

@@ -4,6 +4,9 @@
 namespace m3 {
 
 cudaError_t launch_mimo_step_f32(StepParams &sp, cudaStream_t stream) { return launch_step_d<float>(sp, stream); }
+cudaError_t launch_siso_step_f32(StepParams &sp, cudaStream_t stream) {
+  return launch_siso_step_d<float>(sp, stream);
+}
 
 int step_f32_device_error(bool reset) { return device_error_of_this_unit(reset); }
 

@@ -42,6 +42,7 @@
 #include "m3_async.cuh"
 #include "m3_kernels.cuh"
 #include "m3_mimo_row.cuh"
+#include "m3_siso_tile.cuh"
 #include "m3_step.cuh"
 
 namespace m3 {
@@ -338,6 +339,101 @@ __global__ void __launch_bounds__(kStepThreads, 2) mimo_step_kernel(const StepPa
 }
 
 // ---------------------------------------------------------------------------
+// the SISO step kernel
+// ---------------------------------------------------------------------------
+
+// The SISO update of one (batch row, head) tile, whose parameters are in q:
+// state rows of S lanes with FPL float4 columns each (SisoShape), h and Bx
+// read from L2 (prefetched in phase 0) and written back, y_p = sum_d
+// C[d] h[p, d] + D x_p gated by silu(z_p) -- the streamed SISO kernel's
+// arithmetic, operation for operation (src/kernels/utils.py:73-102).
+template <int BD>
+__device__ void siso_tile_update(const KParams &p, const ParBlock &q, int b, int hh, int t) {
+  using Sh = SisoShape<BD>;
+  constexpr int S = Sh::S, FPL = Sh::FPL, RPW = Sh::RPW;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int j = lane % S, slot = warp * RPW + lane / S, nslots = (int)(blockDim.x / 32) * RPW;
+  const int P = p.P, G = p.D / 4;
+  const Coef cf = {q.sS[kDecay], q.sS[kDT], q.sS[kOmt], q.sS[kHtr]};
+  const float dskip = q.sS[kDskip];
+  float *hg = p.h + (size_t)t * P * p.D;
+  float *bg = p.bx + (size_t)t * P * p.D;
+  const int64_t ybase = (int64_t)b * p.y_sb + (int64_t)hh * p.y_sh;
+  for (int rb = 0; rb < P; rb += nslots) {
+    const int row = rb + slot;
+    const bool rok = row < P;
+    const float xp = rok ? q.sX[row] : 0.f;
+    float part = 0.f;
+#pragma unroll
+    for (int f = 0; f < FPL; ++f) {
+      const int col = j + S * f;
+      if (rok && col < G) {
+        const int o = row * G + col;
+        const float4 ho = ld_state4(hg + (size_t)o * 4);
+        const float4 bo = ld_state4(bg + (size_t)o * 4);
+        const float4 Bq = reinterpret_cast<const float4 *>(q.sB)[col];
+        const float4 Cq = reinterpret_cast<const float4 *>(q.sC)[col];
+        float4 bn, hn;
+        bn.x = xp * Bq.x; bn.y = xp * Bq.y; bn.z = xp * Bq.z; bn.w = xp * Bq.w;
+        hn.x = trap_update(cf, bn.x, bo.x, ho.x);
+        hn.y = trap_update(cf, bn.y, bo.y, ho.y);
+        hn.z = trap_update(cf, bn.z, bo.z, ho.z);
+        hn.w = trap_update(cf, bn.w, bo.w, ho.w);
+        part += Cq.x * hn.x;
+        part += Cq.y * hn.y;
+        part += Cq.z * hn.z;
+        part += Cq.w * hn.w;
+        st_state4(hg + (size_t)o * 4, hn);
+        st_state4(bg + (size_t)o * 4, bn);
+      }
+    }
+    part = group_sum<S>(part);
+    if (j == 0 && rok) st_any(p.y, ybase + (int64_t)row * p.y_sp, (part + dskip * xp) * q.sG[row], p.y_dt);
+  }
+}
+
+// The single-launch step of a SISO layer: phase 1 in_proj, grid barrier,
+// phase 2 one (batch row, head) tile per work item (its parameters, then its
+// P x D state), grid barrier, phase 3 out_proj.  A tile is never split over
+// CTAs: its accumulated angles are read and rewritten by the one CTA.
+template <int BD, typename T>
+__global__ void __launch_bounds__(kStepThreads, 2) siso_step_kernel(const StepParams sp) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ int s_flag;
+  const KParams &p = sp.kp;
+  unsigned base = 0;
+  if (threadIdx.x == 0) base = ld_relaxed(sp.bar);
+
+  prefetch_ranges(sp);
+
+  gemm_phase<T, false>(sp.cfg_in, sp.g_in, NoPre{});
+
+  bool ok = grid_barrier(sp.bar, base + gridDim.x, &s_flag);
+  const ParBlock q = par_block<BD>(reinterpret_cast<unsigned char *>(smem), p);
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
+    q.dtb[i] = ld_any(p.dt_bias, i, p.par_dt);
+    q.dsk[i] = ld_any(p.Dp, i, p.par_dt);
+  }
+  for (int i = threadIdx.x; i < p.D; i += blockDim.x) {
+    q.wB[i] = ld_any(p.wB, i, p.par_dt);
+    q.wC[i] = ld_any(p.wC, i, p.par_dt);
+  }
+  __syncthreads();
+  const int ntiles = p.B * p.H;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int b = t / p.H, hh = t - b * p.H;
+    tile_params_global<BD, true>(p, q, b, hh, t);
+    __syncthreads();
+    siso_tile_update<BD>(p, q, b, hh, t);
+    __syncthreads();  // the next tile reuses the parameter block
+  }
+
+  // barrier 2 inside the first out_proj tile, once its weights are in flight
+  gemm_phase<T, true>(sp.cfg_out, sp.g_out, BarrierPre{sp.bar, base + 2 * gridDim.x, &s_flag, &ok});
+  if (blockIdx.x == 0 && threadIdx.x == 0) sp.bar[0] = base + 2 * gridDim.x;
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -407,6 +503,57 @@ cudaError_t launch_step_r(StepParams &sp, cudaStream_t stream) {
     case 8: return launch_step_p<BD, 8, T>(sp, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+size_t siso_step_smem_bytes(int BD, int P, int H) {
+  int f = 2 * BD + 2 * P + kNScalar + 2 * BD + 2 * H;
+  for (int c = 0; c < kStepGemmCfgs; ++c) {
+    const int g = step_gemm_smem_floats(kCfgKS[c], kCfgKW[c]);
+    f = g > f ? g : f;
+  }
+  return (size_t)f * sizeof(float);
+}
+
+template <int BD, typename T>
+cudaError_t launch_siso_step_t(StepParams &sp, cudaStream_t stream) {
+  auto kern = siso_step_kernel<BD, T>;
+  const size_t smem = siso_step_smem_bytes(BD, sp.kp.P, sp.kp.H);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  static LaunchCache cache;
+  cudaError_t e = ensure_smem_optin(cache, kern, 200 * 1024);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = occupancy_per_sm(cache, kern, kStepThreads, smem, &per_sm);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  if (per_sm > 2) per_sm = 2;
+  const int grid = num_sms_current() * per_sm;
+  sp.rows_per_item = 1;
+  sp.n_items = sp.kp.B * sp.kp.H;
+  sp.cfg_in = step_gemm_cfg(sp.g_in.M, sp.g_in.N, sp.g_in.K, grid);
+  sp.cfg_out = step_gemm_cfg(sp.g_out.M, sp.g_out.N, sp.g_out.K, grid);
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, sp);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_siso_step_d(StepParams &sp, cudaStream_t stream) {
+  if (sp.kp.D <= 32) return launch_siso_step_t<32, T>(sp, stream);
+  if (sp.kp.D <= 64) return launch_siso_step_t<64, T>(sp, stream);
+  if (sp.kp.D <= 128) return launch_siso_step_t<128, T>(sp, stream);
+  return launch_siso_step_t<256, T>(sp, stream);
 }
 
 // d_state <= 32 runs the 32-wide instantiation (the row code masks columns

@@ -128,6 +128,10 @@ def load(path: str = LIB_PATH):
         lib.m3_mimo_step_workspace_bytes.restype = c_int64
         lib.m3_mimo_step.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
         lib.m3_mimo_step.restype = c_int
+        lib.m3_siso_step_workspace_bytes.argtypes = [POINTER(Dims), c_int32, c_int32]
+        lib.m3_siso_step_workspace_bytes.restype = c_int64
+        lib.m3_siso_step.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
+        lib.m3_siso_step.restype = c_int
         lib.m3_mimo_step_static.argtypes = [POINTER(Dims), POINTER(StepArgs), c_void_p]
         lib.m3_mimo_step_static.restype = c_int
         lib.m3_device_error.argtypes = [c_int]

@@ -63,9 +63,16 @@ SINGLE_LAUNCH_MAX_BATCH = 256
 SINGLE_LAUNCH_MAX_FLOP = {torch.float32: 3e8, torch.bfloat16: 1.5e8}
 
 
-def single_launch_preferred(model, batch: int) -> bool:
+def single_launch_preferred(model, batch: int, graph: bool = False) -> bool:
     """Whether the decoder uses the single-launch step for this layer and
-    batch (when the kernel takes the layer at all)."""
+    batch (when the kernel takes the layer at all); ``graph``: for a step
+    captured in a CUDA graph.  A SISO layer takes its single launch in eager
+    steps only: there one launch saves the host time of two (19 against 59 us
+    a step for the d256 layer on B200), while replayed from a graph its three
+    launches measured faster (18.9 against 24.6 us), the single launch's
+    state phase waiting on one CTA per (batch row, head) tile."""
+    if not model.is_mimo and graph:
+        return False
     flop = 2.0 * batch * model.d_model * (model.d_in_proj + model.d_inner)
     limit = SINGLE_LAUNCH_MAX_FLOP.get(model.in_proj.weight.dtype, 0.0)
     return batch <= SINGLE_LAUNCH_MAX_BATCH and flop <= limit
@@ -307,17 +314,18 @@ class Mamba3Decoder:
         self._fused_cache = (key, launch)
         return launch
 
-    def _single_launch(self, state: dict):
+    def _single_launch(self, state: dict, graph: bool = False):
         """Prepared single-launch step for this state and the current
-        weights, or None where the kernel does not take the layer; rebuilt
-        when a weight or parameter changes or another state is passed."""
+        weights, or None where the kernel does not take the layer (or, with
+        ``graph``, is not used in a captured step); rebuilt when a weight or
+        parameter changes, another state is passed or the mode changes."""
         m = self.model
         ts = [m.in_proj.weight, m.out_proj.weight] + [p for p in self._param_list() if p is not None]
         key = (tuple((t.data_ptr(), t._version, t.dtype) for t in ts),
                tuple((t.data_ptr(), tuple(t.shape)) for t in
-                     (state["ssm_state"], state["bx_prev"], state["angle_state"])))
+                     (state["ssm_state"], state["bx_prev"], state["angle_state"])), graph)
         if self._step_cache is None or self._step_cache[0] != key:
-            use = single_launch_preferred(m, state["ssm_state"].shape[0])
+            use = single_launch_preferred(m, state["ssm_state"].shape[0], graph)
             self._step_cache = (key, prepare_decode_step(m, state) if use else None)
         return self._step_cache[1]
 
@@ -328,7 +336,7 @@ class Mamba3Decoder:
         ``use_single_launch`` the three run as one kernel where it applies."""
         m = self.model
         if self.use_single_launch:
-            launch = self._single_launch(state)
+            launch = self._single_launch(state, torch.cuda.is_current_stream_capturing())
             if launch is not None and launch.accepts(u):
                 return launch.run(u), state
         zx = linear(u, m.in_proj.weight)

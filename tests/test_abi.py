@@ -31,7 +31,7 @@ def _declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 21, names
+    assert len(names) == 23, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
@@ -225,6 +225,25 @@ def test_step_workspace_size_and_range():
             setattr(d2, k, v)
         assert lib.m3_mimo_step_workspace_bytes(d2, 256, 0) == -nat.M3_ERR_UNSUPPORTED, kw
     assert lib.m3_mimo_step_workspace_bytes(dims, 254, 0) == -nat.M3_ERR_UNSUPPORTED
+
+
+def test_siso_step_workspace_size_and_range():
+    lib = nat.load()
+    # the reference's SISO d256 layer: 16 heads x headdim 32, d_state 64
+    dims = nat.Dims(batch=4, nheads=16, headdim=32, d_state=64, mimo_rank=1, num_rope_angles=16, ngroups=1,
+                    d_inner=512, A_floor=1e-4)
+    d_in_proj = 2 * 512 + 2 * 64 + 3 * 16 + 16
+    expect = 256 + -(-4 * d_in_proj * 4 // 256) * 256 + -(-4 * 512 * 4 // 256) * 256
+    assert lib.m3_siso_step_workspace_bytes(dims, 256, nat.M3_F32) == expect
+    # heads need not be a multiple of 8, and d_state 256 / headdim 256 are taken
+    for kw in [dict(nheads=4, d_inner=128), dict(headdim=256, nheads=2, d_inner=512),
+               dict(d_state=256, num_rope_angles=64)]:
+        d2 = nat.Dims(**{**{f: getattr(dims, f) for f, _ in nat.Dims._fields_}, **kw})
+        assert lib.m3_siso_step_workspace_bytes(d2, 256, 0) > 0, kw
+    d2 = nat.Dims(**{**{f: getattr(dims, f) for f, _ in nat.Dims._fields_}, "mimo_rank": 4})
+    assert lib.m3_siso_step_workspace_bytes(d2, 256, 0) == -nat.M3_ERR_SHAPE
+    assert lib.m3_siso_step_workspace_bytes(dims, 254, 0) == -nat.M3_ERR_UNSUPPORTED
+    assert lib.m3_siso_step_workspace_bytes(None, 256, 0) == -nat.M3_ERR_NULL
 
 
 def test_step_validation():
