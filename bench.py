@@ -470,9 +470,20 @@ def fused_kernel_roofline(h: Harness, kw: dict, batch: int, dtype_name: str, n: 
 # the stack's projections alone: 24 layers of in_proj (9440 x 2048) and
 # out_proj (2048 x 4096), bf16, batch 256, in one CUDA graph, timed for the
 # library's tcgen05 GEMM (m3_linear_bf16) and for cuBLAS
-PROJECTIONS = {"proj24_d2048_b256_bf16": 24}
+PROJECTIONS = {"proj24_d2048_b256_bf16": 24, "proj24_d2048_b32_bf16": 24, "proj24_d2048_b8_bf16": 24,
+               "proj24_d2048_b1_bf16": 24}
 WORKLOADS["proj24_d2048_b256_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 256,
                                        "bf16")
+# the same projections at one GPU's share of the stack's batch 256 under
+# strong scaling over 8 GPUs (32 rows), and at small-batch decodes (8 rows,
+# 1 row), where the weight-streaming kernel (m3_linear_bf16_skinny) is timed
+# as well
+WORKLOADS["proj24_d2048_b32_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 32,
+                                      "bf16")
+WORKLOADS["proj24_d2048_b8_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 8,
+                                     "bf16")
+WORKLOADS["proj24_d2048_b1_bf16"] = (dict(d_model=2048, d_state=128, headdim=64, is_mimo=True, mimo_rank=4), 1,
+                                     "bf16")
 
 
 # fused-kernel rooflines added to the default run at N=1: the wide SISO layer
@@ -647,12 +658,14 @@ def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, loc
     d_model) and out_proj (d_model x d_inner) with their own bf16 weights,
     all layers in one CUDA graph, replayed without an L2 flush (the 1.3 GB
     of weights stream from HBM anyway); timed for the library's tcgen05 GEMM
-    (m3_linear_bf16) and for cuBLAS.  `value` is the library GEMM's rate in
-    tokens/s (batch x steps / time); the per-layer times and the FLOP rates
-    of both are beside it."""
+    (m3_linear_bf16), for the weight-streaming kernel
+    (m3_linear_bf16_skinny) when a rank's batch is at most 64 rows, and for
+    cuBLAS.  `value` is the rate in tokens/s (batch x steps / time) of the
+    faster library kernel; the per-layer times, FLOP rates and weight-stream
+    bandwidths of all of them are beside it."""
     import torch.nn.functional as F
 
-    from src.kernels.linear import linear_bf16
+    from src.kernels.linear import SKINNY_MAX_M, linear_bf16, linear_bf16_skinny
     from src.models.mamba3 import Mamba3
 
     h = Harness(world, rank, local)
@@ -667,6 +680,11 @@ def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, loc
     y = torch.randn(batch, k_out, device=dev).bfloat16()
     ref = (x.double() @ w_in[0].double().T)
     err = float((linear_bf16(x, w_in[0], torch.float32).double() - ref).abs().max())
+    impls = [("m3_linear_bf16", lambda a, b: linear_bf16(a, b))]
+    if batch <= SKINNY_MAX_M:
+        err = max(err, float((linear_bf16_skinny(x, w_in[0], torch.float32).double() - ref).abs().max()))
+        impls.append(("m3_linear_bf16_skinny", lambda a, b: linear_bf16_skinny(a, b)))
+    impls.append(("cublas", F.linear))
 
     def chain(lin):
         def f():
@@ -680,7 +698,7 @@ def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, loc
     h.clocks_start()
     h.barrier()
     h.clocks_mark()
-    for name, lin in (("m3_linear_bf16", lambda a, b: linear_bf16(a, b)), ("cublas", F.linear)):
+    for name, lin in impls:
         g = h.graphed(chain(lin), warm=max(W, 1))
         ms = h.timed_loop(lambda i: g.replay(), K)
         del g
@@ -691,18 +709,21 @@ def run_projections(args, kw, global_batch, dtype_name, layers, world, rank, loc
     h.close()
     if rank == 0:
         flop = 2.0 * batch * layers * (n_in * k_in + n_out * k_out)
+        wbytes = 2.0 * layers * (n_in * k_in + n_out * k_out)
         per = {k: round(v / layers * 1000.0, 2) for k, v in results.items()}
+        best = min((k for k in results if k != "cublas"), key=lambda k: results[k])
         line = {
-            "metric": "projection tokens/s", "value": round(global_batch / (results["m3_linear_bf16"] * 1e-3), 1),
-            "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(results["m3_linear_bf16"], 5), "higher_is_better": True, "scaling": "strong",
+            "metric": "projection tokens/s", "value": round(global_batch / (results[best] * 1e-3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "impl_timed": best,
+            "ms_per_step": round(results[best], 5), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**config_dict(args.workload, kw, global_batch, world, dtype_name), "layers": layers,
                        "step": "24 x (in_proj, out_proj) GEMMs in one CUDA graph, no L2 flush (weights > L2)"},
             "us_per_layer": per,
             "tflops": {k: round(flop / (v * 1e-3) / 1e12, 1) for k, v in results.items()},
+            "weight_gbs": {k: round(wbytes / (v * 1e-3) / 1e9, 1) for k, v in results.items()},
             "max_abs_err_vs_float64": err,
-            "gpu_launches": K * 2 * layers,
+            "gpu_launches": K * 2 * layers * (len(results) - 1),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -203,6 +203,19 @@ int64_t m3_linear_bf16_workspace_bytes(int32_t M, int32_t N, int32_t K);
 int m3_linear_f32_tc(const float *A_hi, const float *A_lo, int64_t lda, const float *W_hi, const float *W_lo,
                      int64_t ldw, float *C, int64_t ldc, int32_t M, int32_t N, int32_t K, m3_stream_t stream);
 
+/* bf16 linear layer of the decode step's projections for small decode
+ * batches (M <= 64 rows: a GPU's share of a strongly scaled batch, or a
+ * single-stream decode), same operation and call sites as m3_linear_bf16.
+ * At these sizes the call is a stream of the weight, which this kernel reads
+ * once from HBM through the tensor cores (mma.sync bf16, fp32 accumulation;
+ * K split across the warps of a CTA and summed in a fixed order, so results
+ * are deterministic).  A: (M, K) bf16 row stride lda, W: (N, K) bf16 row
+ * stride ldw, C: (M, N) row stride ldc in c_dtype (M3_BF16 rounded to
+ * nearest, or M3_F32).  A and W 16-byte aligned; K, lda, ldw multiples of 8;
+ * C 4-byte aligned.  M3_ERR_SHAPE for M > 64.  No workspace. */
+int m3_linear_bf16_skinny(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
+                          int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream);
+
 /* The operand split m3_linear_f32_tc takes: hi = x with the 13 low mantissa
  * bits cleared (exactly a TF32 value), lo = x - hi (exact in fp32).
  * x: (rows, cols) row stride ldx; hi, lo: row stride ld; 16-byte aligned,

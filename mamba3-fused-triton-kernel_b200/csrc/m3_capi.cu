@@ -12,7 +12,7 @@ namespace {
 
 using m3::KParams;
 
-constexpr int kVersion = 10300;  // 1.3.0
+constexpr int kVersion = 10400;  // 1.4.0
 constexpr int kMaxHeaddim = 4096;
 
 bool dtype_ok(int32_t dt) { return dt == M3_F32 || dt == M3_BF16; }
@@ -383,6 +383,22 @@ int m3_linear_f32_tc(const float *A_hi, const float *A_lo, int64_t lda, const fl
   if (st != M3_OK) return st;
   if (!m3::gemm_tf32x3_supported(A_hi, A_lo, lda, W_hi, W_lo, ldw, C, ldc, M, N, K)) return M3_ERR_UNSUPPORTED;
   return launch_status(m3::launch_gemm_tf32x3(A_hi, A_lo, lda, W_hi, W_lo, ldw, C, ldc, M, N, K,
+                                              reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int m3_linear_bf16_skinny(const void *A, int64_t lda, const void *W, int64_t ldw, void *C, int64_t ldc, int32_t M,
+                          int32_t N, int32_t K, int32_t c_dtype, m3_stream_t stream) {
+  if (!A || !W || !C) return M3_ERR_NULL;
+  if (!dtype_ok(c_dtype)) return M3_ERR_DTYPE;
+  if (M < 0 || M > m3::kSkinnyMaxRows || N <= 0 || K <= 0 || lda < K || ldw < K || ldc < N) return M3_ERR_SHAPE;
+  if (K % 8 || lda % 8 || ldw % 8) return M3_ERR_ALIGN;
+  if (!aligned16(A) || !aligned16(W) || (reinterpret_cast<uintptr_t>(C) & 3u)) return M3_ERR_ALIGN;
+  if (c_dtype == M3_BF16 && (reinterpret_cast<uintptr_t>(C) & 1u)) return M3_ERR_ALIGN;
+  if (M == 0) return M3_OK;
+  const int st = check_device();
+  if (st != M3_OK) return st;
+  if (!m3::gemm_skinny_supported(A, lda, W, ldw, C, ldc, M, N, K)) return M3_ERR_UNSUPPORTED;
+  return launch_status(m3::launch_gemm_skinny(A, lda, W, ldw, C, ldc, M, N, K, c_dtype == M3_BF16,
                                               reinterpret_cast<cudaStream_t>(stream)));
 }
 

@@ -519,6 +519,13 @@ cudaError_t launch_gemm_tf32x3(const float *x, const float *xl, int64_t ldx, con
                                int64_t ldw, float *y, int64_t ldy, int M, int N, int K, cudaStream_t stream);
 cudaError_t launch_tf32_split(const float *x, int64_t ldx, float *hi, float *lo, int64_t ld, int rows, int cols,
                               cudaStream_t stream);
+// The skinny bf16 GEMM for decode batches of up to kSkinnyMaxRows rows
+// (m3_skinny.cu): y = x . w^T, weight streamed once through mma.sync.
+constexpr int kSkinnyMaxRows = 64;
+bool gemm_skinny_supported(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *y, int64_t ldy, int M,
+                           int N, int K);
+cudaError_t launch_gemm_skinny(const void *x, int64_t ldx, const void *w, int64_t ldw, void *y, int64_t ldy, int M,
+                               int N, int K, bool y_bf16, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(int dtype, const void *x, const void *o, const float *w, void *x_out, void *xn,
                                     int M, int N, int64_t ldx, int64_t ldo, int64_t ldxo, int64_t ldn, float eps,

@@ -116,6 +116,9 @@ def load(path: str = LIB_PATH):
         lib.m3_linear_f32_tc.restype = c_int
         lib.m3_split_tf32.argtypes = [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]
         lib.m3_split_tf32.restype = c_int
+        lib.m3_linear_bf16_skinny.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                              c_int32, c_int32, c_int32, c_int32, c_void_p]
+        lib.m3_linear_bf16_skinny.restype = c_int
         lib.m3_mimo_prefill.argtypes = [POINTER(Dims), POINTER(FullArgs), c_int32, c_void_p]
         lib.m3_mimo_prefill.restype = c_int
         lib.m3_siso_prefill.argtypes = [POINTER(Dims), POINTER(FullArgs), c_int32, c_void_p]

@@ -6,13 +6,16 @@ decode regime -- run the library's ``m3_linear_f32`` kernel; larger fp32
 batches run the library's split-precision tensor-core GEMM
 (``m3_linear_f32_tc``: each operand split into a TF32 head and remainder,
 three tcgen05 kind::tf32 products per k step, about fp32 accuracy; the
-weight's split is computed once and cached); with ``TC_ROUTE`` set, bf16
-batches up to ``TC_MAX_M`` rows run the library's tcgen05 GEMM
-(``m3_linear_bf16``: pairs of SMs sharing each batch tile,
-``cta_group::2``); everything else uses cuBLAS through
-``torch.nn.functional.linear``.  ``TC_ROUTE`` is off: at the decode shapes
-measured on B200 cuBLAS is faster (24 layers of in_proj + out_proj at
-batch 256, d_model 2048: 473 us against 860 us).
+weight's split is computed once and cached); bf16 batches of up to
+``SKINNY_ROUTE_M`` rows run the library's weight-streaming kernel
+(``m3_linear_bf16_skinny``: 24 layers of the d_model 2048 stack's in_proj +
+out_proj at 8 rows in 16.4 us a layer against cuBLAS's 21.1 us on B200;
+from 32 rows cuBLAS is faster); with ``TC_ROUTE`` set, bf16 batches up to
+``TC_MAX_M`` rows run the library's tcgen05 GEMM (``m3_linear_bf16``: pairs
+of SMs sharing each batch tile, ``cta_group::2``); everything else uses
+cuBLAS through ``torch.nn.functional.linear``.  ``TC_ROUTE`` is off: at the
+decode shapes measured on B200 cuBLAS is faster (24 layers of in_proj +
+out_proj at batch 256, d_model 2048: 473 us against 860 us).
 """
 
 from __future__ import annotations
@@ -28,6 +31,8 @@ SMALL_M_MAX = 256  # batch rows up to which the latency-optimised kernel is used
 TC_MAX_M = 512     # bf16 batch rows up to which TC_ROUTE uses the tcgen05 GEMM
 TC_ROUTE = False   # route bf16 projections to m3_linear_bf16 (off: cuBLAS is faster at the decode shapes)
 TF32X3_ROUTE = True  # route fp32 batches above SMALL_M_MAX rows to m3_linear_f32_tc
+SKINNY_MAX_M = 64    # bf16 batch rows up to which m3_linear_bf16_skinny applies
+SKINNY_ROUTE_M = 16  # bf16 batch rows up to which linear() routes to it (cuBLAS is faster above)
 
 
 def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
@@ -40,6 +45,14 @@ def uses_small_m_kernel(x: torch.Tensor, weight: torch.Tensor) -> bool:
 def uses_tc_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
     return (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype == torch.bfloat16
             and weight.dtype == torch.bfloat16 and 0 < x.shape[0] <= TC_MAX_M and x.shape[1] >= 64
+            and x.shape[1] % 8 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
+            and weight.stride(1) == 1 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
+
+
+def uses_skinny_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    return (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype == torch.bfloat16
+            and weight.dtype == torch.bfloat16 and 0 < x.shape[0] <= SKINNY_MAX_M and x.shape[1] > 0
             and x.shape[1] % 8 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
             and weight.stride(1) == 1 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)
@@ -140,8 +153,26 @@ def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16)
     return out
 
 
+def linear_bf16_skinny(x: torch.Tensor, weight: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """``x @ weight.T`` for a bf16 batch of at most SKINNY_MAX_M rows on the
+    weight-streaming kernel (fp32 accumulation, output rounded to
+    ``out_dtype``)."""
+    M, K = x.shape
+    N = weight.shape[0]
+    out = torch.empty(M, N, device=x.device, dtype=out_dtype)
+    code = nat.M3_BF16 if out_dtype == torch.bfloat16 else nat.M3_F32
+    with nat.device_guard(x.device):
+        st = nat.load().m3_linear_bf16_skinny(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+                                              out.data_ptr(), out.stride(0), M, N, K, code,
+                                              nat.stream_handle(x.device))
+    nat.check(st, "m3_linear_bf16_skinny")
+    return out
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """``x @ weight.T`` for x (M, K), weight (N, K)."""
+    if x.dim() == 2 and x.shape[0] <= SKINNY_ROUTE_M and uses_skinny_bf16(x, weight):
+        return linear_bf16_skinny(x, weight)
     if TC_ROUTE and uses_tc_bf16(x, weight):
         return linear_bf16(x, weight)
     if TF32X3_ROUTE and uses_tf32x3(x, weight):

@@ -31,13 +31,13 @@ def _declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = nat.load()
     names = _declared_functions()
-    assert len(names) == 23, names
+    assert len(names) == 24, names
     for n in names:
         assert hasattr(lib, n), f"{n} not exported"
     out = subprocess.run(["nm", "-D", "--defined-only", nat.LIB_PATH], capture_output=True, text=True)
     exported = set(re.findall(r"\bT (m3_\w+)", out.stdout))
     assert set(names) <= exported
-    assert lib.m3_version() == 10300
+    assert lib.m3_version() == 10400
     assert nat.status_string(nat.M3_ERR_RANK).startswith("unsupported mimo_rank")
 
 

@@ -45,6 +45,10 @@ def test_dispatch_outside_the_small_batch_regime():
     xb = torch.randn(8, 128, device="cuda").bfloat16()
     assert not uses_small_m_kernel(xb, w.bfloat16())
     torch.testing.assert_close(linear(xb, w.bfloat16()), xb @ w.bfloat16().T)
+    # bf16 batches of up to SKINNY_ROUTE_M rows take the weight-streaming kernel
+    from src.kernels import linear as lin
+    assert 8 <= lin.SKINNY_ROUTE_M and uses_skinny_bf16(xb, w.bfloat16())
+    assert torch.equal(linear(xb, w.bfloat16()), lin.linear_bf16_skinny(xb, w.bfloat16()))
     odd = torch.randn(8, 130, device="cuda")
     assert not uses_small_m_kernel(odd, torch.randn(4, 130, device="cuda"))
 
@@ -155,4 +159,71 @@ def test_tf32x3_strided_rows_and_weight_cache():
             break
         del w2
     from src import _native as nat
+    assert nat.device_error() == 0
+
+
+# ---- bf16 projections of small batches: weight-streaming kernel ----
+
+from src.kernels.linear import SKINNY_MAX_M, linear_bf16_skinny, uses_skinny_bf16  # noqa: E402
+
+SKINNY_SHAPES = [  # M, N, K: the d2048 stack's in_proj / out_proj at 1..64 rows, tails in N and K
+    (1, 9440, 2048), (8, 2048, 4096), (16, 9440, 2048), (17, 2048, 4096), (32, 9440, 2048), (32, 2048, 4096),
+    (33, 1000, 1000), (48, 300, 136), (64, 9440, 2048), (64, 2048, 4096), (5, 7, 8), (64, 129, 4104),
+    (3, 520, 24),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SKINNY_SHAPES)
+def test_skinny_bf16_matches_float64(M, N, K):
+    """bf16 products are exact in fp32, so the error is the fp32
+    accumulation's (the same bound as the tcgen05 GEMM's); the bf16 output
+    is the rounded fp32 output."""
+    g = torch.Generator(device="cuda").manual_seed(3 * M + 7 * N + 13 * K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    assert uses_skinny_bf16(x, w)
+    ref = x.double() @ w.double().T
+    y32 = linear_bf16_skinny(x, w, torch.float32)
+    err = (y32.double() - ref).abs().max().item()
+    assert err <= 2e-6 * K ** 0.5 * max(1.0, ref.abs().max().item()), err
+    y = linear_bf16_skinny(x, w)
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    assert torch.equal(y, y32.bfloat16()), "bf16 output is not the rounded fp32 result"
+    assert torch.equal(linear_bf16_skinny(x, w, torch.float32), y32), "not deterministic"
+
+
+def test_skinny_bf16_strided_rows_and_output():
+    xb = torch.randn(40, 264, device="cuda").bfloat16()
+    wb = (torch.randn(200, 272, device="cuda") * 0.05).bfloat16()
+    x, w = xb[:, :256], wb[:, :256]
+    assert uses_skinny_bf16(x, w)
+    ref = x.double() @ w.double().T
+    torch.testing.assert_close(linear_bf16_skinny(x, w, torch.float32).double(), ref, rtol=0, atol=1e-4)
+    # an output with a row stride wider than N (columns 200..207 untouched)
+    from src import _native as nat
+    out = torch.full((40, 208), 7.0, device="cuda")
+    with nat.device_guard(x.device):
+        st = nat.load().m3_linear_bf16_skinny(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                                              208, 40, 200, 256, nat.M3_F32, nat.stream_handle(x.device))
+    nat.check(st, "m3_linear_bf16_skinny")
+    torch.testing.assert_close(out[:, :200].double(), ref, rtol=0, atol=1e-4)
+    assert (out[:, 200:] == 7.0).all()
+
+
+def test_skinny_bf16_rejects():
+    from src import _native as nat
+    lib = nat.load()
+    x = torch.randn(SKINNY_MAX_M + 1, 128, device="cuda").bfloat16()
+    w = torch.randn(64, 128, device="cuda").bfloat16()
+    y = torch.empty(SKINNY_MAX_M + 1, 64, device="cuda")
+    assert not uses_skinny_bf16(x, w)
+    s = nat.stream_handle(x.device)
+    assert lib.m3_linear_bf16_skinny(x.data_ptr(), 128, w.data_ptr(), 128, y.data_ptr(), 64, SKINNY_MAX_M + 1, 64,
+                                     128, nat.M3_F32, s) == nat.M3_ERR_SHAPE
+    assert lib.m3_linear_bf16_skinny(x.data_ptr(), 128, w.data_ptr(), 128, y.data_ptr(), 64, 4, 64, 124,
+                                     nat.M3_F32, s) == nat.M3_ERR_ALIGN
+    assert lib.m3_linear_bf16_skinny(x.data_ptr() + 2, 128, w.data_ptr(), 128, y.data_ptr(), 64, 4, 64, 120,
+                                     nat.M3_F32, s) == nat.M3_ERR_ALIGN
+    assert lib.m3_linear_bf16_skinny(x.data_ptr(), 128, w.data_ptr(), 128, y.data_ptr(), 64, 0, 64, 128,
+                                     nat.M3_F32, s) == nat.M3_OK
     assert nat.device_error() == 0
