@@ -1056,6 +1056,68 @@ def run_layer(args, kw, global_batch, dtype_name, world, rank, local):
     dec._cuda_graph = None
 
 
+def run_sweep(args, kw, dtype_name, world, rank, local):
+    """The throughput sweep of one layer (the reference's
+    benchmarks/run_bench_extended.py --batch-sizes / --mimo-rank): for every
+    MIMO rank and batch size, the workload's layer with that rank decoded
+    through Mamba3Decoder's captured graph (full-fused path), L2 flushed
+    before every timed step.  One JSON line: per point the step's mean and
+    p50 / p99 ms and tokens/s (batch x steps / time).  One GPU."""
+    from src.models.inference import Mamba3Decoder
+    from src.models.mamba3 import Mamba3
+
+    if world != 1:
+        if rank == 0:
+            print(json.dumps({"metric": "decode tokens/s sweep", "unavailable": "the sweep runs on one GPU"}))
+        return
+    h = Harness(world, rank, local)
+    dev = h.dev
+    wdtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    ranks = [int(r) for r in args.mimo_ranks.split(",")]
+    batches = [int(b) for b in args.batch_sizes.split(",")]
+    K, W = args.steps, args.warmup
+    points = []
+    h.clocks_start()
+    h.clocks_mark()
+    for R in ranks:
+        lkw = dict(kw, is_mimo=True, mimo_rank=R)
+        torch.manual_seed(0)
+        model = Mamba3(**lkw, device=dev, dtype=wdtype)
+        with torch.no_grad():
+            model.in_proj.weight.normal_(0.0, 0.02)
+            model.out_proj.weight.normal_(0.0, 0.02)
+        for B in batches:
+            gen = torch.Generator(device="cpu").manual_seed(1)
+            u_dev = torch.randn(8, B, model.d_model, generator=gen).to(wdtype).to(dev)
+            dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+            state = dec.init_state(B, device=dev)
+            with torch.no_grad():
+                dec.warmup_cuda_graph(state, n_warmup=3)
+                for i in range(W):
+                    dec.step(u_dev[i % 8], state)
+                ms = h.timed_loop(lambda i: dec.step(u_dev[i % 8], state), K)
+            single = dec._step_cache is not None and dec._step_cache[1] is not None
+            points.append({"mimo_rank": R, "batch": B, "ms_per_step": round(float(ms.mean()), 5),
+                           "p50_ms": round(float(np.percentile(ms, 50)), 5),
+                           "p99_ms": round(float(np.percentile(ms, 99)), 5),
+                           "tokens_per_s": round(B * K / (float(ms.sum()) / 1000.0), 1),
+                           "path": "single launch" if single else "in_proj + fused kernel + out_proj"})
+            dec._cuda_graph = None
+            del dec, state
+            torch.cuda.synchronize(dev)
+    h.clocks_mark()
+    clocks = h.clocks_stop()
+    h.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tokens/s sweep", "unit": "tokens/s", "n_gpus": 1, "steps": K, "warmup": W,
+            "higher_is_better": True, "dtype": dtype_name, "data": "synthetic",
+            "config": {**{k: v for k, v in kw.items() if k != "mimo_rank"}, "weights": dtype_name, "state": "f32",
+                       "l2": "flushed (256 MiB write) before every timed step; per-step CUDA events",
+                       "step": "CUDA-graph replay of Mamba3Decoder.step (full-fused path)"},
+            "points": points, "clocks": clocks}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1066,6 +1128,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of reference CPU timing")
     ap.add_argument("--no-fused-rooflines", dest="fused_rooflines", action="store_false",
                     help="skip the extra fused-kernel rooflines of the default run")
+    ap.add_argument("--sweep", action="store_true",
+                    help="throughput sweep of the workload's layer over --batch-sizes and --mimo-ranks (one GPU)")
+    ap.add_argument("--batch-sizes", default="1,8,32,128,512,1024,4096")
+    ap.add_argument("--mimo-ranks", default="1,2,4,8")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1074,7 +1140,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     kw, global_batch, dtype_name = WORKLOADS[args.workload]
 
-    if args.impl == "reference":
+    if args.sweep:
+        if args.impl == "reference" or args.workload in STACKS or args.workload in PREFILLS or \
+                args.workload in PROJECTIONS or args.workload in SSM_WORKLOADS:
+            raise SystemExit("--sweep takes a single-layer workload and the native implementation")
+        run_sweep(args, kw, dtype_name, world, rank, local)
+    elif args.impl == "reference":
         run_reference(args, kw, global_batch, dtype_name, rank)
     elif args.workload in STACKS:
         run_stack(args, kw, global_batch, dtype_name, STACKS[args.workload], world, rank, local)

@@ -3,7 +3,8 @@
 ``linear(x, weight)`` computes ``x @ weight.T`` (``nn.Linear`` without bias,
 src/models/mamba3.py:115,158).  Small fp32 batches -- the latency-bound
 decode regime -- run the library's ``m3_linear_f32`` kernel; larger fp32
-batches run the library's split-precision tensor-core GEMM
+batches (on large layers from a few dozen rows) run the library's
+split-precision tensor-core GEMM
 (``m3_linear_f32_tc``: each operand split into a TF32 head and remainder,
 three tcgen05 kind::tf32 products per k step, about fp32 accuracy; the
 weight's split is computed once and cached); bf16 batches of up to
@@ -30,7 +31,15 @@ from src import _native as nat
 SMALL_M_MAX = 256  # batch rows up to which the latency-optimised kernel is used
 TC_MAX_M = 512     # bf16 batch rows up to which TC_ROUTE uses the tcgen05 GEMM
 TC_ROUTE = False   # route bf16 projections to m3_linear_bf16 (off: cuBLAS is faster at the decode shapes)
-TF32X3_ROUTE = True  # route fp32 batches above SMALL_M_MAX rows to m3_linear_f32_tc
+TF32X3_ROUTE = True  # route large fp32 projections to m3_linear_f32_tc
+# fp32 batches of at most SMALL_M_MAX rows also take m3_linear_f32_tc on
+# large layers (K and N >= 1024) once M x N reaches TF32X3_MIN_WORK and M
+# TF32X3_MIN_ROWS: measured on B200 for the d_model 1024 layer, in_proj
+# (N 4224-6272, K 1024) at 32 rows 30.7 against 41.0 us on the small-batch
+# kernel and at 128 rows 34.8 against 116.7 us; out_proj (N 1024, K 2048)
+# at 128 rows 49.2 against 53.3 us, at 64 rows 47.1 against 28.7 us
+TF32X3_MIN_ROWS = 17
+TF32X3_MIN_WORK = 1 << 17
 SKINNY_MAX_M = 64    # bf16 batch rows up to which m3_linear_bf16_skinny applies
 SKINNY_ROUTE_M = 16  # bf16 batch rows up to which linear() routes to it (cuBLAS is faster above)
 
@@ -59,8 +68,12 @@ def uses_skinny_bf16(x: torch.Tensor, weight: torch.Tensor) -> bool:
 
 
 def uses_tf32x3(x: torch.Tensor, weight: torch.Tensor) -> bool:
-    return (x.is_cuda and x.dim() == 2 and weight.dim() == 2 and x.dtype == torch.float32
-            and weight.dtype == torch.float32 and x.shape[0] > SMALL_M_MAX and x.shape[1] >= 32
+    if x.dim() != 2 or weight.dim() != 2:
+        return False
+    M, K, N = x.shape[0], x.shape[1], weight.shape[0]
+    big = M > SMALL_M_MAX or (M >= TF32X3_MIN_ROWS and M * N >= TF32X3_MIN_WORK and K >= 1024 and N >= 1024)
+    return (big and x.is_cuda and x.dtype == torch.float32
+            and weight.dtype == torch.float32 and x.shape[1] >= 32
             and x.shape[1] % 4 == 0 and weight.shape[1] == x.shape[1] and x.stride(1) == 1
             and weight.stride(1) == 1 and x.stride(0) % 4 == 0 and weight.stride(0) % 4 == 0
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.device == x.device)

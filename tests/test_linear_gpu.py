@@ -104,9 +104,10 @@ def test_tc_bf16_dispatch():
 
 # ---- fp32 projections of larger batches: split-precision tcgen05 GEMM ----
 
-F32TC_SHAPES = [  # M, N, K: the d1024 layer's in_proj (R 4) / out_proj at batch 4096, tails, odd K
+F32TC_SHAPES = [  # M, N, K: the d1024 layer's in_proj (R 4) / out_proj at batch 4096, tails, odd K, and the
+    # mid-sized batches of that layer the tensor-core path takes below SMALL_M_MAX rows
     (4096, 5248, 1024), (4096, 1024, 2048), (257, 64, 32), (300, 1000, 100), (1000, 4480, 1024), (600, 257, 36),
-    (513, 6272, 1024),
+    (513, 6272, 1024), (33, 4224, 1024), (64, 5248, 1024), (128, 1024, 2048), (200, 6272, 1024),
 ]
 
 
@@ -130,6 +131,23 @@ def test_tf32x3_matches_float64(M, N, K):
     assert err <= 2e-6 * K ** 0.5 * scale, err
     err_cublas = ((x @ w.T).double() - ref).abs().max().item()
     assert err <= 8.0 * err_cublas + 1e-6 * scale, (err, err_cublas)
+
+
+def test_tf32x3_dispatch_for_mid_sized_batches():
+    """Below SMALL_M_MAX rows the tensor-core path is taken only on large
+    layers (K and N >= 1024) with enough work; small layers and the
+    smallest batches keep the small-batch kernel."""
+    from src.kernels.linear import TF32X3_MIN_ROWS, TF32X3_MIN_WORK
+    w_in = torch.randn(5248, 1024, device="cuda") * 0.02
+    w_out = torch.randn(1024, 2048, device="cuda") * 0.02
+    assert uses_tf32x3(torch.randn(32, 1024, device="cuda"), w_in)
+    assert not uses_tf32x3(torch.randn(TF32X3_MIN_ROWS - 1, 1024, device="cuda"), w_in)
+    assert not uses_tf32x3(torch.randn(64, 2048, device="cuda"), w_out)  # 64 x 1024 < TF32X3_MIN_WORK
+    assert 128 * 1024 >= TF32X3_MIN_WORK and uses_tf32x3(torch.randn(128, 2048, device="cuda"), w_out)
+    assert not uses_tf32x3(torch.randn(200, 256, device="cuda"), torch.randn(1600, 256, device="cuda"))
+    x = torch.randn(16, 1024, device="cuda")
+    assert uses_small_m_kernel(x, w_in)
+    torch.testing.assert_close(linear(x, w_in), (x.double() @ w_in.double().T).float(), rtol=2e-5, atol=2e-5 * 32)
 
 
 def test_tf32_split_is_exact():
