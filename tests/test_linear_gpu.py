@@ -27,6 +27,19 @@ def test_matches_float64(M, N, K):
     torch.testing.assert_close(y, ref, rtol=2e-5, atol=2e-5 * K ** 0.5)
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("N,K", [(4177, 1024), (1030, 2048), (9, 520), (5248, 1024)])
+def test_small_batch_weight_stream_matches_float64(M, N, K):
+    """1-8 batch rows at K 512-2048 take the weight-streaming path of
+    m3_linear_f32 (weight-row counts not a multiple of the CTA's, K not a
+    multiple of a warp's slice, and 8 rows x 2048 columns of staged batch)."""
+    g = torch.Generator(device="cuda").manual_seed(17 * M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.05
+    assert uses_small_m_kernel(x, w)
+    torch.testing.assert_close(linear(x, w), (x.double() @ w.double().T).float(), rtol=2e-5, atol=2e-5 * K ** 0.5)
+
+
 def test_strided_rows_and_views():
     x_big = torch.randn(64, 300, device="cuda")
     x = x_big[:, :256]  # row stride 300
