@@ -8,10 +8,12 @@
                          (the kernel updates ssm_state, bx_prev and
                          angle_state in place; small fp32 batches run both
                          projections on the library's small-batch GEMM).
-                         MIMO layers the single-launch kernel takes run the
-                         whole step -- both projections included -- as ONE
-                         launch (``use_single_launch``, default on) while
-                         the projections are small (single_launch_preferred).
+                         In eager steps, layers the single-launch kernel
+                         takes run the whole step -- both projections
+                         included -- as ONE launch (``use_single_launch``,
+                         default on) while the projections are small; a
+                         captured step keeps the three launches, which
+                         replay faster (single_launch_preferred).
   use_triton_fused       in_proj -> PyTorch split/norm/RoPE -> CUDA SSM+silu
                          kernel -> out_proj
   use_triton (default)   in_proj -> PyTorch split/norm/RoPE -> CUDA SSM
@@ -55,8 +57,8 @@ from src.kernels.siso_decode_fused import mamba3_siso_decode_fused_triton
 from src.kernels.step import prepare_decode_step
 
 # The single-launch step computes the projections on latency-oriented FP32
-# FMA tiles; once they are large, cuBLAS's tiles (tensor cores for bf16)
-# win.  It serves batches up to SINGLE_LAUNCH_MAX_BATCH whose projection
+# FMA tiles; once they are large, the separate projection kernels win.  It
+# serves eager steps of batches up to SINGLE_LAUNCH_MAX_BATCH whose projection
 # work, 2 * B * d_model * (d_in_proj + d_inner) flop per step, stays within
 # SINGLE_LAUNCH_MAX_FLOP for the weight dtype.
 SINGLE_LAUNCH_MAX_BATCH = 256
@@ -66,12 +68,15 @@ SINGLE_LAUNCH_MAX_FLOP = {torch.float32: 3e8, torch.bfloat16: 1.5e8}
 def single_launch_preferred(model, batch: int, graph: bool = False) -> bool:
     """Whether the decoder uses the single-launch step for this layer and
     batch (when the kernel takes the layer at all); ``graph``: for a step
-    captured in a CUDA graph.  A SISO layer takes its single launch in eager
-    steps only: there one launch saves the host time of two (19 against 59 us
-    a step for the d256 layer on B200), while replayed from a graph its three
-    launches measured faster (18.9 against 24.6 us), the single launch's
-    state phase waiting on one CTA per (batch row, head) tile."""
-    if not model.is_mimo and graph:
+    captured in a CUDA graph.  Only eager steps take it: there one launch
+    saves the host time of two (19 against 59 us a step for the SISO d256
+    layer on B200).  Replayed from a graph, the three launches measured
+    faster on B200 for every layer tried: MIMO R4 d256 at batch 128 27.4
+    against 32.2 us a step, d1024 fp32 at batch 1 22.7 against 49.3 us,
+    SISO d256 18.9 against 24.6 us (the single launch's projection phases
+    stream the weights on FFMA tiles, and its grid barriers wait for the
+    slowest CTA)."""
+    if graph:
         return False
     flop = 2.0 * batch * model.d_model * (model.d_in_proj + model.d_inner)
     limit = SINGLE_LAUNCH_MAX_FLOP.get(model.in_proj.weight.dtype, 0.0)
@@ -186,7 +191,11 @@ class Mamba3Decoder:
             assert u_host.device.type == "cpu" and u_host.is_pinned(), "u_host must be pinned host memory"
             self._host_output = torch.empty(self._graph_output.shape, dtype=self._graph_output.dtype,
                                             pin_memory=True)
-            launch = self._step_cache[1] if self._step_cache is not None else None
+            # the single launch as an eager step would take it: it stores the
+            # output rows straight into host memory
+            launch = None
+            if self.use_single_launch and self._graph_step_fn() == self._step_triton_full_fused:
+                launch = self._single_launch(self._graph_state, graph=False)
             if launch is not None and launch.accepts(self._graph_input):
                 torch.cuda.synchronize(dev)
                 g = torch.cuda.CUDAGraph()

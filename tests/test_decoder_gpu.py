@@ -212,9 +212,10 @@ def test_bf16_weights_match_pytorch_bf16(mimo):
 
 def test_resume_from_saved_state():
     """Checkpoint/resume: a copy of the state after k steps, fed to a fresh
-    decoder, continues exactly like the uninterrupted run."""
+    decoder, continues exactly like the uninterrupted run (both on the
+    three-launch path, which eager and captured steps then share)."""
     model = _model(d_model=256, d_state=64, headdim=32, is_mimo=True, mimo_rank=4)
-    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_single_launch=False)
     torch.manual_seed(5)
     us = torch.randn(12, 3, 256, device="cuda")
     st = dec.init_state(3, device="cuda")
@@ -224,7 +225,7 @@ def test_resume_from_saved_state():
         saved = {k: v.detach().cpu().clone() for k, v in st.items()}
         for t in range(6, 12):
             o_full, st = dec.step(us[t], st)
-        dec2 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+        dec2 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=False)
         st2 = {k: v.cuda() for k, v in saved.items()}
         # warm-up steps would advance a non-zero state: capture with n_warmup=0
         dec2.warmup_cuda_graph(st2, n_warmup=0)

@@ -25,7 +25,8 @@ def _model():
 def test_resume_from_file_on_the_gpu(tmp_path):
     model = _model()
     us = torch.randn(10, 4, 256, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
-    dec = Mamba3Decoder(model, use_triton_full_fused=True)
+    # eager and captured steps on the same (three-launch) path
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_single_launch=False)
     st = dec.init_state(4, device="cuda")
     p = os.path.join(tmp_path, "gpu.m3state")
     with torch.no_grad():
@@ -35,7 +36,7 @@ def test_resume_from_file_on_the_gpu(tmp_path):
         for t in range(5, 10):
             o_full, st = dec.step(us[t], st)
         st2, _ = load_states(p, device="cuda")
-        dec2 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+        dec2 = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=False)
         dec2.warmup_cuda_graph(st2, n_warmup=0)
         for t in range(5, 10):
             o_res, st2 = dec2.step(us[t], st2)

@@ -91,21 +91,34 @@ def test_single_launch_matches_three_launches(shape, dtype):
 
 
 def test_graph_capture_of_the_single_launch():
+    """The single launch replays correctly from a CUDA graph that a caller
+    captures around it; the decoder's own captured step takes the three
+    launches, which replay faster."""
     _, dims, params, model = _layer(256, 64, 32, 4, seed=21)
     B = 128
-    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
-    st = dec.init_state(B, device="cuda")
-    dec.warmup_cuda_graph(st, n_warmup=2)
-    assert dec._step_cache[1] is not None
+    st = Mamba3Decoder(model, use_triton=False).init_state(B, device="cuda")
+    launch = prepare_decode_step(model, st)
+    u_static = torch.zeros(B, 256, device="cuda")
     st_np = orc.init_state(dims, B)
-    u = orc.synthetic_inputs(dims, B, 2 + 12, seed=22)
-    for t in range(2):  # the warm-up steps ran on a zero input
-        _, st_np = orc.decode_step(np.zeros_like(u[0]), params, dims, st_np)
     with torch.no_grad():
+        launch.run(u_static)  # one eager call before capture
+        _, st_np = orc.decode_step(np.zeros((B, 256), np.float32), params, dims, st_np)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = launch.run(u_static)
+        u = orc.synthetic_inputs(dims, B, 12, seed=22)
         for t in range(12):
-            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            u_static.copy_(torch.from_numpy(u[t]))
+            g.replay()
             oe, st_np = orc.decode_step(u[t], params, dims, st_np)
-            np.testing.assert_allclose(o.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
+            np.testing.assert_allclose(out.cpu().numpy(), oe, rtol=1e-4, atol=1e-4, err_msg=f"step {t}")
+    for k in st_np:
+        np.testing.assert_allclose(st[k].cpu().numpy(), st_np[k], rtol=1e-4, atol=1e-4, err_msg=k)
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    dec.warmup_cuda_graph(dec.init_state(B, device="cuda"), n_warmup=1)
+    assert dec._step_cache[1] is None
+    assert nat.device_error() == 0
 
 
 def test_barrier_words_advance_by_two_grids():

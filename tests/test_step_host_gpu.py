@@ -1,6 +1,8 @@
 """GPU test of ``Mamba3Decoder.step_host``: decode steps from and to pinned
 host memory give the device path's results, on the single-launch kernel
-(output stored straight into host memory) and on the three-launch path."""
+(output stored straight into host memory; compared with eager steps, which
+take the same kernel) and on the three-launch path (compared with captured
+steps)."""
 
 from __future__ import annotations
 
@@ -18,10 +20,14 @@ def test_step_host_matches_device_steps(single):
     torch.manual_seed(0)
     model = Mamba3(d_model=256, d_state=64, headdim=32, is_mimo=True, mimo_rank=4, device="cuda")
     a = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=single)
-    b = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True, use_single_launch=single)
+    b = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=not single, use_single_launch=single)
     sa, sb = a.init_state(16, device="cuda"), b.init_state(16, device="cuda")
     a.warmup_cuda_graph(sa, n_warmup=1)
-    b.warmup_cuda_graph(sb, n_warmup=1)
+    if single:
+        with torch.no_grad():
+            b.step(torch.zeros(16, 256, device="cuda"), sb)  # a's warm-up step
+    else:
+        b.warmup_cuda_graph(sb, n_warmup=1)
     g = torch.Generator().manual_seed(3)
     with torch.no_grad():
         for _ in range(5):
