@@ -1016,6 +1016,9 @@ def run_layer(args, kw, global_batch, dtype_name, world, rank, local):
     # host memory where it serves the layer, else copied back)
     h.barrier()
     with torch.no_grad():
+        for i in range(W):  # the first call sets up (and captures the host-output graph)
+            dec.step_host(u_host[i % n_inputs])
+        torch.cuda.synchronize(dev)
         e2e_ms = h.timed_loop(lambda i: dec.step_host(u_host[i % n_inputs]), K, pre_sync=True)
     h.barrier()
     path = ("pinned input copied in; the single-launch kernel stores the output rows into pinned host memory; "
