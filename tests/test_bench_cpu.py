@@ -83,3 +83,14 @@ def test_reference_arm_times_the_reference_cpu_decode():
     assert r.returncode == 0, r.stderr[-2000:]
     (line,) = _json_lines(r.stdout)
     assert line["n_gpus"] == 2 and line["config"]["global_batch"] == 128
+
+
+def test_sweep_takes_single_layer_workloads_only():
+    """``--sweep`` runs one layer over batch sizes and MIMO ranks; a stack,
+    prefill, projection or state-update workload is refused before any GPU
+    work."""
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--sweep", "--workload",
+                        "stack24_d2048_b256_bf16"], capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "single-layer workload" in r.stderr + r.stdout, r.stderr[-500:]
