@@ -265,6 +265,41 @@ def test_sweep_layer_batch_4096_matches_oracle(R):
         assert rel <= 1e-4, (k, rel)
 
 
+@pytest.mark.parametrize("R", [1, 8])
+@pytest.mark.parametrize("B", [1, 4, 8, 32, 128])
+def test_sweep_layer_small_batches_match_oracle(R, B):
+    """The sweep's small and mid batches through the decoder's captured step
+    (three launches): for 1-8 rows both fp32 projections run on the
+    weight-streaming GEMV (fp32 FMAs, the kernel tolerance 1e-4); from 32
+    rows in_proj runs on the split-precision tensor-core GEMM (the build's
+    1e-3 elementwise and 1e-4 on the state's RMS difference, as at batch
+    4096)."""
+    kw = dict(SWEEP_LAYER, mimo_rank=R)
+    dims = orc.layer_dims(**kw)
+    params = orc.synthetic_params(dims, 420 + R + B, randomize_small=True)
+    model = Mamba3(**kw, device="cuda")
+    load_params(model, params)
+    dec = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    st = dec.init_state(B, device="cuda")
+    dec.warmup_cuda_graph(st, n_warmup=1)  # one step on a zero input
+    u = orc.synthetic_inputs(dims, B, 3, 430 + R + B)
+    st_np = orc.init_state(dims, B)
+    _, st_np = orc.decode_step(np.zeros((B, dims["d_model"]), np.float32), params, dims, st_np)
+    tol = TOL if B <= 8 else TOL3
+    with torch.no_grad():
+        for t in range(3):
+            o, st = dec.step(torch.from_numpy(u[t]).cuda(), st)
+            oe, st_np = orc.decode_step(u[t], params, dims, st_np)
+            np.testing.assert_allclose(o.cpu().numpy(), oe, **tol, err_msg=f"step {t}")
+    for k in st_np:
+        got = st[k].cpu().numpy()
+        np.testing.assert_allclose(got, st_np[k], **tol, err_msg=k)
+        if B > 8:
+            rel = np.sqrt(np.mean((got - st_np[k]) ** 2) / np.mean(st_np[k] ** 2))
+            assert rel <= 1e-4, (k, rel)
+    assert dec._step_cache[1] is None
+
+
 # ---------------------------------------------------------------------------
 # the wide layer: d512, 16 heads, bf16 weights, SISO and MIMO R8
 # ---------------------------------------------------------------------------
