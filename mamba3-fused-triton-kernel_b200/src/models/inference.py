@@ -63,6 +63,12 @@ from src.kernels.step import prepare_decode_step
 # SINGLE_LAUNCH_MAX_FLOP for the weight dtype.
 SINGLE_LAUNCH_MAX_BATCH = 256
 SINGLE_LAUNCH_MAX_FLOP = {torch.float32: 3e8, torch.bfloat16: 1.5e8}
+# step_host stores the single launch's output rows straight into pinned host
+# memory for layers whose projection weights take at most this many bytes;
+# larger layers replay the captured three launches and copy the output back.
+# Measured on B200 (step_host, median us): MIMO R4 d256 (2.2 MB) batch 128
+# 46.9 zero-copy against 48.1; d1024 fp32 (30 MB) batch 1 50.8 against 32.9.
+STEP_HOST_SINGLE_MAX_WEIGHT_BYTES = 4 << 20
 
 
 def single_launch_preferred(model, batch: int, graph: bool = False) -> bool:
@@ -173,8 +179,9 @@ class Mamba3Decoder:
 
         ``u_host`` is a pinned (batch, d_model) tensor of the weight dtype.
         It is copied into the captured graph's input; where the
-        single-launch kernel serves the layer, a second graph of that kernel
-        writes the output rows straight into a pinned host buffer (no
+        single-launch kernel serves the layer and the projection weights are
+        small (STEP_HOST_SINGLE_MAX_WEIGHT_BYTES), a second graph of that
+        kernel writes the output rows straight into a pinned host buffer (no
         device-to-host copy), otherwise the captured step is replayed and its
         output copied back.  Returns the pinned output buffer once the
         device is idle: the same tensor every call, so copy it to keep a
@@ -194,7 +201,10 @@ class Mamba3Decoder:
             # the single launch as an eager step would take it: it stores the
             # output rows straight into host memory
             launch = None
-            if self.use_single_launch and self._graph_step_fn() == self._step_triton_full_fused:
+            m = self.model
+            wbytes = (m.in_proj.weight.numel() + m.out_proj.weight.numel()) * m.in_proj.weight.element_size()
+            if self.use_single_launch and self._graph_step_fn() == self._step_triton_full_fused and \
+                    wbytes <= STEP_HOST_SINGLE_MAX_WEIGHT_BYTES:
                 launch = self._single_launch(self._graph_state, graph=False)
             if launch is not None and launch.accepts(self._graph_input):
                 torch.cuda.synchronize(dev)

@@ -53,3 +53,28 @@ def test_step_host_needs_a_graph_and_pinned_input():
     dec.step_host(torch.zeros(1, 64).pin_memory())
     with pytest.raises(AssertionError):
         dec.step_host(torch.zeros(2, 64).pin_memory())  # wrong shape
+
+
+def test_step_host_of_a_large_layer_replays_the_captured_step():
+    """Projection weights above STEP_HOST_SINGLE_MAX_WEIGHT_BYTES: step_host
+    replays the captured three launches and copies the output back (faster
+    there than the single launch's zero-copy rows), with the device path's
+    results."""
+    from src.models.inference import STEP_HOST_SINGLE_MAX_WEIGHT_BYTES
+    torch.manual_seed(1)
+    model = Mamba3(d_model=1024, d_state=128, headdim=64, is_mimo=True, mimo_rank=4, device="cuda")
+    wbytes = (model.in_proj.weight.numel() + model.out_proj.weight.numel()) * 4
+    assert wbytes > STEP_HOST_SINGLE_MAX_WEIGHT_BYTES
+    a = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    b = Mamba3Decoder(model, use_triton_full_fused=True, use_cuda_graph=True)
+    sa, sb = a.init_state(2, device="cuda"), b.init_state(2, device="cuda")
+    a.warmup_cuda_graph(sa, n_warmup=1)
+    b.warmup_cuda_graph(sb, n_warmup=1)
+    g = torch.Generator().manual_seed(4)
+    with torch.no_grad():
+        for _ in range(3):
+            u = torch.randn(2, 1024, generator=g).pin_memory()
+            oh = a.step_host(u)
+            od, _ = b.step(u.cuda(), sb)
+            torch.testing.assert_close(oh, od.cpu(), rtol=0, atol=0)
+    assert a._host_graph is None
